@@ -1,0 +1,513 @@
+"""Benchmark of the fused GEMM + bias + activation hot path on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+                    [--workload NAME] [--no-extra]
+    python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N
+
+Headline workload: ``ffn_up_silu_8192x4096x14336_bf16`` —
+Y = SiLU(X[8192,4096] @ W[4096,14336] + b), bf16 in/out, fp32 accumulate,
+seeded synthetic inputs.  With N ranks, W and b are column-sharded
+(N-slices of 14336/N), X is replicated, and each rank computes its slice of Y
+with no collective: total work is fixed (strong scaling).
+
+A step is one fused launch per rank.  `value` = 2*M*N*K / step time in
+TFLOP/s (whole job), where the step time is the CUDA-event time of the
+launch on the launching stream, summed over K steps, max over ranks.  L2 is
+flushed (256 MiB write) before every timed launch, outside the events.
+`e2e` is the same metric through the public API (`fused_linear`) with the
+step's inputs copied from pinned host memory and Y copied back inside the
+timed region.  `--impl reference` times the CPU reference arm: the oracle's
+fp32 restatement of the reference expression act(a @ b + bias)
+(kernel.py:64-66) with numpy/BLAS on the host cores, on a bounded row
+sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "fused GEMM+bias+act TFLOP/s & % bf16 peak at 1/2/4/8 B200; decode HBM GB/s"
+DEFAULT_WORKLOAD = "ffn_up_silu_8192x4096x14336_bf16"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+L2_FLUSH_BYTES = 256 << 20
+DATA = "synthetic: seeded X~N(0,1), W~N(0,1/K), bias~U(-0.1,0.1)"
+
+
+def _peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text()), "measured"
+        except ValueError:
+            pass
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def _dist_env() -> tuple[int, int, int]:
+    return (int(os.environ.get("RANK", 0)), int(os.environ.get("WORLD_SIZE", 1)),
+            int(os.environ.get("LOCAL_RANK", 0)))
+
+
+def _traffic(workload: str, world: int):
+    """DRAM bytes per launch from a committed ncu capture, if one exists."""
+    p = ROOT / "profiles" / "dram_traffic.json"
+    if not p.exists():
+        return None
+    try:
+        data = json.loads(p.read_text())
+    except ValueError:
+        return None
+    entry = data.get(f"{workload}@{world}") or (data.get(workload) if world == 1 else None)
+    return entry.get("bytes_per_launch") if isinstance(entry, dict) else None
+
+
+# --------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock, power and clock-event reasons of one GPU via NVML
+    (what nvidia-smi reads) every `period` seconds in a background thread."""
+
+    REASONS = {
+        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "sw_power_cap": 0x4,
+    }
+
+    def __init__(self, uuid: str | None, period: float = 0.02):
+        self.samples: list[tuple[float, int, float, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        self._handle = None
+        self._nvml = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._handle = (pynvml.nvmlDeviceGetHandleByUUID(uuid) if uuid
+                            else pynvml.nvmlDeviceGetHandleByIndex(0))
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._handle, pynvml.NVML_CLOCK_SM)
+        except Exception:  # NVML unavailable: report no clocks
+            self._handle = None
+        self.period = period
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                sm = nv.nvmlDeviceGetClockInfo(self._handle, nv.NVML_CLOCK_SM)
+                pw = nv.nvmlDeviceGetPowerUsage(self._handle) / 1000.0
+                rs = nv.nvmlDeviceGetCurrentClocksEventReasons(self._handle)
+                self.samples.append((time.time(), sm, pw, rs))
+            except Exception:
+                pass
+            self._stop.wait(self.period)
+
+    def start(self):
+        if self._handle is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def stop(self) -> dict | None:
+        if self._thread is None:
+            return None
+        self._stop.set()
+        self._thread.join()
+        if not self.samples:
+            return None
+        loaded = [s for s in self.samples if s[2] > 200.0] or self.samples
+        reasons = sorted({name for s in loaded for name, bit in self.REASONS.items() if s[3] & bit})
+        return {"sm_mhz": statistics.median(s[1] for s in loaded), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(loaded),
+                "power_w_max": round(max(s[2] for s in loaded), 1)}
+
+
+# ------------------------------------------------------------ CPU arm
+def _cpu_threads() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:  # pragma: no cover
+        return os.cpu_count() or 1
+
+
+def cpu_reference_step(X32, W32, b32, act: str) -> float:
+    """One bounded step of the CPU reference arm; returns seconds."""
+    import oracle
+    t0 = time.perf_counter()
+    oracle.fused_linear_f32(X32, W32, b32, act)
+    return time.perf_counter() - t0
+
+
+def cpu_baseline(w, W_host=None, target_s: float = 8.0) -> dict:
+    """The oracle's fp32 restatement timed on the host cores on a bounded
+    sample (rows of X) of the workload; value in TFLOP/s."""
+    import numpy as np
+    import torch
+    from deepx_op_gpukernelcompiler_b200.workloads import make_inputs
+
+    rows0 = min(w.M, 64)
+    inp = make_inputs(w, device="cpu", M=rows0)
+    W32 = (W_host if W_host is not None else inp["W"]).float().numpy()
+    b32 = inp["bias"].float().numpy()
+    X32 = inp["X"].float().numpy()
+    cpu_reference_step(X32, W32, b32, w.act)  # warm BLAS threads
+    t = cpu_reference_step(X32, W32, b32, w.act)
+    rows = int(min(w.M, max(rows0, rows0 * target_s / max(t, 1e-6) / 2)))
+    Xs = np.random.default_rng(0).standard_normal((rows, w.K), dtype=np.float32)
+    Xs = torch.from_numpy(Xs).to(w.torch_dtype).float().numpy()
+    reps, elapsed = 0, 0.0
+    while reps < 2 or elapsed < target_s * 0.5:
+        elapsed += cpu_reference_step(Xs, W32, b32, w.act)
+        reps += 1
+        if elapsed > target_s * 1.5:
+            break
+    flops = 2.0 * rows * w.K * W32.shape[1] * reps
+    return {"value": round(flops / elapsed / 1e12, 4), "unit": "TFLOP/s",
+            "cores": _cpu_threads(), "kind": "port",
+            "sample": f"{reps} x act(X[{rows},{w.K}] @ W[{w.K},{W32.shape[1]}] + b) in fp32 "
+                      f"(numpy/OpenBLAS), {elapsed:.1f} s"}
+
+
+def run_reference(args) -> None:
+    rank, world, _ = _dist_env()
+    if rank != 0:
+        return
+    import numpy as np
+    from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS, make_inputs
+
+    w = WORKLOADS[args.workload]
+    rows = 512 if w.M >= 512 else w.M
+    inp = make_inputs(w, device="cpu", M=rows)
+    X32 = inp["X"].float().numpy()
+    W32 = inp["W"].float().numpy()
+    b32 = inp["bias"].float().numpy()
+    for _ in range(args.warmup):
+        cpu_reference_step(X32, W32, b32, w.act)
+    times = [cpu_reference_step(X32, W32, b32, w.act) for _ in range(args.steps)]
+    total = sum(times)
+    flops_step = 2.0 * rows * w.K * w.N
+    value = flops_step * len(times) / total / 1e12
+    line = {
+        "metric": METRIC, "impl": "reference", "value": round(value, 4), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / len(times) * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": DATA,
+        "config": {"workload": w.name, "M": w.M, "K": w.K, "N": w.N, "act": w.act,
+                   "sample_rows_per_step": rows, "parallelism": "host cores (rank 0)"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": _cpu_threads(),
+                         "kind": "port",
+                         "sample": f"per step act(X[{rows},{w.K}] @ W[{w.K},{w.N}] + b), fp32 "
+                                   "numpy/OpenBLAS restatement of kernel.py:64-66"},
+        "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+        "gpu_launches": 0,
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ GPU arm
+def _time_launches(fn, steps, flush, stream):
+    """CUDA-event time of each launch (flush outside the events), ms list."""
+    import torch
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for s, e in evs:
+        flush()
+        s.record(stream)
+        fn()
+        e.record(stream)
+    torch.cuda.synchronize()
+    return [s.elapsed_time(e) for s, e in evs]
+
+
+def _max_over_ranks(x: float, world: int, device) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([x], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def run_gpu(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from deepx_op_gpukernelcompiler_b200 import _native, fused_linear
+    from deepx_op_gpukernelcompiler_b200.shard import shard_bounds
+    from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS
+
+    rank, world, local = _dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    peaks, peak_kind = _peaks()
+    w = WORKLOADS[args.workload]
+    n0, n1 = shard_bounds(w.N, world, rank, 64)
+    n_loc = n1 - n0
+
+    # Inputs: X replicated, this rank's W/bias column shard; seeded on device.
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(w.seed * 1000 + rank)
+    dt = w.torch_dtype
+    X = torch.randn(w.M, w.K, generator=gen, device=dev).to(dt)
+    Wt = (torch.randn(w.K, n_loc, generator=gen, device=dev) / math.sqrt(w.K)).to(dt)
+    b = (torch.rand(n_loc, generator=gen, device=dev) * 0.2 - 0.1).to(dt)
+    Y = torch.empty(w.M, n_loc, dtype=dt, device=dev)
+    flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        fused_linear(X, Wt, b, w.act, out=Y)
+
+    def flush():
+        flush_buf.zero_()
+
+    uuid = None
+    try:
+        uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        pass
+    sampler = ClockSampler(uuid).start()
+
+    # Warm-up: at least W steps and ~1 s of work so clocks settle.
+    for _ in range(max(1, args.warmup)):
+        step()
+    torch.cuda.synchronize()
+    t_end = time.time() + 1.0
+    while time.time() < t_end:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
+
+    _barrier(world)
+    torch.cuda.synchronize()
+    times = _time_launches(step, args.steps, flush, stream)
+    torch.cuda.synchronize()
+    _barrier(world)
+    clocks = sampler.stop()
+    status = _native.device_status(stream.cuda_stream)
+    if status:
+        raise RuntimeError(f"device status {status}: a kernel wait timed out")
+
+    local_ms = sum(times)
+    total_ms = _max_over_ranks(local_ms, world, dev)
+    ms_step = total_ms / args.steps
+    flops_total = 2.0 * w.M * w.N * w.K
+    value = flops_total / (ms_step * 1e-3) / 1e12
+    flops_rank = 2.0 * w.M * n_loc * w.K
+    achieved = flops_rank / (local_ms / args.steps * 1e-3) / 1e12
+    peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+
+    # End to end through the public API: pinned host inputs in, Y out.
+    Xh = X.cpu().pin_memory()
+    Wh = Wt.cpu().pin_memory()
+    bh = b.cpu().pin_memory()
+    Yh = torch.empty(w.M, n_loc, dtype=dt).pin_memory()
+
+    def e2e_step():
+        Xd = Xh.to(dev, non_blocking=True)
+        Wd = Wh.to(dev, non_blocking=True)
+        bd = bh.to(dev, non_blocking=True)
+        out = fused_linear(Xd, Wd, bd, w.act)
+        Yh.copy_(out, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    e2e_step()
+    torch.cuda.synchronize()
+    _barrier(world)
+    e2e_times = _time_launches(e2e_step, e2e_steps, lambda: None, stream)
+    _barrier(world)
+    e2e_ms = _max_over_ranks(sum(e2e_times), world, dev) / e2e_steps
+    esz = torch.finfo(dt).bits // 8
+    h2d = (w.M * w.K + w.K * n_loc + n_loc) * esz
+    d2h = w.M * n_loc * esz
+
+    extra = {}
+    if not args.no_extra:
+        extra = run_extras(args, world, rank, dev, peaks, flush)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        cpu = cpu_baseline(w, W_host=Wt.cpu())
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_step, 4),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16" if dt == torch.bfloat16 else str(dt).replace("torch.", ""),
+            "data": DATA,
+            "config": {"workload": w.name, "M": w.M, "K": w.K, "N": w.N, "act": w.act,
+                       "parallelism": f"column-parallel N-shard x{world} (no collective)",
+                       "n_per_rank": n_loc, "l2": "flushed before each timed launch (256 MiB write)",
+                       "kernel": "umma"},
+            "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
+                         "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
+                         "peak_source": f"bf16_tflops burst, {peak_kind}",
+                         "traffic": _traffic(w.name, world)},
+            "e2e": {"value": round(flops_total / (e2e_ms * 1e-3) / 1e12, 2), "unit": "TFLOP/s",
+                    "ms_per_step": round(e2e_ms, 3), "h2d_bytes_per_step": h2d * world,
+                    "d2h_bytes_per_step": d2h * world,
+                    "api": "deepx_op_gpukernelcompiler_b200.fused_linear (C ABI dx_fused_linear)"},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "extra": extra,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_extras(args, world, rank, dev, peaks, flush) -> dict:
+    """The other workloads of the metric: decode HBM GB/s, the square GEMM and
+    the MLP chain (all ranks take part; timings are max over ranks)."""
+    import torch
+    from deepx_op_gpukernelcompiler_b200 import fused_linear
+    from deepx_op_gpukernelcompiler_b200.shard import ParallelMLP, shard_bounds
+    from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS
+
+    out = {}
+    stream = torch.cuda.current_stream(dev)
+    steps = max(5, min(args.steps, 20))
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    tflops_peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+
+    # Decode: GELU-erf(X[16,8192] W[8192,28672] + b), fp16, N-sharded.
+    w = WORKLOADS["decode_gelu_erf_16x8192x28672_f16"]
+    n0, n1 = shard_bounds(w.N, world, rank, 64)
+    n_loc = n1 - n0
+    g = torch.Generator(device=dev)
+    g.manual_seed(w.seed * 1000 + rank)
+    X = torch.randn(w.M, w.K, generator=g, device=dev).to(w.torch_dtype)
+    # Enough weight copies that their total exceeds L2 (rotated per step).
+    copies = max(1, math.ceil(3 * (128 << 20) / (w.K * n_loc * 2)))
+    Ws = [(torch.randn(w.K, n_loc, generator=g, device=dev) / math.sqrt(w.K)).to(w.torch_dtype)
+          for _ in range(copies)]
+    b = (torch.rand(n_loc, generator=g, device=dev) * 0.2 - 0.1).to(w.torch_dtype)
+    Y = torch.empty(w.M, n_loc, dtype=w.torch_dtype, device=dev)
+    it = [0]
+
+    def dec():
+        fused_linear(X, Ws[it[0] % copies], b, w.act, out=Y)
+        it[0] += 1
+
+    for _ in range(5):
+        dec()
+    torch.cuda.synchronize()
+    _barrier(world)
+    t = _time_launches(dec, steps, flush, stream)
+    ms = _max_over_ranks(sum(t), world, dev) / steps
+    bytes_rank = 2 * (w.M * w.K + w.K * n_loc + n_loc + w.M * n_loc)
+    bytes_total = w.min_bytes
+    out[w.name] = {"value": round(bytes_total / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
+                   "ms": round(ms, 4), "kernel": "decode",
+                   "roofline": {"bound": "hbm", "achieved": round(bytes_rank / (sum(t) / steps * 1e-3) / 1e9, 1),
+                                "peak": hbm, "unit": "GB/s",
+                                "frac": round(bytes_rank / (sum(t) / steps * 1e-3) / 1e9 / hbm, 4)},
+                   "l2": f"{copies} rotated weight copies + flush"}
+    del Ws, X, Y
+
+    # Square GEMM: GELU-tanh(X[4096,4096] W[4096,4096] + b), bf16 (per rank
+    # an N-slice, no collective).
+    w = WORKLOADS["linear_gelu_tanh_4096x4096x4096_bf16"]
+    n0, n1 = shard_bounds(w.N, world, rank, 64)
+    n_loc = n1 - n0
+    X = torch.randn(w.M, w.K, generator=g, device=dev).to(w.torch_dtype)
+    Wt = (torch.randn(w.K, n_loc, generator=g, device=dev) / math.sqrt(w.K)).to(w.torch_dtype)
+    b = (torch.rand(n_loc, generator=g, device=dev) * 0.2 - 0.1).to(w.torch_dtype)
+    Y = torch.empty(w.M, n_loc, dtype=w.torch_dtype, device=dev)
+
+    def sq():
+        fused_linear(X, Wt, b, w.act, out=Y)
+
+    for _ in range(5):
+        sq()
+    torch.cuda.synchronize()
+    _barrier(world)
+    t = _time_launches(sq, steps, flush, stream)
+    ms = _max_over_ranks(sum(t), world, dev) / steps
+    tf = w.flops / (ms * 1e-3) / 1e12
+    out[w.name] = {"value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+                   "frac_of_peak": round(tf / world / tflops_peak, 4), "kernel": "umma"}
+    del X, Wt, b, Y
+
+    # MLP chain: Y = GELU(X W1 + b1) W2 + b2 + X; column -> row parallel with
+    # one all-reduce of Y (NCCL) when world > 1.
+    w = WORKLOADS["mlp_residual_16384x4096x16384_bf16"]
+    h0, h1 = shard_bounds(w.N, world, rank, 64)
+    h_loc = h1 - h0
+    dt = w.torch_dtype
+    X = torch.randn(w.M, w.K, generator=g, device=dev).to(dt)
+    W1 = (torch.randn(w.K, h_loc, generator=g, device=dev) / math.sqrt(w.K)).to(dt)
+    b1 = (torch.rand(h_loc, generator=g, device=dev) * 0.2 - 0.1).to(dt)
+    W2 = (torch.randn(h_loc, w.K, generator=g, device=dev) / math.sqrt(w.N)).to(dt)
+    b2 = (torch.rand(w.K, generator=g, device=dev) * 0.2 - 0.1).to(dt)
+    H = torch.empty(w.M, h_loc, dtype=dt, device=dev)
+    Yo = torch.empty(w.M, w.K, dtype=dt, device=dev)
+    if world > 1:
+        mlp = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, chunks=4)
+        run = lambda: mlp(X, hidden=H, out=Yo)  # noqa: E731
+    else:
+        from deepx_op_gpukernelcompiler_b200 import mlp_residual
+        run = lambda: mlp_residual(X, W1, b1, W2, b2, w.act, hidden=H, out=Yo)  # noqa: E731
+    for _ in range(3):
+        run()
+    torch.cuda.synchronize()
+    _barrier(world)
+    msteps = max(3, steps // 2)
+    t = _time_launches(run, msteps, flush, stream)
+    ms = _max_over_ranks(sum(t), world, dev) / msteps
+    tf = w.flops / (ms * 1e-3) / 1e12
+    out[w.name] = {"value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+                   "frac_of_peak": round(tf / world / tflops_peak, 4),
+                   "parallelism": f"column->row x{world}" + (" + NCCL all-reduce" if world > 1 else ""),
+                   "gpu_launches_per_step": 2 if world == 1 else 1 + 4}
+    return out
+
+
+def main() -> None:
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
+    ap.add_argument("--no-extra", action="store_true", help="skip the decode/square/MLP lines")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    _, world, _ = _dist_env()
+    if world != args.gpus and args.impl == "b200":
+        print(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE",
+              file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

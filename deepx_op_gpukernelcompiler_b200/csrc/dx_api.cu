@@ -1,0 +1,475 @@
+// dx_api.cu — the C ABI declared in include/deepx_fused.h: argument checks,
+// kernel selection, TMA descriptor encoding and launches.
+//
+// Behavioural contract mirrored from the reference engines
+// (kernel_triton.py:70-89, kernel_tilelang.py:23-55): Y = act(X @ W + b) with
+// an fp32 accumulator and the output in the input dtype.  Differences that
+// the reference gets wrong and this library does not: ragged M/N are masked
+// (kernel_triton.py:49-50 loads unmasked rows), the output keeps its true
+// dtype (kernel_triton.py:65 always rounds to fp16), and GELU is selectable
+// as tanh (the reference oracle, fusion.py:89) or erf (its kernels).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <utility>
+
+#include "deepx_fused.h"
+#include "dx_decode.cuh"
+#include "dx_epilogue.cuh"
+#include "dx_ptx.cuh"
+#include "dx_simt.cuh"
+#include "dx_umma_gemm.cuh"
+
+namespace {
+
+using dx::DecodeParams;
+using dx::DecodeShape;
+using dx::UmmaParams;
+using dx::UmmaShape;
+
+thread_local std::string t_last_error;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_error = buf;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(DX_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorName(e), cudaGetErrorString(e));
+}
+
+// ------------------------------------------------------------ driver entry
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+bool load_encode_fn() {
+  std::call_once(g_encode_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  return g_encode != nullptr;
+}
+
+// --------------------------------------------------------- device facts
+std::mutex g_mu;
+std::map<int, int> g_sm_count;
+std::map<std::pair<int, const void*>, bool> g_attr_done;
+
+int device_sms(int dev, int* sms) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_sm_count.find(dev);
+  if (it != g_sm_count.end()) {
+    *sms = it->second;
+    return DX_OK;
+  }
+  int v = 0;
+  cudaError_t e = cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute(SM count)");
+  g_sm_count[dev] = v;
+  *sms = v;
+  return DX_OK;
+}
+
+int ensure_smem_attr(int dev, const void* fn, int smem_bytes, bool max_carveout) {
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto key = std::make_pair(dev, fn);
+  if (g_attr_done.count(key)) return DX_OK;
+  cudaError_t e =
+      cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(max dynamic smem)");
+  if (max_carveout) {
+    e = cudaFuncSetAttribute(fn, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(carveout)");
+  }
+  g_attr_done[key] = true;
+  return DX_OK;
+}
+
+// ------------------------------------------------------------- TMA maps
+int make_tmap_2d(CUtensorMap* m, const void* ptr, CUtensorMapDataType dt, uint64_t inner,
+                 uint64_t outer, uint64_t ld_elems, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle sw, const char* name) {
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_elems * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = g_encode(m, dt, 2, const_cast<void*>(ptr), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return fail(DX_ERR_CUDA, "cuTensorMapEncodeTiled(%s) failed with CUresult %d", name,
+                static_cast<int>(r));
+  return DX_OK;
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// A 16-bit matrix TMA can address: 16-byte-aligned base, row pitch a
+// multiple of 16 bytes.
+bool tma_ok(const void* p, int64_t ld) { return p != nullptr && aligned16(p) && (ld * 2) % 16 == 0; }
+
+struct Problem {
+  const void *X, *W, *bias, *R;
+  void* Y;
+  int64_t M, N, K, ldx, ldw, ldr, ldy;
+  int dtype, act;
+  void* ws;
+  size_t ws_bytes;
+  cudaStream_t stream;
+};
+
+// ----------------------------------------------------------- decode plan
+constexpr int kDecodeMaxM = 64;
+
+int decode_mn(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
+
+long long decode_cta_of_host(long long u, long long U, int G) {
+  int g = static_cast<int>((u * G) / U);
+  while (g + 1 < G && ((static_cast<long long>(g) + 1) * U) / G <= u) ++g;
+  return g;
+}
+
+struct DecodePlan {
+  int n_tiles = 0, kbt = 0, grid = 0, max_seg = 0, mn = 16;
+  long long units = 0;
+  size_t ticket_bytes = 0, bytes = 0;
+};
+
+DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sms) {
+  DecodePlan d;
+  d.mn = decode_mn(M);
+  d.n_tiles = static_cast<int>((N + 127) / 128);
+  d.kbt = static_cast<int>((K + 63) / 64);
+  d.units = static_cast<long long>(d.n_tiles) * d.kbt;
+  const long long want = 2LL * sms;
+  d.grid = static_cast<int>(std::max<long long>(1, std::min<long long>(d.units, want)));
+  int ms = 1;
+  for (int t = 0; t < d.n_tiles; ++t) {
+    const long long f = decode_cta_of_host(static_cast<long long>(t) * d.kbt, d.units, d.grid);
+    const long long l =
+        decode_cta_of_host(static_cast<long long>(t + 1) * d.kbt - 1, d.units, d.grid);
+    ms = std::max<int>(ms, static_cast<int>(l - f + 1));
+  }
+  d.max_seg = ms;
+  d.ticket_bytes = ((static_cast<size_t>(d.n_tiles) * 4 * sizeof(int)) + 255) & ~size_t(255);
+  d.bytes = d.ticket_bytes +
+            static_cast<size_t>(d.n_tiles) * d.max_seg * d.mn * 128 * sizeof(float);
+  return d;
+}
+
+// -------------------------------------------------------------- launches
+CUtensorMapDataType tma_dtype(int dtype) {
+  return dtype == DX_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+}
+
+int pick_bn(int64_t M, int64_t N, int sms) {
+  if (N <= 128) return 128;
+  const int64_t mt = (M + 127) / 128;
+  const int64_t t256 = mt * ((N + 255) / 256);
+  const int64_t t128 = mt * ((N + 127) / 128);
+  const double c256 = static_cast<double>((t256 + sms - 1) / sms) * 256.0;
+  const double c128 = static_cast<double>((t128 + sms - 1) / sms) * 128.0 * 1.1;
+  return c128 < c256 ? 128 : 256;
+}
+
+template <int BN, typename T>
+int launch_umma(const Problem& pr, int dev, int sms) {
+  using S = UmmaShape<BN>;
+  auto kern = dx::umma_fused_linear_kernel<BN, T>;
+  int rc = ensure_smem_attr(dev, reinterpret_cast<const void*>(kern), S::SMEM_BYTES, false);
+  if (rc) return rc;
+  const CUtensorMapDataType dt = tma_dtype(pr.dtype);
+  CUtensorMap tA, tB, tY, tR;
+  if ((rc = make_tmap_2d(&tA, pr.X, dt, pr.K, pr.M, pr.ldx, 64, 128,
+                         CU_TENSOR_MAP_SWIZZLE_128B, "X")))
+    return rc;
+  if ((rc = make_tmap_2d(&tB, pr.W, dt, pr.N, pr.K, pr.ldw, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B,
+                         "W")))
+    return rc;
+  if ((rc = make_tmap_2d(&tY, pr.Y, dt, pr.N, pr.M, pr.ldy, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B,
+                         "Y")))
+    return rc;
+  if (pr.R != nullptr) {
+    if ((rc = make_tmap_2d(&tR, pr.R, dt, pr.N, pr.M, pr.ldr, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B,
+                           "R")))
+      return rc;
+  } else {
+    tR = tY;  // never read: has_residual == 0
+  }
+  UmmaParams p{};
+  p.M = static_cast<int>(pr.M);
+  p.N = static_cast<int>(pr.N);
+  p.K = static_cast<int>(pr.K);
+  p.m_tiles = static_cast<int>((pr.M + 127) / 128);
+  p.n_tiles = static_cast<int>((pr.N + BN - 1) / BN);
+  p.k_blocks = static_cast<int>((pr.K + 63) / 64);
+  p.num_tiles = p.m_tiles * p.n_tiles;
+  // Keep the X panel of one raster group (group_m x 128 rows x K) within
+  // ~48 MB so it stays L2-resident while all of W streams past it.
+  const int64_t panel = 128 * pr.K * 2;
+  p.group_m = static_cast<int>(
+      std::max<int64_t>(1, std::min<int64_t>(p.m_tiles, (48LL << 20) / std::max<int64_t>(panel, 1))));
+  p.bias = pr.bias;
+  p.act = pr.act;
+  p.has_residual = pr.R != nullptr ? 1 : 0;
+  const int grid = std::min(p.num_tiles, sms);
+  kern<<<grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tA, tB, tY, tR, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch umma_fused_linear_kernel");
+  return DX_OK;
+}
+
+template <int MN, typename T>
+int launch_decode(const Problem& pr, int dev, int sms, const DecodePlan& d) {
+  using S = DecodeShape<MN>;
+  auto kern = dx::decode_fused_linear_kernel<MN, T>;
+  int rc = ensure_smem_attr(dev, reinterpret_cast<const void*>(kern), S::SMEM_BYTES, true);
+  if (rc) return rc;
+  const CUtensorMapDataType dt = tma_dtype(pr.dtype);
+  CUtensorMap tW, tX;
+  if ((rc = make_tmap_2d(&tW, pr.W, dt, pr.N, pr.K, pr.ldw, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B,
+                         "W")))
+    return rc;
+  if ((rc = make_tmap_2d(&tX, pr.X, dt, pr.K, pr.M, pr.ldx, 64, MN, CU_TENSOR_MAP_SWIZZLE_128B,
+                         "X")))
+    return rc;
+  DecodeParams p{};
+  p.M = static_cast<int>(pr.M);
+  p.N = static_cast<int>(pr.N);
+  p.K = static_cast<int>(pr.K);
+  p.n_tiles = d.n_tiles;
+  p.kbt = d.kbt;
+  p.units = d.units;
+  p.grid = d.grid;
+  p.max_seg = d.max_seg;
+  p.ldy = pr.ldy;
+  p.ldr = pr.ldr;
+  p.bias = pr.bias;
+  p.residual = pr.R;
+  p.Y = pr.Y;
+  p.tickets = static_cast<int*>(pr.ws);
+  p.partials = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + d.ticket_bytes);
+  p.act = pr.act;
+  (void)sms;
+  kern<<<d.grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tW, tX, p);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch decode_fused_linear_kernel");
+  return DX_OK;
+}
+
+template <typename T>
+int launch_simt(const Problem& pr, int sms) {
+  const T* X = static_cast<const T*>(pr.X);
+  const T* W = static_cast<const T*>(pr.W);
+  const T* b = static_cast<const T*>(pr.bias);
+  const T* R = static_cast<const T*>(pr.R);
+  T* Y = static_cast<T*>(pr.Y);
+  const int M = static_cast<int>(pr.M), N = static_cast<int>(pr.N), K = static_cast<int>(pr.K);
+  const int64_t big_tiles = ((pr.M + 63) / 64) * ((pr.N + 63) / 64);
+  if (big_tiles >= 2LL * sms) {
+    if ((pr.M + 63) / 64 > 65535) return fail(DX_ERR_UNSUPPORTED, "M too large for the SIMT kernel");
+    dim3 grid(static_cast<unsigned>((pr.N + 63) / 64), static_cast<unsigned>((pr.M + 63) / 64));
+    dx::simt_fused_linear_kernel<T, 64, 64><<<grid, 256, 0, pr.stream>>>(
+        X, W, b, R, Y, M, N, K, pr.ldx, pr.ldw, pr.ldr, pr.ldy, pr.act);
+  } else {
+    if ((pr.M + 31) / 32 > 65535) return fail(DX_ERR_UNSUPPORTED, "M too large for the SIMT kernel");
+    dim3 grid(static_cast<unsigned>((pr.N + 31) / 32), static_cast<unsigned>((pr.M + 31) / 32));
+    dx::simt_fused_linear_kernel<T, 32, 32><<<grid, 256, 0, pr.stream>>>(
+        X, W, b, R, Y, M, N, K, pr.ldx, pr.ldw, pr.ldr, pr.ldy, pr.act);
+  }
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch simt_fused_linear_kernel");
+  return DX_OK;
+}
+
+// ---------------------------------------------------------- validation
+int validate(const Problem& p, int kernel) {
+  if (p.dtype < DX_DTYPE_F32 || p.dtype > DX_DTYPE_BF16)
+    return fail(DX_ERR_INVALID_ARGUMENT, "unknown dtype %d", p.dtype);
+  if (p.act < DX_ACT_NONE || p.act > DX_ACT_SILU)
+    return fail(DX_ERR_INVALID_ARGUMENT, "unknown activation %d", p.act);
+  if (kernel < DX_KERNEL_AUTO || kernel > DX_KERNEL_SIMT)
+    return fail(DX_ERR_INVALID_ARGUMENT, "unknown kernel variant %d", kernel);
+  if (p.M < 0 || p.N < 0 || p.K < 0)
+    return fail(DX_ERR_INVALID_ARGUMENT, "negative shape M=%lld N=%lld K=%lld", (long long)p.M,
+                (long long)p.N, (long long)p.K);
+  const int64_t kMax = 0x7fffffffLL;
+  if (p.M > kMax || p.N > kMax || p.K > kMax)
+    return fail(DX_ERR_UNSUPPORTED, "dimension above 2^31-1");
+  if (p.M == 0 || p.N == 0) return DX_OK;
+  if (p.Y == nullptr) return fail(DX_ERR_INVALID_ARGUMENT, "Y is NULL");
+  if (p.K > 0 && (p.X == nullptr || p.W == nullptr))
+    return fail(DX_ERR_INVALID_ARGUMENT, "X or W is NULL");
+  if (p.ldx < std::max<int64_t>(p.K, 1))
+    return fail(DX_ERR_INVALID_ARGUMENT, "ldx=%lld < K=%lld", (long long)p.ldx, (long long)p.K);
+  if (p.ldw < p.N)
+    return fail(DX_ERR_INVALID_ARGUMENT, "ldw=%lld < N=%lld", (long long)p.ldw, (long long)p.N);
+  if (p.ldy < p.N)
+    return fail(DX_ERR_INVALID_ARGUMENT, "ldy=%lld < N=%lld", (long long)p.ldy, (long long)p.N);
+  if (p.R != nullptr && p.ldr < p.N)
+    return fail(DX_ERR_INVALID_ARGUMENT, "ldr=%lld < N=%lld", (long long)p.ldr, (long long)p.N);
+  return DX_OK;
+}
+
+bool umma_eligible(const Problem& p) {
+  if (p.dtype == DX_DTYPE_F32 || p.K == 0) return false;
+  if (!tma_ok(p.X, p.ldx) || !tma_ok(p.W, p.ldw) || !tma_ok(p.Y, p.ldy)) return false;
+  if (p.R != nullptr && !tma_ok(p.R, p.ldr)) return false;
+  return true;
+}
+
+bool decode_eligible(const Problem& p) {
+  if (p.dtype == DX_DTYPE_F32 || p.K == 0 || p.M > kDecodeMaxM) return false;
+  return tma_ok(p.X, p.ldx) && tma_ok(p.W, p.ldw);
+}
+
+int select_variant(const Problem& p, int sms, bool ws_known) {
+  if (p.dtype == DX_DTYPE_F32 || p.K == 0) return DX_KERNEL_SIMT;
+  if (decode_eligible(p)) {
+    if (!ws_known) return DX_KERNEL_DECODE;
+    const DecodePlan d = decode_plan(p.M, p.N, p.K, sms);
+    if (p.ws != nullptr && p.ws_bytes >= d.bytes && aligned16(p.ws)) return DX_KERNEL_DECODE;
+  }
+  if (umma_eligible(p)) return DX_KERNEL_UMMA;
+  return DX_KERNEL_SIMT;
+}
+
+template <typename T>
+int dispatch_typed(const Problem& p, int variant, int dev, int sms) {
+  switch (variant) {
+    case DX_KERNEL_UMMA: {
+      const int bn = pick_bn(p.M, p.N, sms);
+      return bn == 256 ? launch_umma<256, T>(p, dev, sms) : launch_umma<128, T>(p, dev, sms);
+    }
+    case DX_KERNEL_DECODE: {
+      const DecodePlan d = decode_plan(p.M, p.N, p.K, sms);
+      if (d.mn == 16) return launch_decode<16, T>(p, dev, sms, d);
+      if (d.mn == 32) return launch_decode<32, T>(p, dev, sms, d);
+      return launch_decode<64, T>(p, dev, sms, d);
+    }
+    default:
+      return launch_simt<T>(p, sms);
+  }
+}
+
+int run(const Problem& p, int kernel) {
+  t_last_error.clear();
+  int rc = validate(p, kernel);
+  if (rc) return rc;
+  if (p.M == 0 || p.N == 0) return DX_OK;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int sms = 0;
+  if ((rc = device_sms(dev, &sms))) return rc;
+
+  int variant = kernel == DX_KERNEL_AUTO ? select_variant(p, sms, true) : kernel;
+  if (variant == DX_KERNEL_UMMA || variant == DX_KERNEL_DECODE) {
+    if (!load_encode_fn())
+      return fail(DX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  }
+  if (variant == DX_KERNEL_UMMA && !umma_eligible(p))
+    return fail(DX_ERR_UNSUPPORTED,
+                "tcgen05 kernel needs fp16/bf16, K > 0, 16-byte-aligned pointers and row "
+                "pitches that are multiples of 16 bytes");
+  if (variant == DX_KERNEL_DECODE) {
+    if (!decode_eligible(p))
+      return fail(DX_ERR_UNSUPPORTED,
+                  "decode kernel needs fp16/bf16, 0 < K, M <= %d, and 16-byte-aligned X/W "
+                  "with row pitches that are multiples of 16 bytes",
+                  kDecodeMaxM);
+    const DecodePlan d = decode_plan(p.M, p.N, p.K, sms);
+    if (p.ws == nullptr || p.ws_bytes < d.bytes || !aligned16(p.ws))
+      return fail(DX_ERR_WORKSPACE, "decode kernel needs a 16-byte-aligned workspace of %zu bytes",
+                  d.bytes);
+  }
+  switch (p.dtype) {
+    case DX_DTYPE_F32:
+      if (variant != DX_KERNEL_SIMT)
+        return fail(DX_ERR_UNSUPPORTED, "fp32 runs only on the exact-fp32 SIMT kernel");
+      return launch_simt<float>(p, sms);
+    case DX_DTYPE_F16:
+      return dispatch_typed<__half>(p, variant, dev, sms);
+    default:
+      return dispatch_typed<__nv_bfloat16>(p, variant, dev, sms);
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+int dx_fused_linear_ex(const void* X, const void* W, const void* bias, const void* R, void* Y,
+                       int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw, int64_t ldr,
+                       int64_t ldy, int dtype, int act, int kernel, void* workspace,
+                       size_t workspace_bytes, void* stream) {
+  Problem p{X, W, bias, R, Y, M, N, K, ldx, ldw, ldr, ldy, dtype, act, workspace, workspace_bytes,
+            static_cast<cudaStream_t>(stream)};
+  return run(p, kernel);
+}
+
+int dx_fused_linear(const void* X, const void* W, const void* bias, const void* R, void* Y,
+                    int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw, int64_t ldr,
+                    int64_t ldy, int dtype, int act, void* workspace, size_t workspace_bytes,
+                    void* stream) {
+  return dx_fused_linear_ex(X, W, bias, R, Y, M, N, K, ldx, ldw, ldr, ldy, dtype, act,
+                            DX_KERNEL_AUTO, workspace, workspace_bytes, stream);
+}
+
+size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K, int dtype, int kernel) {
+  t_last_error.clear();
+  if (M <= 0 || N <= 0 || K <= 0 || dtype == DX_DTYPE_F32) return 0;
+  if (kernel == DX_KERNEL_UMMA || kernel == DX_KERNEL_SIMT) return 0;
+  if (M > kDecodeMaxM) return 0;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || device_sms(dev, &sms) != DX_OK) return 0;
+  return decode_plan(M, N, K, sms).bytes;
+}
+
+int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype) {
+  if (dtype == DX_DTYPE_F32 || K <= 0) return DX_KERNEL_SIMT;
+  if ((K * 2) % 16 != 0 || (N * 2) % 16 != 0) return DX_KERNEL_SIMT;
+  if (M <= kDecodeMaxM) return DX_KERNEL_DECODE;
+  return DX_KERNEL_UMMA;
+}
+
+const char* dx_last_error_string(void) { return t_last_error.c_str(); }
+
+int dx_device_status(void* stream, int* status) {
+  t_last_error.clear();
+  if (status == nullptr) return fail(DX_ERR_INVALID_ARGUMENT, "status is NULL");
+  cudaError_t e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  int v = 0;
+  e = cudaMemcpyFromSymbol(&v, dx::g_device_status, sizeof(int));
+  if (e != cudaSuccess) return cuda_fail(e, "read device status");
+  if (v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(dx::g_device_status, &zero, sizeof(int));
+    if (e != cudaSuccess) return cuda_fail(e, "clear device status");
+  }
+  *status = v;
+  return DX_OK;
+}
+
+int dx_version(void) { return 100; }
+
+}  // extern "C"

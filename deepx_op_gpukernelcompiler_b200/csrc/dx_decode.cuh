@@ -1,0 +1,297 @@
+// dx_decode.cuh — skinny-M (decode) fused linear, HBM-bound:
+//   Y[M,N] = act(X[M,K] @ W[K,N] + bias[N]) (+ R),  M <= 64, fp16/bf16.
+//
+// With M <= 64 every element of W is used at most 64 times, so the kernel's
+// job is to stream W from HBM exactly once at full bandwidth.  Design:
+//   * swap-AB on the tensor core: D^T[n, m] = sum_k W^T[n, k] X^T[k, m], so
+//     the 128-wide UMMA M dimension runs over N (W's contiguous axis, read
+//     by TMA straight from its row-major layout as an MN-major operand) and
+//     the UMMA N dimension is the padded batch MN = 16/32/64 (X as a K-major
+//     operand).  D lives in TMEM: 128 lanes x MN fp32 columns.
+//   * split-K with an even partition of the (n-tile, k-block) work units
+//     over all CTAs (2 per SM), so every SM streams the same number of bytes
+//     regardless of N/K; a CTA's range crosses at most a few n-tiles.
+//   * partial sums of a tile that several CTAs share go to a workspace as
+//     fp32; the last CTA to finish a tile (atomic ticket) sums the partials
+//     in fixed segment order — deterministic, no float atomics — applies
+//     bias, activation and residual, stores Y, and resets the ticket to 0.
+// Bounded waits and exit draining as in dx_umma_gemm.cuh.
+#pragma once
+
+#include "dx_epilogue.cuh"
+#include "dx_ptx.cuh"
+
+namespace dx {
+
+struct DecodeParams {
+  int M, N, K;
+  int n_tiles;          // ceil(N / 128)
+  int kbt;              // k-blocks (64 deep) per tile
+  long long units;      // n_tiles * kbt
+  int grid;             // CTAs
+  int max_seg;          // partial-sum slots per tile
+  long long ldy, ldr;
+  const void* bias;     // N elements or nullptr
+  const void* residual; // [M, N] (ldr) or nullptr
+  void* Y;
+  float* partials;      // [n_tiles][max_seg][MN][128] fp32
+  int* tickets;         // [n_tiles][4] (per warp quarter), zero between calls
+  int act;
+};
+
+template <int MN>
+struct DecodeShape {
+  static constexpr int BK = 64;
+  static constexpr int W_BOX_BYTES = 64 * BK * 2;  // [64 k x 64 n]
+  static constexpr int W_BYTES = 2 * W_BOX_BYTES;  // 128 n per stage
+  static constexpr int X_BYTES = MN * BK * 2;      // MN rows x 128 B
+  static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
+  static constexpr int STAGES = MN <= 16 ? 6 : (MN <= 32 ? 5 : 4);
+  static constexpr int TMEM_COLS = (2 * MN < 32) ? 32 : 2 * MN;
+  static constexpr int THREADS = 192;
+  static constexpr int OFF_W = 0;
+  static constexpr int OFF_X = OFF_W + STAGES * W_BYTES;
+  static constexpr int OFF_BAR = OFF_X + STAGES * X_BYTES;
+  static constexpr int BAR_FULL = 0;
+  static constexpr int BAR_EMPTY = STAGES;
+  static constexpr int BAR_TFULL = 2 * STAGES;
+  static constexpr int BAR_TEMPTY = 2 * STAGES + 2;
+  static constexpr int BAR_DRAIN = 2 * STAGES + 4;
+  static constexpr int NUM_BARS = BAR_DRAIN + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // tmem base, abort flag
+  static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 16;
+  static_assert(MN == 16 || MN == 32 || MN == 64, "decode batch tile");
+  static_assert(X_BYTES % 1024 == 0, "X stage alignment");
+};
+
+// CTA whose work range holds unit u (ranges are [g*U/G, (g+1)*U/G)).
+__device__ __forceinline__ int decode_cta_of(long long u, long long U, int G) {
+  int g = static_cast<int>((u * G) / U);
+  while (g + 1 < G && ((static_cast<long long>(g) + 1) * U) / G <= u) ++g;
+  return g;
+}
+
+template <int MN, typename T>
+__global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 2)
+    decode_fused_linear_kernel(const __grid_constant__ CUtensorMap tmW,
+                               const __grid_constant__ CUtensorMap tmX, const DecodeParams p) {
+  using S = DecodeShape<MN>;
+  using Tr = ElemTraits<T>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* const base_ptr = smem_raw + (base - raw_u32);
+
+  const uint32_t sW = base + S::OFF_W;
+  const uint32_t sX = base + S::OFF_X;
+  const uint32_t bars = base + S::OFF_BAR;
+  uint32_t* const tmem_word = reinterpret_cast<uint32_t*>(base_ptr + S::OFF_MISC);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(base_ptr + S::OFF_MISC + 4);
+  auto bar = [bars](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int g = blockIdx.x;
+  const long long U = p.units;
+  const long long u_begin = (static_cast<long long>(g) * U) / p.grid;
+  const long long u_end = (static_cast<long long>(g + 1) * U) / p.grid;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::STAGES; ++s) {
+      mbar_init(bar(S::BAR_FULL + s), 1);
+      mbar_init(bar(S::BAR_EMPTY + s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(S::BAR_TFULL + b), 1);
+      mbar_init(bar(S::BAR_TEMPTY + b), 4);
+    }
+    mbar_init(bar(S::BAR_DRAIN), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmW);
+    tma_prefetch_desc(&tmX);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_word), S::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_word;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      int s = 0;
+      uint32_t ph = 0, issued = 0;
+      bool ok = true;
+      for (long long u = u_begin; ok && u < u_end;) {
+        const int t = static_cast<int>(u / p.kbt);
+        const int kb0 = static_cast<int>(u - static_cast<long long>(t) * p.kbt);
+        const int kb1 = static_cast<int>(p.kbt < kb0 + (u_end - u) ? (long long)p.kbt : kb0 + (u_end - u));
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(bar(S::BAR_EMPTY + s), ph ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = bar(S::BAR_FULL + s);
+          mbar_arrive_expect_tx(fb, S::STAGE_BYTES);
+          tma_load_2d(&tmW, sW + s * S::W_BYTES, fb, t * 128, kb * S::BK);
+          tma_load_2d(&tmW, sW + s * S::W_BYTES + S::W_BOX_BYTES, fb, t * 128 + 64, kb * S::BK);
+          tma_load_2d(&tmX, sX + s * S::X_BYTES, fb, kb * S::BK, 0);
+          ++issued;
+          if (++s == S::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        u += kb1 - kb0;
+      }
+      const uint32_t n_drain = issued < (uint32_t)S::STAGES ? issued : (uint32_t)S::STAGES;
+      for (uint32_t i = issued - n_drain; i < issued; ++i)
+        mbar_wait_drain(bar(S::BAR_FULL + (int)(i % S::STAGES)), (i / S::STAGES) & 1u);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(Tr::kIsBf16, 128, MN, true, false);
+      int s = 0, local = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (long long u = u_begin; ok && u < u_end; ++local) {
+        const int t = static_cast<int>(u / p.kbt);
+        const int kb0 = static_cast<int>(u - static_cast<long long>(t) * p.kbt);
+        const int kb1 = static_cast<int>(p.kbt < kb0 + (u_end - u) ? (long long)p.kbt : kb0 + (u_end - u));
+        u += kb1 - kb0;
+        const int b = local & 1;
+        const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
+        if (!mbar_wait(bar(S::BAR_TEMPTY + b), use_ph ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * MN);
+        for (int kb = kb0; kb < kb1; ++kb) {
+          if (!mbar_wait(bar(S::BAR_FULL + s), ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          // W^T tile: MN-major (n contiguous), two 64-wide n groups one box
+          // apart, 8-row k groups 1024 B apart; +2048 B per K=16 step.
+          const uint64_t ad = smem_desc_sw128(sW + s * S::W_BYTES, S::W_BOX_BYTES, 1024);
+          // X tile: K-major rows of 128 B, 8-row groups 1024 B apart.
+          const uint64_t bd = smem_desc_sw128(sX + s * S::X_BYTES, 16, 1024);
+#pragma unroll
+          for (int k = 0; k < S::BK / 16; ++k)
+            umma_f16(d_tmem, ad + 128ull * k, bd + 2ull * k, idesc,
+                     (kb != kb0 || k != 0) ? 1u : 0u);
+          umma_commit(bar(S::BAR_EMPTY + s));
+          if (++s == S::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (ok) umma_commit(bar(S::BAR_TFULL + b));
+      }
+      umma_commit(bar(S::BAR_DRAIN));
+      mbar_wait_drain(bar(S::BAR_DRAIN), 0);
+    }
+    __syncwarp();
+  } else {
+    // --------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    const int n_local = q * 32 + lane;
+    const T* const bias = static_cast<const T*>(p.bias);
+    const T* const res = static_cast<const T*>(p.residual);
+    T* const Y = static_cast<T*>(p.Y);
+    const int M = p.M;
+    int local = 0;
+    for (long long u = u_begin; u < u_end; ++local) {
+      const int t = static_cast<int>(u / p.kbt);
+      const int kb0 = static_cast<int>(u - static_cast<long long>(t) * p.kbt);
+      const int kb1 = static_cast<int>(p.kbt < kb0 + (u_end - u) ? (long long)p.kbt : kb0 + (u_end - u));
+      u += kb1 - kb0;
+      const int b = local & 1;
+      const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
+      if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
+      tc_fence_after();
+      float acc[MN];
+      const uint32_t taddr =
+          tmem_base + static_cast<uint32_t>(b * MN) + (static_cast<uint32_t>(q * 32) << 16);
+      if constexpr (MN == 16) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(taddr, r);
+        tmem_wait_ld();
+#pragma unroll
+        for (int j = 0; j < 16; ++j) acc[j] = __uint_as_float(r[j]);
+      } else {
+#pragma unroll
+        for (int h = 0; h < MN / 32; ++h) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(taddr + 32u * h, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[32 * h + j] = __uint_as_float(r[j]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(S::BAR_TEMPTY + b));
+
+      if (!(kb0 == 0 && kb1 == p.kbt)) {
+        // Tile shared with other CTAs: publish this segment's partial sums.
+        const int first = decode_cta_of(static_cast<long long>(t) * p.kbt, U, p.grid);
+        const int last = decode_cta_of(static_cast<long long>(t + 1) * p.kbt - 1, U, p.grid);
+        const int nseg = last - first + 1;
+        float* const part_t = p.partials + static_cast<size_t>(t) * p.max_seg * MN * 128;
+        float* const mine = part_t + static_cast<size_t>(g - first) * MN * 128;
+#pragma unroll
+        for (int m = 0; m < MN; ++m)
+          if (m < M) mine[m * 128 + n_local] = acc[m];
+        __threadfence();
+        __syncwarp();
+        // One ticket per (tile, warp quarter): each warp finishes its own 32
+        // columns, so no cross-warp barrier can be left waiting on an exit.
+        int ticket = 0;
+        if (lane == 0) ticket = atomicAdd(p.tickets + t * 4 + q, 1);
+        ticket = __shfl_sync(0xffffffffu, ticket, 0);
+        if (ticket != nseg - 1) continue;
+        __threadfence();
+        // Fixed summation order over segments: bitwise identical results
+        // whichever CTA finishes last.
+#pragma unroll
+        for (int m = 0; m < MN; ++m) acc[m] = 0.0f;
+        for (int sg = 0; sg < nseg; ++sg) {
+          const float* src = part_t + static_cast<size_t>(sg) * MN * 128;
+#pragma unroll
+          for (int m = 0; m < MN; ++m)
+            if (m < M) acc[m] += __ldcg(src + m * 128 + n_local);
+        }
+        if (lane == 0) p.tickets[t * 4 + q] = 0;
+      }
+      const int n = t * 128 + n_local;
+      if (n < p.N) {
+        const float bv = bias != nullptr ? Tr::to_float(bias[n]) : 0.0f;
+#pragma unroll
+        for (int m = 0; m < MN; ++m) {
+          if (m < M) {
+            float y = act_apply(acc[m] + bv, p.act);
+            if (res != nullptr) y += Tr::to_float(res[m * p.ldr + n]);
+            Y[m * p.ldy + n] = Tr::from_float(y);
+          }
+        }
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+}
+
+}  // namespace dx

@@ -1,0 +1,83 @@
+// dx_epilogue.cuh — element types and the fused epilogue math shared by all
+// kernels: y = act(acc + bias) (+ residual), computed in fp32.
+//
+// Activation definitions follow the reference:
+//   relu            torch.relu                     (fusion.py:88)
+//   gelu (tanh)     F.gelu(approximate='tanh')     (fusion.py:89)
+//   gelu (erf)      0.5*x*(erf(x/sqrt(2)) + 1)     (kernel_triton.py:61,
+//                                                   kernel_tilelang.py:17)
+//   silu / swish    x * sigmoid(x)                 (fusion.py:90-91,
+//                                                   kernel_triton.py:63)
+// The transcendental parts call CUDA's own tanhf / erff / expf.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace dx {
+
+enum Act : int { kActNone = 0, kActRelu = 1, kActGeluTanh = 2, kActGeluErf = 3, kActSilu = 4 };
+
+__device__ __forceinline__ float act_apply(float x, int act) {
+  switch (act) {
+    case kActRelu:
+      return fmaxf(x, 0.0f);
+    case kActGeluTanh: {
+      // sqrt(2/pi) * (x + 0.044715 x^3)
+      const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
+      return 0.5f * x * (1.0f + tanhf(u));
+    }
+    case kActGeluErf:
+      return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));
+    case kActSilu:
+      return x / (1.0f + expf(-x));
+    default:
+      return x;
+  }
+}
+
+template <typename T>
+struct ElemTraits;
+
+template <>
+struct ElemTraits<float> {
+  static constexpr bool kIsBf16 = false;
+  __device__ __forceinline__ static float to_float(float v) { return v; }
+  __device__ __forceinline__ static float from_float(float v) { return v; }
+};
+
+template <>
+struct ElemTraits<__half> {
+  static constexpr bool kIsBf16 = false;
+  __device__ __forceinline__ static float to_float(__half v) { return __half2float(v); }
+  __device__ __forceinline__ static __half from_float(float v) { return __float2half_rn(v); }
+  // Two fp32 values -> packed pair (low half = first).
+  __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static float2 unpack2(uint32_t u) {
+    __half2 h = *reinterpret_cast<__half2*>(&u);
+    return __half22float2(h);
+  }
+};
+
+template <>
+struct ElemTraits<__nv_bfloat16> {
+  static constexpr bool kIsBf16 = true;
+  __device__ __forceinline__ static float to_float(__nv_bfloat16 v) { return __bfloat162float(v); }
+  __device__ __forceinline__ static __nv_bfloat16 from_float(float v) {
+    return __float2bfloat16_rn(v);
+  }
+  __device__ __forceinline__ static uint32_t pack2(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t*>(&h);
+  }
+  __device__ __forceinline__ static float2 unpack2(uint32_t u) {
+    __nv_bfloat162 h = *reinterpret_cast<__nv_bfloat162*>(&u);
+    return __bfloat1622float2(h);
+  }
+};
+
+}  // namespace dx

@@ -1,0 +1,84 @@
+// dx_simt.cuh — CUDA-core fused linear with fp32 FFMA accumulation.
+//
+// Serves two cases the tensor-core kernels do not:
+//   * fp32 inputs: the exact-fp32 path (no TF32 rounding of the operands),
+//     needed for the fp32 tolerance of 1e-4;
+//   * fp16/bf16 problems whose strides or pointers TMA cannot address
+//     (rows not a multiple of 16 bytes), and K == 0.
+// Each thread accumulates its outputs over k = 0..K-1 in order, so results
+// are deterministic.  Tiles are BM x BN with 256 threads in a 16 x 16 grid;
+// thread (ty, tx) owns rows ty + 16 i and columns tx + 16 j.
+#pragma once
+
+#include "dx_epilogue.cuh"
+
+namespace dx {
+
+template <typename T, int BM, int BN>
+__global__ void __launch_bounds__(256)
+    simt_fused_linear_kernel(const T* __restrict__ X, const T* __restrict__ W,
+                             const T* __restrict__ bias, const T* __restrict__ R,
+                             T* __restrict__ Y, int M, int N, int K, long long ldx, long long ldw,
+                             long long ldr, long long ldy, int act) {
+  using Tr = ElemTraits<T>;
+  constexpr int BK = 16;
+  constexpr int TM = BM / 16;
+  constexpr int TN = BN / 16;
+  __shared__ float As[BK][BM + 1];
+  __shared__ float Bs[BK][BN];
+  const int tx = threadIdx.x & 15;
+  const int ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * BM;
+  const int n0 = blockIdx.x * BN;
+
+  float acc[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
+
+  for (int k0 = 0; k0 < K; k0 += BK) {
+    for (int idx = threadIdx.x; idx < BM * BK; idx += 256) {
+      const int mm = idx / BK, kk = idx % BK;
+      const int m = m0 + mm, k = k0 + kk;
+      As[kk][mm] = (m < M && k < K) ? Tr::to_float(X[m * ldx + k]) : 0.0f;
+    }
+    for (int idx = threadIdx.x; idx < BK * BN; idx += 256) {
+      const int kk = idx / BN, nn = idx % BN;
+      const int k = k0 + kk, n = n0 + nn;
+      Bs[kk][nn] = (k < K && n < N) ? Tr::to_float(W[k * ldw + n]) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float a[TM], b[TN];
+#pragma unroll
+      for (int i = 0; i < TM; ++i) a[i] = As[kk][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < TN; ++j) b[j] = Bs[kk][tx + 16 * j];
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int i = 0; i < TM; ++i) {
+    const int m = m0 + ty + 16 * i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      const int n = n0 + tx + 16 * j;
+      if (n >= N) continue;
+      float v = acc[i][j];
+      if (bias != nullptr) v += Tr::to_float(bias[n]);
+      v = act_apply(v, act);
+      if (R != nullptr) v += Tr::to_float(R[m * ldr + n]);
+      Y[m * ldy + n] = Tr::from_float(v);
+    }
+  }
+}
+
+}  // namespace dx

@@ -1,0 +1,151 @@
+"""PyTorch-facing wrapper of the fused linear C ABI.
+
+``fused_linear(X, W, bias, activation, residual)`` computes
+``act(X @ W + bias) + residual`` on the tensors' CUDA device, on the current
+stream, through ``dx_fused_linear`` (include/deepx_fused.h).  PyTorch only
+provides device memory and the stream; the arithmetic runs in the sm_100a
+kernels of ``csrc/``.  Inputs must be CUDA tensors — there is no CPU path.
+
+Activation names follow the reference: ``relu``, ``gelu`` (tanh
+approximation, as ``ACTIVATION_PT['gelu']`` in fusion.py:89), ``silu`` and
+``swish`` (= silu, fusion.py:91), plus the explicit ``gelu_tanh`` /
+``gelu_erf`` (the erf form is what kernel_triton.py:61 and
+kernel_tilelang.py:17 compute).
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _native as nat
+
+ACTIVATION_CODES = {
+    None: nat.DX_ACT_NONE,
+    "none": nat.DX_ACT_NONE,
+    "relu": nat.DX_ACT_RELU,
+    "gelu": nat.DX_ACT_GELU_TANH,
+    "gelu_tanh": nat.DX_ACT_GELU_TANH,
+    "gelu_erf": nat.DX_ACT_GELU_ERF,
+    "silu": nat.DX_ACT_SILU,
+    "swish": nat.DX_ACT_SILU,
+}
+
+DTYPE_CODES = {
+    torch.float32: nat.DX_DTYPE_F32,
+    torch.float16: nat.DX_DTYPE_F16,
+    torch.bfloat16: nat.DX_DTYPE_BF16,
+}
+
+# Zero-filled workspaces, one per (device, stream): the decode kernel leaves
+# its tickets at zero after every call, so a buffer is reused as is.  A
+# workspace is never shared by two streams, so concurrent calls cannot race.
+_ws_lock = threading.Lock()
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def activation_code(activation) -> int:
+    try:
+        return ACTIVATION_CODES[activation]
+    except KeyError:
+        raise ValueError(f"unsupported activation {activation!r}; expected one of "
+                         f"{sorted(k for k in ACTIVATION_CODES if k)}") from None
+
+
+def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor | None:
+    if nbytes == 0:
+        return None
+    key = (device.index, stream)
+    with _ws_lock:
+        buf = _workspaces.get(key)
+        if buf is None or buf.numel() < nbytes:
+            buf = torch.zeros(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+            _workspaces[key] = buf
+        return buf
+
+
+def reset_workspaces() -> None:
+    """Drop cached workspaces (after a device timeout left tickets set)."""
+    with _ws_lock:
+        _workspaces.clear()
+
+
+def _check_matrix(name: str, t: torch.Tensor, rows: int | None, cols: int | None) -> None:
+    if t.dim() != 2:
+        raise ValueError(f"{name} must be 2-D, got shape {tuple(t.shape)}")
+    if rows is not None and t.shape[0] != rows:
+        raise ValueError(f"{name} has {t.shape[0]} rows, expected {rows}")
+    if cols is not None and t.shape[1] != cols:
+        raise ValueError(f"{name} has {t.shape[1]} columns, expected {cols}")
+    if t.shape[1] > 1 and t.stride(1) != 1:
+        raise ValueError(f"{name} must have unit stride along its last dimension")
+    if t.shape[0] > 1 and t.stride(0) < t.shape[1]:
+        raise ValueError(f"{name} rows overlap (stride {t.stride(0)} < {t.shape[1]})")
+
+
+def _ld(t: torch.Tensor) -> int:
+    return max(t.stride(0), t.shape[1], 1) if t.shape[0] > 1 else max(t.shape[1], 1)
+
+
+def fused_linear(X: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None = None,
+                 activation=None, residual: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None, kernel: str = "auto") -> torch.Tensor:
+    """Y = act(X @ W + bias) + residual, one fused launch on X's device."""
+    act = activation_code(activation)
+    if kernel not in nat.KERNEL_NAMES:
+        raise ValueError(f"unknown kernel {kernel!r}; expected one of {list(nat.KERNEL_NAMES)}")
+    if not isinstance(X, torch.Tensor) or not isinstance(W, torch.Tensor):
+        raise TypeError("X and W must be torch tensors")
+    if X.device.type != "cuda":
+        raise ValueError("fused_linear runs on CUDA tensors only (the engine has no CPU path)")
+    if X.dtype not in DTYPE_CODES:
+        raise ValueError(f"unsupported dtype {X.dtype}; expected float32, float16 or bfloat16")
+    _check_matrix("X", X, None, None)
+    M, K = X.shape
+    _check_matrix("W", W, K, None)
+    N = W.shape[1]
+    tensors = {"W": W}
+    if bias is not None:
+        if bias.dim() != 1 or bias.shape[0] != N:
+            raise ValueError(f"bias must have shape ({N},), got {tuple(bias.shape)}")
+        if not bias.is_contiguous():
+            raise ValueError("bias must be contiguous")
+        tensors["bias"] = bias
+    if residual is not None:
+        _check_matrix("residual", residual, M, N)
+        tensors["residual"] = residual
+    if out is None:
+        out = torch.empty((M, N), dtype=X.dtype, device=X.device)
+    else:
+        _check_matrix("out", out, M, N)
+        tensors["out"] = out
+    for name, t in tensors.items():
+        if t.dtype != X.dtype:
+            raise ValueError(f"{name} dtype {t.dtype} differs from X dtype {X.dtype}")
+        if t.device != X.device:
+            raise ValueError(f"{name} is on {t.device}, X is on {X.device}")
+
+    lib = nat.load()
+    dtype = DTYPE_CODES[X.dtype]
+    kcode = nat.KERNEL_NAMES[kernel]
+    with torch.cuda.device(X.device):
+        stream = torch.cuda.current_stream(X.device).cuda_stream
+        ws_bytes = lib.dx_fused_linear_workspace_size(M, N, K, dtype, kcode)
+        ws = _workspace(X.device, stream, ws_bytes)
+        rc = lib.dx_fused_linear_ex(
+            X.data_ptr(), W.data_ptr(),
+            bias.data_ptr() if bias is not None else None,
+            residual.data_ptr() if residual is not None else None,
+            out.data_ptr(), M, N, K, _ld(X), _ld(W),
+            _ld(residual) if residual is not None else 0, _ld(out),
+            dtype, act, kcode,
+            ws.data_ptr() if ws is not None else None,
+            ws.numel() if ws is not None else 0, stream)
+    nat.check("dx_fused_linear", rc)
+    return out
+
+
+def selected_kernel(M: int, N: int, K: int, dtype: torch.dtype) -> str:
+    """Name of the kernel variant the engine picks for this problem."""
+    code = nat.load().dx_select_kernel(M, N, K, DTYPE_CODES[dtype])
+    return {v: k for k, v in nat.KERNEL_NAMES.items()}[code]

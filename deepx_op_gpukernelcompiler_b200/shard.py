@@ -1,0 +1,146 @@
+"""Megatron-style partitioning of the fused linear over ranks (one per GPU).
+
+The reference runs on one GPU only.  Large problems are split here the
+standard way, one process per GPU over ``torch.distributed`` (NCCL on GPUs):
+
+* ``ColumnParallelLinear`` — a single fused layer Y = act(X W + b): rank r
+  owns the column slice W[:, n_r0:n_r1] and bias[n_r0:n_r1] and produces
+  Y[:, n_r0:n_r1].  No data-path collective (``gather_output=True`` adds an
+  all-gather for callers that need the full Y on every rank).
+* ``ParallelMLP`` — the two-GEMM chain Y = act(X W1 + b1) W2 + b2 + X:
+  W1 column-sharded, W2 row-sharded with the same hidden slice, so
+  H_r = act(X W1_r + b1_r) stays local and Y = sum_r H_r W2_r needs one
+  all-reduce (SUM).  b2 and the residual X are added exactly once, inside
+  rank 0's second fused launch.  With ``chunks > 1`` the second GEMM runs in
+  M-chunks and each chunk's all-reduce is issued asynchronously while the
+  next chunk computes.
+
+Shard boundaries are multiples of ``align`` elements (default 64) so every
+slice of a row-major matrix starts on a 128-byte boundary and stays
+addressable by TMA.  The compute function is injectable (``linear_fn``,
+signature of ``linear.fused_linear``) so the partitioning logic can be run
+on CPU ranks in tests; by default it is the B200 engine.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+
+def shard_bounds(n: int, world: int, rank: int, align: int = 64) -> tuple[int, int]:
+    """[start, end) of rank's slice of n items; boundaries are multiples of
+    `align` (except the final end), slices as even as that allows."""
+    if world <= 0 or not 0 <= rank < world:
+        raise ValueError(f"bad rank {rank} for world size {world}")
+    units = (n + align - 1) // align
+    base, extra = divmod(units, world)
+    start_u = rank * base + min(rank, extra)
+    end_u = start_u + base + (1 if rank < extra else 0)
+    return min(start_u * align, n), min(end_u * align, n)
+
+
+def _default_linear():
+    from .linear import fused_linear
+    return fused_linear
+
+
+def _group_info(group):
+    return dist.get_world_size(group), dist.get_rank(group)
+
+
+class ColumnParallelLinear:
+    """Y[:, slice_r] = act(X @ W[:, slice_r] + b[slice_r]) on every rank."""
+
+    def __init__(self, W_full: torch.Tensor, bias_full: torch.Tensor | None, activation=None,
+                 group=None, gather_output: bool = False, linear_fn=None, align: int = 64):
+        world, rank = _group_info(group)
+        self.group, self.world, self.rank = group, world, rank
+        self.n_total = W_full.shape[1]
+        self.align = align
+        self.n0, self.n1 = shard_bounds(self.n_total, world, rank, align)
+        self.W = W_full[:, self.n0:self.n1].contiguous()
+        self.bias = bias_full[self.n0:self.n1].contiguous() if bias_full is not None else None
+        self.activation = activation
+        self.gather_output = gather_output
+        self.linear_fn = linear_fn or _default_linear()
+
+    @classmethod
+    def from_shard(cls, W_shard, bias_shard, n_total: int, n0: int, activation=None, group=None,
+                   gather_output: bool = False, linear_fn=None):
+        """Build from a shard the caller already holds (no full matrix)."""
+        self = cls.__new__(cls)
+        self.group = group
+        self.world, self.rank = _group_info(group)
+        self.n_total, self.n0, self.n1 = n_total, n0, n0 + W_shard.shape[1]
+        self.align = 64
+        self.W, self.bias = W_shard, bias_shard
+        self.activation, self.gather_output = activation, gather_output
+        self.linear_fn = linear_fn or _default_linear()
+        return self
+
+    def __call__(self, X: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+        Y = self.linear_fn(X, self.W, self.bias, self.activation, out=out)
+        if not self.gather_output:
+            return Y
+        bounds = [shard_bounds(self.n_total, self.world, r, self.align) for r in range(self.world)]
+        sizes = [e - s for s, e in bounds]
+        # Shards may differ in width; gather equal-size padded blocks.
+        width = max(sizes)
+        buf = torch.zeros((X.shape[0], width), dtype=Y.dtype, device=Y.device)
+        buf[:, :Y.shape[1]] = Y
+        parts = [torch.empty_like(buf) for _ in range(self.world)]
+        dist.all_gather(parts, buf, group=self.group)
+        return torch.cat([p[:, :sz] for p, sz in zip(parts, sizes)], dim=1)
+
+
+class ParallelMLP:
+    """Y = act(X W1 + b1) W2 + b2 + X with W1 column- and W2 row-sharded."""
+
+    def __init__(self, W1_full, b1_full, W2_full, b2_full, activation="gelu", group=None,
+                 linear_fn=None, chunks: int = 1, align: int = 64):
+        world, rank = _group_info(group)
+        self.group, self.world, self.rank = group, world, rank
+        hidden = W1_full.shape[1]
+        if W2_full.shape[0] != hidden:
+            raise ValueError("W1 columns and W2 rows must match")
+        self.h0, self.h1 = shard_bounds(hidden, world, rank, align)
+        self.W1 = W1_full[:, self.h0:self.h1].contiguous()
+        self.b1 = b1_full[self.h0:self.h1].contiguous() if b1_full is not None else None
+        self.W2 = W2_full[self.h0:self.h1, :].contiguous()
+        self.b2 = b2_full.contiguous() if (b2_full is not None and rank == 0) else None
+        self.activation = activation
+        self.linear_fn = linear_fn or _default_linear()
+        self.chunks = max(1, int(chunks))
+
+    @classmethod
+    def from_shards(cls, W1_shard, b1_shard, W2_shard, b2_full, activation="gelu", group=None,
+                    linear_fn=None, chunks: int = 1):
+        self = cls.__new__(cls)
+        self.group = group
+        self.world, self.rank = _group_info(group)
+        self.W1, self.b1, self.W2 = W1_shard, b1_shard, W2_shard
+        self.b2 = b2_full if self.rank == 0 else None
+        self.activation = activation
+        self.linear_fn = linear_fn or _default_linear()
+        self.chunks = max(1, int(chunks))
+        return self
+
+    def __call__(self, X: torch.Tensor, hidden: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+        M = X.shape[0]
+        H = self.linear_fn(X, self.W1, self.b1, self.activation, out=hidden)
+        Y = out if out is not None else torch.empty((M, self.W2.shape[1]), dtype=X.dtype,
+                                                    device=X.device)
+        residual_rank = self.rank == 0
+        handles = []
+        step = (M + self.chunks - 1) // self.chunks
+        for m0 in range(0, M, step):
+            m1 = min(M, m0 + step)
+            self.linear_fn(H[m0:m1], self.W2, self.b2, None,
+                           residual=X[m0:m1] if residual_rank else None, out=Y[m0:m1])
+            if self.world > 1:
+                handles.append(dist.all_reduce(Y[m0:m1], op=dist.ReduceOp.SUM, group=self.group,
+                                               async_op=True))
+        for h in handles:
+            h.wait()
+        return Y

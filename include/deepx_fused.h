@@ -1,0 +1,126 @@
+/*
+ * deepx_fused.h — C ABI of the B200 fused GEMM + bias + activation engine.
+ *
+ * One operation:  Y[M,N] = act(X[M,K] @ W[K,N] + bias[N]) (+ R[M,N])
+ *
+ * This is the drop-in replacement for the kernels the reference compiles for
+ * its `linear*` fusion patterns:
+ *   - deepx_op_gpukernelcompiler/kernel_triton.py:24-89  (Triton `_kernel`,
+ *     `make_linear_kernel(activation) -> kernel_fn(A, B, bias) -> C`)
+ *   - deepx_op_gpukernelcompiler/kernel_tilelang.py:23-55 (TileLang `main`)
+ *   - the raw-pointer runtime entry the design docs describe but never build:
+ *     `kernel_fn(x_ptr, W_ptr, b_ptr, out_ptr, cuda_stream)`
+ *     (doc/kvlang-to-tilelang-interface.md:79-98,
+ *      doc/kernel-compiler-analysis.md:113-134).
+ *
+ * Conventions (all entry points):
+ *   - Matrices are row-major with an explicit leading dimension in ELEMENTS:
+ *     X[m*ldx + k], W[k*ldw + n] (W is K x N, i.e. `x @ W`), Y[m*ldy + n],
+ *     R[m*ldr + n].  bias is a dense vector of N elements.
+ *   - X, W, bias, R and Y share one element type (`dtype`); accumulation is
+ *     always fp32.  The output has the input dtype, as in the reference
+ *     (kernel_triton.py:74 allocates C with A.dtype).
+ *   - Epilogue order: Y = act(acc + bias) + R.  bias and R may be NULL.
+ *   - The caller owns every buffer (inputs, output and workspace), as in the
+ *     docs' runtime contract (doc/kvlang-to-tilelang-interface.md:86-89).  The
+ *     library never allocates, frees or synchronises on the caller's behalf;
+ *     every launch goes to `stream` (a cudaStream_t; NULL = legacy default).
+ *   - Return value: DX_OK (0) or a negative DX_ERR_* code.  The message of the
+ *     last failure on the calling thread is available from
+ *     dx_last_error_string().
+ *   - Device-side waits are bounded: a kernel that times out sets a per-device
+ *     status word (read with dx_device_status) and returns instead of hanging.
+ */
+#ifndef DEEPX_FUSED_H_
+#define DEEPX_FUSED_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---- return codes ------------------------------------------------------ */
+#define DX_OK                     0
+#define DX_ERR_INVALID_ARGUMENT  -1   /* bad shape, stride, pointer or enum   */
+#define DX_ERR_UNSUPPORTED       -2   /* valid request this build cannot run  */
+#define DX_ERR_CUDA              -3   /* a CUDA runtime/driver call failed    */
+#define DX_ERR_WORKSPACE         -4   /* workspace missing or too small       */
+#define DX_ERR_DEVICE_TIMEOUT    -5   /* a kernel's bounded wait ran out      */
+
+/* ---- element types ----------------------------------------------------- */
+#define DX_DTYPE_F32   0   /* exact fp32 FFMA path (no TF32)                 */
+#define DX_DTYPE_F16   1   /* tcgen05 kind::f16, fp32 accumulate             */
+#define DX_DTYPE_BF16  2   /* tcgen05 kind::f16 (bf16), fp32 accumulate      */
+
+/* ---- activations (fusion.py ACTIVATION_PT + the kernels' erf GELU) ------ */
+#define DX_ACT_NONE       0  /* pattern `linear`                             */
+#define DX_ACT_RELU       1  /* `linear_relu`   (fusion.py:88)               */
+#define DX_ACT_GELU_TANH  2  /* `linear_gelu`   (fusion.py:89, tanh approx)  */
+#define DX_ACT_GELU_ERF   3  /* exact GELU of kernel_triton.py:61,
+                                kernel_tilelang.py:17                        */
+#define DX_ACT_SILU       4  /* `linear_silu` / `linear_swish` (fusion.py:90-91) */
+
+/* ---- kernel variants --------------------------------------------------- */
+#define DX_KERNEL_AUTO    0  /* pick by shape, dtype and alignment           */
+#define DX_KERNEL_UMMA    1  /* persistent tcgen05 + TMEM + TMA GEMM         */
+#define DX_KERNEL_DECODE  2  /* swap-AB split-K tcgen05 kernel, M <= 64      */
+#define DX_KERNEL_SIMT    3  /* CUDA-core FFMA kernel (fp32, odd strides)    */
+
+/* Device status bits reported by dx_device_status. */
+#define DX_DEVICE_STATUS_TIMEOUT  1
+
+/*
+ * Fused linear: Y = act(X @ W + bias) + R on `stream`.
+ * Replaces kernel_triton.py:70-89 `kernel_fn(A, B, bias)` and
+ * kernel_tilelang.py:26-53 `main(A, B, bias, C)`; the pointer form is the
+ * docs' `kernel_fn(x_ptr, W_ptr, b_ptr, out_ptr, cuda_stream)`
+ * (doc/kvlang-to-tilelang-interface.md:92) with the shape passed explicitly.
+ * `workspace` may be NULL when dx_fused_linear_workspace_size() returns 0 for
+ * the call; otherwise it must hold that many bytes, have been zero-filled
+ * before its first use, and not be used by two calls at once (the kernels
+ * leave it zero-filled again on success).
+ */
+int dx_fused_linear(const void* X, const void* W, const void* bias,
+                    const void* R, void* Y,
+                    int64_t M, int64_t N, int64_t K,
+                    int64_t ldx, int64_t ldw, int64_t ldr, int64_t ldy,
+                    int dtype, int act,
+                    void* workspace, size_t workspace_bytes,
+                    void* stream);
+
+/* Same as dx_fused_linear with the kernel variant forced (DX_KERNEL_*).
+ * Used by tests and benchmarks to pin one implementation. */
+int dx_fused_linear_ex(const void* X, const void* W, const void* bias,
+                       const void* R, void* Y,
+                       int64_t M, int64_t N, int64_t K,
+                       int64_t ldx, int64_t ldw, int64_t ldr, int64_t ldy,
+                       int dtype, int act, int kernel,
+                       void* workspace, size_t workspace_bytes,
+                       void* stream);
+
+/* Workspace bytes that dx_fused_linear(_ex) needs for this problem and
+ * variant (DX_KERNEL_AUTO resolves as dx_select_kernel does). */
+size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K,
+                                      int dtype, int kernel);
+
+/* The variant DX_KERNEL_AUTO picks for a problem with contiguous rows
+ * (ld == row length) and 16-byte-aligned pointers. */
+int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype);
+
+/* Message of the last failed call on this thread ("" if none). */
+const char* dx_last_error_string(void);
+
+/* Synchronises `stream`, then reads and clears the calling device's status
+ * word (DX_DEVICE_STATUS_* bits) into *status. */
+int dx_device_status(void* stream, int* status);
+
+/* ABI version: 100 * major + minor. */
+int dx_version(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* DEEPX_FUSED_H_ */

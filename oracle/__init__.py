@@ -1,0 +1,14 @@
+"""ORACLE — test infrastructure only.
+
+CPU restatements of the reference's fused-linear oracle used to check the
+engine.  Only tests/, __graft_entry__.smoke() and bench.py's CPU baseline
+may import this package; the engine never does.
+"""
+from .fused_linear import (  # noqa: F401
+    ACT_CODES,
+    activation_f64,
+    fused_linear_f32,
+    fused_linear_f64,
+    mlp_residual_f32,
+    mlp_residual_f64,
+)

@@ -1,0 +1,140 @@
+"""The C-ABI library: loads, exports every declared symbol, and rejects bad
+arguments on the host before touching a device (CPU; no compute calls)."""
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from deepx_op_gpukernelcompiler_b200 import _build, _native as nat
+from deepx_op_gpukernelcompiler_b200 import fused_linear, make_linear_kernel
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+@pytest.fixture(scope="module")
+def lib():
+    _build.build()
+    return nat.load()
+
+
+def _declared_functions() -> set[str]:
+    names = set()
+    for header in (ROOT / "include").glob("*.h"):
+        text = header.read_text()
+        names |= set(re.findall(r"^\s*(?:const\s+)?[\w]+\s*\*?\s*(dx_\w+)\s*\(", text, re.M))
+    return names
+
+
+def test_every_declared_symbol_is_exported(lib):
+    declared = _declared_functions()
+    assert {"dx_fused_linear", "dx_fused_linear_ex", "dx_last_error_string"} <= declared
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+    assert declared == set(nat.SIGNATURES), "ctypes signatures out of sync with the header"
+
+
+def test_library_is_sm100a_only():
+    lib_bytes = nat.LIB_PATH.read_bytes()
+    assert b"sm_100a" in lib_bytes
+
+
+def test_version(lib):
+    assert lib.dx_version() == 100
+
+
+def _call(lib, **kw):
+    args = dict(X=None, W=None, bias=None, R=None, Y=None, M=4, N=4, K=4, ldx=4, ldw=4, ldr=0,
+                ldy=4, dtype=nat.DX_DTYPE_BF16, act=0, kernel=0, ws=None, ws_bytes=0, stream=None)
+    args.update(kw)
+    return lib.dx_fused_linear_ex(args["X"], args["W"], args["bias"], args["R"], args["Y"],
+                                  args["M"], args["N"], args["K"], args["ldx"], args["ldw"],
+                                  args["ldr"], args["ldy"], args["dtype"], args["act"],
+                                  args["kernel"], args["ws"], args["ws_bytes"], args["stream"])
+
+
+FAKE = 0x1000  # never dereferenced: validation fails first
+
+
+@pytest.mark.parametrize("kw,code,needle", [
+    (dict(dtype=7), nat.DX_ERR_INVALID_ARGUMENT, "dtype"),
+    (dict(act=9), nat.DX_ERR_INVALID_ARGUMENT, "activation"),
+    (dict(kernel=5), nat.DX_ERR_INVALID_ARGUMENT, "kernel"),
+    (dict(M=-1), nat.DX_ERR_INVALID_ARGUMENT, "negative"),
+    (dict(M=1 << 40), nat.DX_ERR_UNSUPPORTED, "2^31"),
+    (dict(Y=None, X=FAKE, W=FAKE), nat.DX_ERR_INVALID_ARGUMENT, "Y is NULL"),
+    (dict(Y=FAKE), nat.DX_ERR_INVALID_ARGUMENT, "X or W"),
+    (dict(X=FAKE, W=FAKE, Y=FAKE, ldx=3), nat.DX_ERR_INVALID_ARGUMENT, "ldx"),
+    (dict(X=FAKE, W=FAKE, Y=FAKE, ldw=2), nat.DX_ERR_INVALID_ARGUMENT, "ldw"),
+    (dict(X=FAKE, W=FAKE, Y=FAKE, ldy=1), nat.DX_ERR_INVALID_ARGUMENT, "ldy"),
+    (dict(X=FAKE, W=FAKE, Y=FAKE, R=FAKE, ldr=2), nat.DX_ERR_INVALID_ARGUMENT, "ldr"),
+])
+def test_host_validation(lib, kw, code, needle):
+    assert _call(lib, **kw) == code
+    assert needle in nat.last_error()
+
+
+def test_empty_problem_is_a_no_op(lib):
+    assert _call(lib, M=0) == nat.DX_OK
+    assert _call(lib, N=0) == nat.DX_OK
+    assert nat.last_error() == ""
+
+
+def test_kernel_selection(lib):
+    assert lib.dx_select_kernel(256, 512, 512, nat.DX_DTYPE_F32) == nat.DX_KERNEL_SIMT
+    assert lib.dx_select_kernel(16, 28672, 8192, nat.DX_DTYPE_F16) == nat.DX_KERNEL_DECODE
+    assert lib.dx_select_kernel(8192, 14336, 4096, nat.DX_DTYPE_BF16) == nat.DX_KERNEL_UMMA
+    assert lib.dx_select_kernel(8192, 14336, 4095, nat.DX_DTYPE_BF16) == nat.DX_KERNEL_SIMT
+    assert lib.dx_select_kernel(64, 100, 0, nat.DX_DTYPE_BF16) == nat.DX_KERNEL_SIMT
+
+
+def test_workspace_is_zero_when_not_needed(lib):
+    assert lib.dx_fused_linear_workspace_size(8192, 14336, 4096, nat.DX_DTYPE_BF16,
+                                              nat.DX_KERNEL_UMMA) == 0
+    assert lib.dx_fused_linear_workspace_size(16, 512, 512, nat.DX_DTYPE_F32, 0) == 0
+
+
+def test_error_string_is_thread_local(lib):
+    import threading
+    _call(lib, dtype=7)
+    seen = {}
+
+    def worker():
+        seen["other"] = nat.last_error()
+
+    t = threading.Thread(target=worker)
+    t.start()
+    t.join()
+    assert seen["other"] == ""
+    assert "dtype" in nat.last_error()
+
+
+def test_native_error_carries_code(lib):
+    with pytest.raises(nat.NativeError) as ei:
+        nat.check("dx_fused_linear", _call(lib, act=9))
+    assert ei.value.code == nat.DX_ERR_INVALID_ARGUMENT
+
+
+def test_wrapper_rejects_cpu_tensors():
+    with pytest.raises(ValueError, match="CUDA"):
+        fused_linear(torch.zeros(4, 4), torch.zeros(4, 4))
+
+
+def test_wrapper_rejects_unknown_activation():
+    with pytest.raises(ValueError, match="activation"):
+        make_linear_kernel("tanh")
+    with pytest.raises(ValueError, match="kernel"):
+        fused_linear(torch.zeros(4, 4), torch.zeros(4, 4), kernel="cublas")
+
+
+def test_missing_library_fails_loudly(monkeypatch, tmp_path):
+    monkeypatch.setattr(nat, "_lib", None)
+    monkeypatch.setattr(nat, "LIB_PATH", tmp_path / "absent.so")
+    with pytest.raises(RuntimeError, match="not built"):
+        nat.load()
+
+
+def test_ctypes_types_match_header(lib):
+    assert lib.dx_fused_linear.restype is ctypes.c_int
+    assert lib.dx_fused_linear_workspace_size.restype is ctypes.c_size_t

@@ -1,0 +1,212 @@
+"""Engine parity on the GPU, through the C ABI (gpu).
+
+Every kernel variant against the golden outputs of the reference oracle and
+against the CPU oracle on seeded inputs, at the tolerances of the workloads:
+fp32 rtol = atol = 1e-4, fp16/bf16 (fp32 accumulate) rtol = atol = 2e-2.
+"""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from deepx_op_gpukernelcompiler_b200 import _native as nat
+from deepx_op_gpukernelcompiler_b200 import fused_linear, mlp_residual
+from deepx_op_gpukernelcompiler_b200.linear import selected_kernel
+from golden_data import cases, load
+
+pytestmark = pytest.mark.gpu
+
+TOL = {torch.float32: (1e-4, 1e-4), torch.float16: (2e-2, 2e-2), torch.bfloat16: (2e-2, 2e-2)}
+DT = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}
+DEV = torch.device("cuda:0")
+
+
+def _variants(case):
+    if case["dtype"] == "f32":
+        return ["auto", "simt"]
+    out = ["auto", "simt", "umma"]
+    if case["M"] <= 64:
+        out.append("decode")
+    return out
+
+
+def _assert_close(got: torch.Tensor, ref, dtype, what=""):
+    rtol, atol = TOL[dtype]
+    g = got.float().cpu().numpy()
+    r = ref.numpy() if isinstance(ref, torch.Tensor) else np.asarray(ref)
+    bad = ~np.isclose(g, r, rtol=rtol, atol=atol)
+    if bad.any():
+        idx = np.argwhere(bad)[0]
+        raise AssertionError(f"{what}: {bad.sum()} of {bad.size} elements off; first at {tuple(idx)}: "
+                             f"got {g[tuple(idx)]}, want {r[tuple(idx)]}; max |diff| "
+                             f"{np.abs(g - r).max():.4g}")
+
+
+def _status_clean():
+    assert nat.device_status(torch.cuda.current_stream().cuda_stream) == 0
+
+
+@pytest.mark.parametrize("case", [c for c in cases() if not c["mlp"]], ids=lambda c: c["name"])
+def test_golden_linear(case):
+    t = {k: v.to(DEV) for k, v in load(case).items()}
+    dt = DT[case["dtype"]]
+    for kern in _variants(case):
+        Y = fused_linear(t["X"], t["W"], t["bias"], case["act"], residual=t.get("R"), kernel=kern)
+        torch.cuda.synchronize()
+        _assert_close(Y, t["Y"].cpu(), dt, f"{case['name']} [{kern}]")
+    _status_clean()
+
+
+@pytest.mark.parametrize("case", [c for c in cases() if c["mlp"]], ids=lambda c: c["name"])
+def test_golden_mlp(case):
+    t = {k: v.to(DEV) for k, v in load(case).items()}
+    Y = mlp_residual(t["X"], t["W1"], t["b1"], t["W2"], t["b2"], case["act"])
+    torch.cuda.synchronize()
+    _assert_close(Y, t["Y"].cpu(), DT[case["dtype"]], case["name"])
+
+
+def _rand(M, K, N, dtype, seed, residual=False):
+    g = torch.Generator().manual_seed(seed)
+    X = torch.randn(M, K, generator=g).to(dtype)
+    W = (torch.randn(K, N, generator=g) / max(K, 1) ** 0.5).to(dtype)
+    b = (torch.rand(N, generator=g) * 0.2 - 0.1).to(dtype)
+    R = torch.randn(M, N, generator=g).to(dtype) if residual else None
+    return X, W, b, R
+
+
+SHAPES = [  # (M, K, N): tile edges, ragged K/N/M, single rows/columns
+    (1, 64, 128), (7, 72, 136), (16, 1024, 1024), (33, 200, 264), (64, 4096, 512),
+    (65, 64, 64), (127, 128, 128), (128, 64, 256), (129, 136, 392), (255, 520, 520),
+    (256, 64, 1024), (300, 1000, 8), (513, 256, 760), (1024, 2048, 768),
+]
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("M,K,N", SHAPES)
+def test_shapes_all_variants(M, K, N, dtype):
+    X, W, b, _ = _rand(M, K, N, dtype, seed=M * 7 + K * 3 + N)
+    ref = oracle.fused_linear_f64(X, W, b, "gelu_erf")
+    Xd, Wd, bd = X.to(DEV), W.to(DEV), b.to(DEV)
+    variants = ["auto", "umma", "simt"] + (["decode"] if M <= 64 else [])
+    for kern in variants:
+        Y = fused_linear(Xd, Wd, bd, "gelu_erf", kernel=kern)
+        torch.cuda.synchronize()
+        _assert_close(Y, ref, dtype, f"{M}x{K}x{N} {dtype} [{kern}]")
+    _status_clean()
+
+
+@pytest.mark.parametrize("act", [None, "relu", "gelu", "gelu_erf", "silu", "swish"])
+@pytest.mark.parametrize("kern", ["umma", "decode"])
+def test_activations_with_residual(act, kern):
+    M = 48 if kern == "decode" else 200
+    X, W, b, R = _rand(M, 256, 320, torch.bfloat16, seed=11, residual=True)
+    ref = oracle.fused_linear_f64(X, W, b, act, residual=R)
+    Y = fused_linear(X.to(DEV), W.to(DEV), b.to(DEV), act, residual=R.to(DEV), kernel=kern)
+    torch.cuda.synchronize()
+    _assert_close(Y, ref, torch.bfloat16, f"{act} residual [{kern}]")
+
+
+@pytest.mark.parametrize("kern", ["umma", "decode", "simt"])
+def test_no_bias(kern):
+    X, W, _, _ = _rand(32, 128, 256, torch.float16, seed=5)
+    ref = oracle.fused_linear_f64(X, W, None, "relu")
+    Y = fused_linear(X.to(DEV), W.to(DEV), None, "relu", kernel=kern)
+    torch.cuda.synchronize()
+    _assert_close(Y, ref, torch.float16, f"no bias [{kern}]")
+
+
+@pytest.mark.parametrize("kern", ["umma", "decode", "simt"])
+def test_strided_views(kern):
+    """Row pitches larger than the row length (column slices of wider buffers)."""
+    M, K, N = 40, 192, 256
+    X, W, b, R = _rand(M, K, N, torch.bfloat16, seed=9, residual=True)
+    Xb = torch.zeros(M, K + 64, dtype=X.dtype)
+    Xb[:, 32:32 + K] = X
+    Wb = torch.zeros(K, N + 128, dtype=W.dtype)
+    Wb[:, 64:64 + N] = W
+    Rb = torch.zeros(M, N + 8, dtype=R.dtype)
+    Rb[:, :N] = R
+    Xd, Wd, Rd = Xb.to(DEV), Wb.to(DEV), Rb.to(DEV)
+    Yb = torch.full((M, N + 16), 7.0, dtype=X.dtype, device=DEV)
+    out = Yb[:, 8:8 + N]
+    fused_linear(Xd[:, 32:32 + K], Wd[:, 64:64 + N], b.to(DEV), "silu", residual=Rd[:, :N],
+                 out=out, kernel=kern)
+    torch.cuda.synchronize()
+    ref = oracle.fused_linear_f64(X, W, b, "silu", residual=R)
+    _assert_close(out, ref, torch.bfloat16, f"strided [{kern}]")
+    assert torch.all(Yb[:, :8] == 7) and torch.all(Yb[:, 8 + N:] == 7), "wrote outside out"
+
+
+def test_fp32_exact_path():
+    X, W, b, R = _rand(130, 300, 70, torch.float32, seed=3, residual=True)
+    Y = fused_linear(X.to(DEV), W.to(DEV), b.to(DEV), "gelu", residual=R.to(DEV))
+    torch.cuda.synchronize()
+    _assert_close(Y, oracle.fused_linear_f64(X, W, b, "gelu", residual=R), torch.float32, "fp32")
+
+
+def test_misaligned_rows_fall_back_to_simt():
+    """K = 45: rows are not 16-byte multiples, so TMA cannot address them."""
+    X, W, b, _ = _rand(100, 45, 77, torch.bfloat16, seed=4)
+    assert selected_kernel(100, 77, 45, torch.bfloat16) == "simt"
+    Y = fused_linear(X.to(DEV), W.to(DEV), b.to(DEV), "relu")
+    torch.cuda.synchronize()
+    _assert_close(Y, oracle.fused_linear_f64(X, W, b, "relu"), torch.bfloat16, "K=45 auto")
+    with pytest.raises(nat.NativeError) as ei:
+        fused_linear(X.to(DEV), W.to(DEV), b.to(DEV), "relu", kernel="umma")
+    assert ei.value.code == nat.DX_ERR_UNSUPPORTED
+
+
+def test_k_zero_gives_act_of_bias():
+    b = torch.tensor([1.0, -2.0, 3.0, -4.0] * 4, dtype=torch.bfloat16)
+    X = torch.empty(5, 0, dtype=torch.bfloat16, device=DEV)
+    W = torch.empty(0, 16, dtype=torch.bfloat16, device=DEV)
+    Y = fused_linear(X, W, b.to(DEV), "relu")
+    torch.cuda.synchronize()
+    assert torch.equal(Y.cpu(), torch.relu(b).expand(5, 16))
+
+
+def test_decode_without_workspace_is_rejected():
+    lib = nat.load()
+    X, W, b, _ = _rand(16, 128, 256, torch.float16, seed=1)
+    Xd, Wd, bd = X.to(DEV), W.to(DEV), b.to(DEV)
+    Y = torch.empty(16, 256, dtype=torch.float16, device=DEV)
+    rc = lib.dx_fused_linear_ex(Xd.data_ptr(), Wd.data_ptr(), bd.data_ptr(), None, Y.data_ptr(),
+                                16, 256, 128, 128, 256, 0, 256, nat.DX_DTYPE_F16, 0,
+                                nat.DX_KERNEL_DECODE, None, 0, None)
+    assert rc == nat.DX_ERR_WORKSPACE
+    # AUTO without a workspace picks the tensor-core GEMM instead.
+    rc = lib.dx_fused_linear(Xd.data_ptr(), Wd.data_ptr(), bd.data_ptr(), None, Y.data_ptr(),
+                             16, 256, 128, 128, 256, 0, 256, nat.DX_DTYPE_F16, 0, None, 0, None)
+    assert rc == nat.DX_OK
+    torch.cuda.synchronize()
+    _assert_close(Y, oracle.fused_linear_f64(X, W, b, None), torch.float16, "auto w/o workspace")
+
+
+@pytest.mark.parametrize("kern,M", [("umma", 1000), ("decode", 16)])
+def test_bitwise_deterministic(kern, M):
+    X, W, b, _ = _rand(M, 2048, 1536, torch.bfloat16, seed=21)
+    Xd, Wd, bd = X.to(DEV), W.to(DEV), b.to(DEV)
+    Y1 = fused_linear(Xd, Wd, bd, "silu", kernel=kern)
+    Y2 = fused_linear(Xd, Wd, bd, "silu", kernel=kern)
+    torch.cuda.synchronize()
+    assert torch.equal(Y1, Y2)
+
+
+def test_decode_tickets_reset_across_shapes():
+    """The split-K workspace is reused across calls of different shapes."""
+    for (M, K, N) in [(16, 4096, 1024), (3, 640, 2048), (64, 8192, 256), (16, 4096, 1024)]:
+        X, W, b, _ = _rand(M, K, N, torch.float16, seed=M + K + N)
+        Y = fused_linear(X.to(DEV), W.to(DEV), b.to(DEV), "gelu_erf", kernel="decode")
+        torch.cuda.synchronize()
+        _assert_close(Y, oracle.fused_linear_f64(X, W, b, "gelu_erf"), torch.float16,
+                      f"decode {M}x{K}x{N}")
+    _status_clean()
+
+
+def test_nonzero_stream():
+    s = torch.cuda.Stream()
+    X, W, b, _ = _rand(256, 512, 512, torch.bfloat16, seed=2)
+    with torch.cuda.stream(s):
+        Y = fused_linear(X.to(DEV), W.to(DEV), b.to(DEV), "relu")
+    s.synchronize()
+    _assert_close(Y, oracle.fused_linear_f64(X, W, b, "relu"), torch.bfloat16, "side stream")
