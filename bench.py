@@ -3,6 +3,7 @@
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
                     [--workload NAME] [--no-extra]
     python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N
+    python bench.py --profile --workload NAME --steps 1 --warmup 2   (for ncu)
 
 Headline workload: ``ffn_up_silu_8192x4096x14336_bf16`` —
 Y = SiLU(X[8192,4096] @ W[4096,14336] + b), bf16 in/out, fp32 accumulate,
@@ -216,11 +217,15 @@ def run_reference(args) -> None:
 
 
 # ------------------------------------------------------------ GPU arm
-def _time_launches(fn, steps, flush, stream):
-    """CUDA-event time of each launch (flush outside the events), ms list."""
+def _time_launches(fn, steps, flush, stream, host_us_per_step: float = 80.0):
+    """CUDA-event time of each launch (flush outside the events), ms list.
+
+    A device-side sleep is queued first, long enough for the host to enqueue
+    every step behind it, so no event pair brackets host enqueue time."""
     import torch
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(steps)]
+    torch.cuda._sleep(int(steps * host_us_per_step * 1e-6 * 2.0e9))
     for s, e in evs:
         flush()
         s.record(stream)
@@ -292,6 +297,16 @@ def run_gpu(args) -> None:
     for _ in range(max(1, args.warmup)):
         step()
     torch.cuda.synchronize()
+    plan = _native.last_launch_plan()
+    if args.profile:
+        # Profiling mode: exactly W warm-up + K timed launches, nothing else.
+        times = _time_launches(step, args.steps, flush, stream)
+        sampler.stop()
+        print(json.dumps({"profile": w.name, "rank": rank, "launch_ms": times, "plan": plan}),
+              flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
     t_end = time.time() + 1.0
     while time.time() < t_end:
         for _ in range(20):
@@ -359,7 +374,7 @@ def run_gpu(args) -> None:
             "config": {"workload": w.name, "M": w.M, "K": w.K, "N": w.N, "act": w.act,
                        "parallelism": f"column-parallel N-shard x{world} (no collective)",
                        "n_per_rank": n_loc, "l2": "flushed before each timed launch (256 MiB write)",
-                       "kernel": "umma"},
+                       "kernel": plan},
             "roofline": {"bound": "tensor", "achieved": round(achieved, 2), "peak": peak,
                          "unit": "TFLOP/s", "frac": round(achieved / peak, 4),
                          "peak_source": f"bf16_tflops burst, {peak_kind}",
@@ -401,8 +416,10 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
     g = torch.Generator(device=dev)
     g.manual_seed(w.seed * 1000 + rank)
     X = torch.randn(w.M, w.K, generator=g, device=dev).to(w.torch_dtype)
-    # Enough weight copies that their total exceeds L2 (rotated per step).
-    copies = max(1, math.ceil(3 * (128 << 20) / (w.K * n_loc * 2)))
+    # Rotated weight copies, together at least 3x the L2 size: every step
+    # streams W from HBM without an L2 flush (whose dirty lines would be
+    # written back during the timed launch).
+    copies = max(2, math.ceil(3 * (128 << 20) / (w.K * n_loc * 2)))
     Ws = [(torch.randn(w.K, n_loc, generator=g, device=dev) / math.sqrt(w.K)).to(w.torch_dtype)
           for _ in range(copies)]
     b = (torch.rand(n_loc, generator=g, device=dev) * 0.2 - 0.1).to(w.torch_dtype)
@@ -417,7 +434,7 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
         dec()
     torch.cuda.synchronize()
     _barrier(world)
-    t = _time_launches(dec, steps, flush, stream)
+    t = _time_launches(dec, steps, lambda: None, stream)
     ms = _max_over_ranks(sum(t), world, dev) / steps
     bytes_rank = 2 * (w.M * w.K + w.K * n_loc + n_loc + w.M * n_loc)
     bytes_total = w.min_bytes
@@ -426,7 +443,7 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
                    "roofline": {"bound": "hbm", "achieved": round(bytes_rank / (sum(t) / steps * 1e-3) / 1e9, 1),
                                 "peak": hbm, "unit": "GB/s",
                                 "frac": round(bytes_rank / (sum(t) / steps * 1e-3) / 1e9 / hbm, 4)},
-                   "l2": f"{copies} rotated weight copies + flush"}
+                   "l2": f"{copies} rotated weight copies (>= 3x L2), no flush"}
     del Ws, X, Y
 
     # Square GEMM: GELU-tanh(X[4096,4096] W[4096,4096] + b), bf16 (per rank
@@ -496,6 +513,8 @@ def main() -> None:
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-extra", action="store_true", help="skip the decode/square/MLP lines")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--profile", action="store_true",
+                    help="run only W warm-up and K timed launches of the workload (for ncu)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -45,8 +45,10 @@ DX_KERNEL_AUTO = 0
 DX_KERNEL_UMMA = 1
 DX_KERNEL_DECODE = 2
 DX_KERNEL_SIMT = 3
+DX_KERNEL_UMMA_1CTA = 4
 KERNEL_NAMES = {"auto": DX_KERNEL_AUTO, "umma": DX_KERNEL_UMMA,
-                "decode": DX_KERNEL_DECODE, "simt": DX_KERNEL_SIMT}
+                "decode": DX_KERNEL_DECODE, "simt": DX_KERNEL_SIMT,
+                "umma_1cta": DX_KERNEL_UMMA_1CTA}
 
 DX_DEVICE_STATUS_TIMEOUT = 1
 
@@ -61,6 +63,7 @@ SIGNATURES = {
     "dx_fused_linear_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, ctypes.c_int, ctypes.c_int]),
     "dx_select_kernel": (ctypes.c_int, [_i64, _i64, _i64, ctypes.c_int]),
     "dx_last_error_string": (ctypes.c_char_p, []),
+    "dx_last_launch_plan": (ctypes.c_char_p, []),
     "dx_device_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int)]),
     "dx_version": (ctypes.c_int, []),
 }
@@ -99,6 +102,11 @@ def load() -> ctypes.CDLL:
 
 def last_error() -> str:
     return load().dx_last_error_string().decode("utf-8", "replace")
+
+
+def last_launch_plan() -> str:
+    """Kernel variant, tiling and grid of the last launch on this thread."""
+    return load().dx_last_launch_plan().decode("utf-8", "replace")
 
 
 def check(func: str, rc: int) -> None:

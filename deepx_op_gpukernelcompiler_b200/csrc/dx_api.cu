@@ -32,10 +32,12 @@ namespace {
 
 using dx::DecodeParams;
 using dx::DecodeShape;
+using dx::Umma2Shape;
 using dx::UmmaParams;
 using dx::UmmaShape;
 
 thread_local std::string t_last_error;
+thread_local std::string t_last_plan;
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -45,6 +47,15 @@ int fail(int code, const char* fmt, ...) {
   va_end(ap);
   t_last_error = buf;
   return code;
+}
+
+void set_plan(const char* fmt, ...) {
+  char buf[256];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  t_last_plan = buf;
 }
 
 int cuda_fail(cudaError_t e, const char* what) {
@@ -190,50 +201,142 @@ int pick_bn(int64_t M, int64_t N, int sms) {
   return c128 < c256 ? 128 : 256;
 }
 
+// Pair tiles are 256 x BN; pick BN by estimated waves over the resident pairs.
+int pick_pair_bn(int64_t M, int64_t N, int pair_slots) {
+  if (N <= 128) return 128;
+  const int64_t mt = (M + 255) / 256;
+  const int64_t t256 = mt * ((N + 255) / 256);
+  const int64_t t128 = mt * ((N + 127) / 128);
+  const double c256 = static_cast<double>((t256 + pair_slots - 1) / pair_slots) * 256.0;
+  const double c128 = static_cast<double>((t128 + pair_slots - 1) / pair_slots) * 128.0 * 1.1;
+  return c128 < c256 ? 128 : 256;
+}
+
+// Rows of X per raster group: keep group_m x rows x K x 2 bytes within ~48 MB
+// (about a third of L2), with groups of equal size.
+int pick_group_m(int m_tiles, int64_t rows_per_tile, int64_t K) {
+  const int64_t panel = std::max<int64_t>(rows_per_tile * K * 2, 1);
+  const int64_t max_g = std::max<int64_t>(1, (48LL << 20) / panel);
+  const int64_t groups = (m_tiles + max_g - 1) / max_g;
+  return static_cast<int>((m_tiles + groups - 1) / groups);
+}
+
+int make_umma_maps(const Problem& pr, CUtensorMap* tA, CUtensorMap* tB, CUtensorMap* tY,
+                   CUtensorMap* tR) {
+  const CUtensorMapDataType dt = tma_dtype(pr.dtype);
+  int rc;
+  if ((rc = make_tmap_2d(tA, pr.X, dt, pr.K, pr.M, pr.ldx, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B,
+                         "X")))
+    return rc;
+  if ((rc = make_tmap_2d(tB, pr.W, dt, pr.N, pr.K, pr.ldw, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B,
+                         "W")))
+    return rc;
+  if ((rc = make_tmap_2d(tY, pr.Y, dt, pr.N, pr.M, pr.ldy, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B,
+                         "Y")))
+    return rc;
+  if (pr.R != nullptr) {
+    if ((rc = make_tmap_2d(tR, pr.R, dt, pr.N, pr.M, pr.ldr, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B,
+                           "R")))
+      return rc;
+  } else {
+    *tR = *tY;  // never read: has_residual == 0
+  }
+  return DX_OK;
+}
+
+UmmaParams umma_params(const Problem& pr, int rows_per_tile, int bn) {
+  UmmaParams p{};
+  p.M = static_cast<int>(pr.M);
+  p.N = static_cast<int>(pr.N);
+  p.K = static_cast<int>(pr.K);
+  p.m_tiles = static_cast<int>((pr.M + rows_per_tile - 1) / rows_per_tile);
+  p.n_tiles = static_cast<int>((pr.N + bn - 1) / bn);
+  p.k_blocks = static_cast<int>((pr.K + 63) / 64);
+  p.num_tiles = p.m_tiles * p.n_tiles;
+  p.group_m = pick_group_m(p.m_tiles, rows_per_tile, pr.K);
+  p.bias = pr.bias;
+  p.act = pr.act;
+  p.has_residual = pr.R != nullptr ? 1 : 0;
+  return p;
+}
+
 template <int BN, typename T>
 int launch_umma(const Problem& pr, int dev, int sms) {
   using S = UmmaShape<BN>;
   auto kern = dx::umma_fused_linear_kernel<BN, T>;
   int rc = ensure_smem_attr(dev, reinterpret_cast<const void*>(kern), S::SMEM_BYTES, false);
   if (rc) return rc;
-  const CUtensorMapDataType dt = tma_dtype(pr.dtype);
   CUtensorMap tA, tB, tY, tR;
-  if ((rc = make_tmap_2d(&tA, pr.X, dt, pr.K, pr.M, pr.ldx, 64, 128,
-                         CU_TENSOR_MAP_SWIZZLE_128B, "X")))
-    return rc;
-  if ((rc = make_tmap_2d(&tB, pr.W, dt, pr.N, pr.K, pr.ldw, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B,
-                         "W")))
-    return rc;
-  if ((rc = make_tmap_2d(&tY, pr.Y, dt, pr.N, pr.M, pr.ldy, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B,
-                         "Y")))
-    return rc;
-  if (pr.R != nullptr) {
-    if ((rc = make_tmap_2d(&tR, pr.R, dt, pr.N, pr.M, pr.ldr, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B,
-                           "R")))
-      return rc;
-  } else {
-    tR = tY;  // never read: has_residual == 0
-  }
-  UmmaParams p{};
-  p.M = static_cast<int>(pr.M);
-  p.N = static_cast<int>(pr.N);
-  p.K = static_cast<int>(pr.K);
-  p.m_tiles = static_cast<int>((pr.M + 127) / 128);
-  p.n_tiles = static_cast<int>((pr.N + BN - 1) / BN);
-  p.k_blocks = static_cast<int>((pr.K + 63) / 64);
-  p.num_tiles = p.m_tiles * p.n_tiles;
-  // Keep the X panel of one raster group (group_m x 128 rows x K) within
-  // ~48 MB so it stays L2-resident while all of W streams past it.
-  const int64_t panel = 128 * pr.K * 2;
-  p.group_m = static_cast<int>(
-      std::max<int64_t>(1, std::min<int64_t>(p.m_tiles, (48LL << 20) / std::max<int64_t>(panel, 1))));
-  p.bias = pr.bias;
-  p.act = pr.act;
-  p.has_residual = pr.R != nullptr ? 1 : 0;
+  if ((rc = make_umma_maps(pr, &tA, &tB, &tY, &tR))) return rc;
+  const UmmaParams p = umma_params(pr, 128, BN);
   const int grid = std::min(p.num_tiles, sms);
+  set_plan("umma_1cta tile=128x%d stages=%d grid=%d tiles=%d group_m=%d smem=%d", BN, S::STAGES,
+           grid, p.num_tiles, p.group_m, S::SMEM_BYTES);
   kern<<<grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tA, tB, tY, tR, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch umma_fused_linear_kernel");
+  return DX_OK;
+}
+
+cudaLaunchConfig_t pair_launch_config(int grid, int threads, int smem, cudaStream_t s,
+                                      cudaLaunchAttribute* attr) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = s;
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cfg;
+}
+
+std::map<int, int> g_pair_slots;
+
+// How many CTA pairs of the pair kernel can be resident at once (cached per
+// device; the pair kernels share one shared-memory footprint class).
+template <int BN, typename T>
+int pair_slots(int dev, int sms) {
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    auto it = g_pair_slots.find(dev);
+    if (it != g_pair_slots.end()) return it->second;
+  }
+  using S = Umma2Shape<BN>;
+  auto kern = dx::umma2_fused_linear_kernel<BN, T>;
+  if (ensure_smem_attr(dev, reinterpret_cast<const void*>(kern), S::SMEM_BYTES, false) != DX_OK)
+    return 0;
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pair_launch_config(2 * (sms / 2), S::THREADS, S::SMEM_BYTES, nullptr, attr);
+  int n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(kern), &cfg) != cudaSuccess)
+    n = 0;
+  (void)cudaGetLastError();
+  std::lock_guard<std::mutex> lk(g_mu);
+  g_pair_slots[dev] = n;
+  return n;
+}
+
+template <int BN, typename T>
+int launch_umma2(const Problem& pr, int dev, int slots) {
+  using S = Umma2Shape<BN>;
+  auto kern = dx::umma2_fused_linear_kernel<BN, T>;
+  int rc = ensure_smem_attr(dev, reinterpret_cast<const void*>(kern), S::SMEM_BYTES, false);
+  if (rc) return rc;
+  CUtensorMap tA, tB, tY, tR;
+  if ((rc = make_umma_maps(pr, &tA, &tB, &tY, &tR))) return rc;
+  const UmmaParams p = umma_params(pr, 256, BN);
+  const int grid = 2 * std::min(p.num_tiles, slots);
+  set_plan("umma_pair tile=256x%d stages=%d grid=%d pair_slots=%d tiles=%d group_m=%d smem=%d", BN,
+           S::STAGES, grid, slots, p.num_tiles, p.group_m, S::SMEM_BYTES);
+  cudaLaunchAttribute attr[1];
+  cudaLaunchConfig_t cfg = pair_launch_config(grid, S::THREADS, S::SMEM_BYTES, pr.stream, attr);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tY, tR, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch umma2_fused_linear_kernel");
   return DX_OK;
 }
 
@@ -269,6 +372,8 @@ int launch_decode(const Problem& pr, int dev, int sms, const DecodePlan& d) {
   p.partials = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + d.ticket_bytes);
   p.act = pr.act;
   (void)sms;
+  set_plan("decode mn=%d stages=%d grid=%d n_tiles=%d kbt=%d max_seg=%d workspace=%zu", MN,
+           S::STAGES, d.grid, d.n_tiles, d.kbt, d.max_seg, d.bytes);
   kern<<<d.grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tW, tX, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch decode_fused_linear_kernel");
@@ -284,6 +389,8 @@ int launch_simt(const Problem& pr, int sms) {
   T* Y = static_cast<T*>(pr.Y);
   const int M = static_cast<int>(pr.M), N = static_cast<int>(pr.N), K = static_cast<int>(pr.K);
   const int64_t big_tiles = ((pr.M + 63) / 64) * ((pr.N + 63) / 64);
+  set_plan("simt tile=%d grid=%lld", big_tiles >= 2LL * sms ? 64 : 32,
+           (long long)(big_tiles >= 2LL * sms ? big_tiles : ((pr.M + 31) / 32) * ((pr.N + 31) / 32)));
   if (big_tiles >= 2LL * sms) {
     if ((pr.M + 63) / 64 > 65535) return fail(DX_ERR_UNSUPPORTED, "M too large for the SIMT kernel");
     dim3 grid(static_cast<unsigned>((pr.N + 63) / 64), static_cast<unsigned>((pr.M + 63) / 64));
@@ -306,7 +413,7 @@ int validate(const Problem& p, int kernel) {
     return fail(DX_ERR_INVALID_ARGUMENT, "unknown dtype %d", p.dtype);
   if (p.act < DX_ACT_NONE || p.act > DX_ACT_SILU)
     return fail(DX_ERR_INVALID_ARGUMENT, "unknown activation %d", p.act);
-  if (kernel < DX_KERNEL_AUTO || kernel > DX_KERNEL_SIMT)
+  if (kernel < DX_KERNEL_AUTO || kernel > DX_KERNEL_UMMA_1CTA)
     return fail(DX_ERR_INVALID_ARGUMENT, "unknown kernel variant %d", kernel);
   if (p.M < 0 || p.N < 0 || p.K < 0)
     return fail(DX_ERR_INVALID_ARGUMENT, "negative shape M=%lld N=%lld K=%lld", (long long)p.M,
@@ -355,7 +462,15 @@ int select_variant(const Problem& p, int sms, bool ws_known) {
 template <typename T>
 int dispatch_typed(const Problem& p, int variant, int dev, int sms) {
   switch (variant) {
-    case DX_KERNEL_UMMA: {
+    case DX_KERNEL_UMMA:
+    case DX_KERNEL_UMMA_1CTA: {
+      // CTA pairs for M >= 256 (256-row tiles), single CTAs below that.
+      const int slots =
+          (p.M >= 256 && variant == DX_KERNEL_UMMA) ? pair_slots<256, T>(dev, sms) : 0;
+      if (slots > 0) {
+        const int bn = pick_pair_bn(p.M, p.N, slots);
+        return bn == 256 ? launch_umma2<256, T>(p, dev, slots) : launch_umma2<128, T>(p, dev, slots);
+      }
       const int bn = pick_bn(p.M, p.N, sms);
       return bn == 256 ? launch_umma<256, T>(p, dev, sms) : launch_umma<128, T>(p, dev, sms);
     }
@@ -382,11 +497,11 @@ int run(const Problem& p, int kernel) {
   if ((rc = device_sms(dev, &sms))) return rc;
 
   int variant = kernel == DX_KERNEL_AUTO ? select_variant(p, sms, true) : kernel;
-  if (variant == DX_KERNEL_UMMA || variant == DX_KERNEL_DECODE) {
+  if (variant == DX_KERNEL_UMMA || variant == DX_KERNEL_UMMA_1CTA || variant == DX_KERNEL_DECODE) {
     if (!load_encode_fn())
       return fail(DX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
   }
-  if (variant == DX_KERNEL_UMMA && !umma_eligible(p))
+  if ((variant == DX_KERNEL_UMMA || variant == DX_KERNEL_UMMA_1CTA) && !umma_eligible(p))
     return fail(DX_ERR_UNSUPPORTED,
                 "tcgen05 kernel needs fp16/bf16, K > 0, 16-byte-aligned pointers and row "
                 "pitches that are multiples of 16 bytes");
@@ -437,7 +552,8 @@ int dx_fused_linear(const void* X, const void* W, const void* bias, const void* 
 size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K, int dtype, int kernel) {
   t_last_error.clear();
   if (M <= 0 || N <= 0 || K <= 0 || dtype == DX_DTYPE_F32) return 0;
-  if (kernel == DX_KERNEL_UMMA || kernel == DX_KERNEL_SIMT) return 0;
+  if (kernel == DX_KERNEL_UMMA || kernel == DX_KERNEL_SIMT || kernel == DX_KERNEL_UMMA_1CTA)
+    return 0;
   if (M > kDecodeMaxM) return 0;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || device_sms(dev, &sms) != DX_OK) return 0;
@@ -452,6 +568,8 @@ int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype) {
 }
 
 const char* dx_last_error_string(void) { return t_last_error.c_str(); }
+
+const char* dx_last_launch_plan(void) { return t_last_plan.c_str(); }
 
 int dx_device_status(void* stream, int* status) {
   t_last_error.clear();

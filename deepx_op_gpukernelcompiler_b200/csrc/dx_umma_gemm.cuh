@@ -1,23 +1,35 @@
-// dx_umma_gemm.cuh — persistent tcgen05 GEMM with the fused linear epilogue:
+// dx_umma_gemm.cuh — persistent tcgen05 GEMMs with the fused linear epilogue:
 //   Y[M,N] = act(X[M,K] @ W[K,N] + bias[N]) (+ R[M,N]),  fp16/bf16 in and out,
 //   fp32 accumulation in TMEM.
 //
 // This replaces the reference's per-tile K loop + epilogue
-// (kernel_triton.py:47-67, kernel_tilelang.py:36-53) with a B200 design:
-//   * one CTA per SM, looping over 128 x BN output tiles (static schedule,
-//     M-fastest inside groups of `group_m` m-tiles so a panel of X stays in
-//     L2 while all of W streams past it);
-//   * warp 0: TMA producer.  X tiles [128 x 64] (K-major) and W tiles
-//     [64 x BN] (N-major, i.e. W exactly as it sits in memory) land in a
-//     STAGES-deep ring of 128-byte-swizzled shared-memory buffers;
-//   * warp 1: TMEM allocator and the single thread that issues
-//     tcgen05.mma (M=128, N=BN, K=16) into one of two TMEM accumulators;
-//   * warps 2-5: epilogue.  Each warp owns the 32 TMEM lanes (= tile rows) it
-//     may address, pulls 32 columns at a time with tcgen05.ld, adds bias,
-//     applies the activation, adds the residual (TMA-loaded into the same
-//     staging buffer), converts and TMA-stores.  The output tile crosses HBM
-//     exactly once; the next tile's main loop runs in the other accumulator
-//     meanwhile.
+// (kernel_triton.py:47-67, kernel_tilelang.py:36-53) with a B200 design.
+// Two kernels share one structure:
+//
+//   umma2_fused_linear_kernel  (main path) — CTA pairs (clusters of 2, one
+//     CTA per SM).  A pair owns a 256 x BN output tile: each CTA loads its own
+//     128 rows of X and its own BN/2 columns of W, and the leader CTA issues
+//     tcgen05.mma.cta_group::2 (M = 256, N = BN, K = 16), which reads A from
+//     both CTAs and B from both CTAs and writes each CTA's 128 rows into that
+//     CTA's TMEM.  Per SM this halves the W bytes that must be staged in
+//     shared memory per MMA compared with a single-CTA 128 x BN tile.
+//   umma_fused_linear_kernel   (M < 256) — single CTA, 128 x BN tiles.
+//
+// Roles inside a CTA (192 threads):
+//   warp 0   TMA producer: X tiles [128 x 64] (K-major) and W tiles
+//            [64 x 64] boxes (N-major, W exactly as it lies in memory) into
+//            a STAGES-deep ring of 128-byte-swizzled buffers;
+//   warp 1   TMEM allocator; its lane 0 (in the leader CTA for pairs) issues
+//            the MMAs into one of two TMEM accumulators (double buffer);
+//   warps 2-5 epilogue: each warp owns the 32 TMEM lanes (= tile rows) it may
+//            address, pulls 32 fp32 columns at a time with tcgen05.ld, adds
+//            bias, applies the activation, adds the residual (TMA-loaded into
+//            the staging buffer), converts, and TMA-stores.  The output tile
+//            crosses HBM exactly once; the next tile's main loop runs in the
+//            other accumulator meanwhile.
+// Tiles are visited M-fastest inside groups of `group_m` m-tiles, so a band
+// of X stays in L2 while all of W streams past it; Y and R are streamed with
+// an evict-first L2 policy.
 // Every mbarrier wait is bounded (dx_ptx.cuh); a timed-out CTA drains its
 // copies in flight, frees TMEM and exits with the device status bit set.
 #pragma once
@@ -29,43 +41,11 @@ namespace dx {
 
 struct UmmaParams {
   int M, N, K;
-  int m_tiles, n_tiles, k_blocks, num_tiles;
-  int group_m;       // m-tiles per raster group
-  const void* bias;  // N elements, or nullptr
+  int m_tiles, n_tiles, k_blocks, num_tiles;  // tiles of (rows per tile) x BN
+  int group_m;                                // m-tiles per raster group
+  const void* bias;                           // N elements, or nullptr
   int act;
   int has_residual;
-};
-
-template <int BN>
-struct UmmaShape {
-  static constexpr int BM = 128;
-  static constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
-  static constexpr int A_BYTES = BM * BK * 2;
-  static constexpr int B_BYTES = BK * BN * 2;
-  static constexpr int B_BOX_BYTES = BK * 64 * 2;  // one [64 k x 64 n] TMA box
-  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN == 256) ? 4 : 6;
-  static constexpr int EPI_WARPS = 4;
-  static constexpr int EPI_BUF_BYTES = 32 * 32 * 2;  // [32 rows x 32 cols] 16-bit
-  static constexpr int TMEM_COLS = 2 * BN;           // two fp32 accumulators
-  static constexpr int THREADS = 64 + 32 * EPI_WARPS;
-  static constexpr int OFF_A = 0;
-  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
-  static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
-  static constexpr int OFF_BAR = OFF_EPI + EPI_WARPS * 2 * EPI_BUF_BYTES;
-  // full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2],
-  // residual[EPI_WARPS][2], drain
-  static constexpr int BAR_FULL = 0;
-  static constexpr int BAR_EMPTY = STAGES;
-  static constexpr int BAR_TFULL = 2 * STAGES;
-  static constexpr int BAR_TEMPTY = 2 * STAGES + 2;
-  static constexpr int BAR_RES = 2 * STAGES + 4;
-  static constexpr int BAR_DRAIN = BAR_RES + 2 * EPI_WARPS;
-  static constexpr int NUM_BARS = BAR_DRAIN + 1;
-  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // tmem base, abort flag
-  static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 16;
-  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
-  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N");
 };
 
 __device__ __forceinline__ void umma_tile_coords(const UmmaParams& p, int t, int& mb, int& nb) {
@@ -77,6 +57,169 @@ __device__ __forceinline__ void umma_tile_coords(const UmmaParams& p, int t, int
   mb = m_first + r % gm;
   nb = r / gm;
 }
+
+constexpr int kEpiWarps = 4;
+constexpr int kEpiBufBytes = 32 * 32 * 2;  // [32 rows x 32 cols] of 16-bit
+
+// What one epilogue warp needs to finish accumulators.
+template <typename T>
+struct EpilogueCtx {
+  const CUtensorMap* tmY;
+  const CUtensorMap* tmR;
+  const T* bias;
+  bool bias_vec_ok;
+  int M, N, act, has_residual;
+  uint32_t ebuf0;      // this warp's two staging buffers (shared address)
+  uint8_t* ebuf_ptr0;  // same, generic pointer
+  uint32_t rbar0;      // this warp's two residual-load barriers (8 B apart)
+  uint64_t pol_stream; // evict-first policy for Y stores and R loads
+};
+
+// Drains one 128 x BN accumulator: this warp handles TMEM lanes
+// [32q, 32q+32), i.e. global rows row0 + 32q + lane, columns n0 .. n0+BN.
+// `release()` is called (lane 0, after the last TMEM read) to hand the
+// accumulator back to the MMA issuer.  `it` counts staging-buffer uses.
+// Returns false if a bounded wait gave up.
+template <int BN, typename T, typename Release>
+__device__ __forceinline__ bool epilogue_tile(const EpilogueCtx<T>& c, uint32_t tmem_acc, int q,
+                                              int lane, int row0, int n0, uint32_t& it,
+                                              volatile int* abort_flag, Release release) {
+  using Tr = ElemTraits<T>;
+  const uint32_t row_off = static_cast<uint32_t>(lane) * 64u;
+  const uint32_t row_sw = (static_cast<uint32_t>(lane) >> 1) & 3u;  // 64-byte swizzle phase
+  const int row_base = row0 + q * 32;
+  const bool rows_live = row_base < c.M;
+#pragma unroll 1
+  for (int ch = 0; ch < BN / 32; ++ch) {
+    const int n_c = n0 + 32 * ch;
+    const bool live = rows_live && n_c < c.N;  // warp-uniform
+    if (!live) {
+      if (ch == BN / 32 - 1) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) release();
+      }
+      continue;
+    }
+    const int buf = it & 1;
+    const uint32_t ebuf = c.ebuf0 + buf * kEpiBufBytes;
+    uint8_t* const ebp = c.ebuf_ptr0 + buf * kEpiBufBytes;
+    const uint32_t rbar = c.rbar0 + 8u * buf;
+    // The store issued two chunks ago from this buffer must have read it.
+    if (lane == 0) bulk_wait_group_read<1>();
+    __syncwarp();
+    if (c.has_residual && lane == 0) {
+      mbar_arrive_expect_tx(rbar, kEpiBufBytes);
+      tma_load_2d_hint(c.tmR, ebuf, rbar, n_c, row_base, c.pol_stream);
+    }
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(tmem_acc + static_cast<uint32_t>(32 * ch) +
+                           (static_cast<uint32_t>(q * 32) << 16),
+                       r);
+    tmem_wait_ld();
+    if (ch == BN / 32 - 1) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) release();
+    }
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    if (c.bias != nullptr) {
+      if (c.bias_vec_ok && n_c + 32 <= c.N) {
+        const uint4* bp = reinterpret_cast<const uint4*>(c.bias + n_c);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint4 w = __ldg(bp + j);
+          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int h = 0; h < 4; ++h) {
+            const float2 f = Tr::unpack2(wv[h]);
+            v[8 * j + 2 * h] += f.x;
+            v[8 * j + 2 * h + 1] += f.y;
+          }
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j)
+          if (n_c + j < c.N) v[j] += Tr::to_float(c.bias[n_c + j]);
+      }
+    }
+    if (c.act != kActNone) {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = act_apply(v[j], c.act);
+    }
+    if (c.has_residual) {
+      const uint32_t par = (it >> 1) & 1u;
+      if (!mbar_wait(rbar, par, abort_flag)) {
+        mbar_wait_drain(rbar, par);  // the load still lands in this buffer
+        return false;
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 w = *reinterpret_cast<const uint4*>(
+            ebp + row_off + ((static_cast<uint32_t>(j) ^ row_sw) << 4));
+        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 f = Tr::unpack2(wv[h]);
+          v[8 * j + 2 * h] += f.x;
+          v[8 * j + 2 * h + 1] += f.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      uint4 w;
+      w.x = Tr::pack2(v[8 * j + 0], v[8 * j + 1]);
+      w.y = Tr::pack2(v[8 * j + 2], v[8 * j + 3]);
+      w.z = Tr::pack2(v[8 * j + 4], v[8 * j + 5]);
+      w.w = Tr::pack2(v[8 * j + 6], v[8 * j + 7]);
+      *reinterpret_cast<uint4*>(ebp + row_off + ((static_cast<uint32_t>(j) ^ row_sw) << 4)) = w;
+    }
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d_hint(c.tmY, ebuf, n_c, row_base, c.pol_stream);
+      bulk_commit_group();
+    }
+    ++it;
+  }
+  return true;
+}
+
+// =====================================================================
+// Single-CTA kernel: 128 x BN tiles.
+// =====================================================================
+template <int BN>
+struct UmmaShape {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;  // 64 x 16-bit = one 128-byte swizzle row
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BK * BN * 2;
+  static constexpr int B_BOX_BYTES = BK * 64 * 2;  // one [64 k x 64 n] TMA box
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN == 256) ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;  // two fp32 accumulators
+  static constexpr int THREADS = 64 + 32 * kEpiWarps;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_BAR = OFF_EPI + kEpiWarps * 2 * kEpiBufBytes;
+  // full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2],
+  // residual[kEpiWarps][2], drain
+  static constexpr int BAR_FULL = 0;
+  static constexpr int BAR_EMPTY = STAGES;
+  static constexpr int BAR_TFULL = 2 * STAGES;
+  static constexpr int BAR_TEMPTY = 2 * STAGES + 2;
+  static constexpr int BAR_RES = 2 * STAGES + 4;
+  static constexpr int BAR_DRAIN = BAR_RES + 2 * kEpiWarps;
+  static constexpr int NUM_BARS = BAR_DRAIN + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // tmem base, abort flag
+  static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 16;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N");
+};
 
 template <int BN, typename T>
 __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
@@ -108,9 +251,9 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(bar(S::BAR_TFULL + b), 1);
-      mbar_init(bar(S::BAR_TEMPTY + b), S::EPI_WARPS);
+      mbar_init(bar(S::BAR_TEMPTY + b), kEpiWarps);
     }
-    for (int i = 0; i < 2 * S::EPI_WARPS; ++i) mbar_init(bar(S::BAR_RES + i), 1);
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(bar(S::BAR_RES + i), 1);
     mbar_init(bar(S::BAR_DRAIN), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -133,6 +276,7 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
+      const uint64_t pol = make_l2_policy_evict_normal();
       int s = 0;
       uint32_t ph = 0, issued = 0;
       bool ok = true;
@@ -147,11 +291,11 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
           }
           const uint32_t fb = bar(S::BAR_FULL + s);
           mbar_arrive_expect_tx(fb, S::STAGE_BYTES);
-          tma_load_2d(&tmA, sA + s * S::A_BYTES, fb, kb * S::BK, m0);
+          tma_load_2d_hint(&tmA, sA + s * S::A_BYTES, fb, kb * S::BK, m0, pol);
 #pragma unroll
           for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d(&tmB, sB + s * S::B_BYTES + j * S::B_BOX_BYTES, fb, n0 + 64 * j,
-                        kb * S::BK);
+            tma_load_2d_hint(&tmB, sB + s * S::B_BYTES + j * S::B_BOX_BYTES, fb, n0 + 64 * j,
+                             kb * S::BK, pol);
           ++issued;
           if (++s == S::STAGES) {
             s = 0;
@@ -210,110 +354,33 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
     // --------------------------------------------------------- epilogue
     const int e = warp - 2;  // epilogue warp index 0..3
     const int q = warp & 3;  // TMEM lane quarter this warp may address
-    const T* const bias = static_cast<const T*>(p.bias);
-    const bool bias_vec_ok = bias != nullptr && (reinterpret_cast<uintptr_t>(bias) & 15u) == 0;
-    const uint32_t ebuf0 = base + S::OFF_EPI + e * 2 * S::EPI_BUF_BYTES;
-    uint8_t* const ebuf_ptr0 = base_ptr + S::OFF_EPI + e * 2 * S::EPI_BUF_BYTES;
-    const uint32_t row_off = static_cast<uint32_t>(lane) * 64u;
-    const uint32_t row_sw = (static_cast<uint32_t>(lane) >> 1) & 3u;  // 64-byte swizzle phase
+    EpilogueCtx<T> c;
+    c.tmY = &tmY;
+    c.tmR = &tmR;
+    c.bias = static_cast<const T*>(p.bias);
+    c.bias_vec_ok = c.bias != nullptr && (reinterpret_cast<uintptr_t>(c.bias) & 15u) == 0;
+    c.M = p.M;
+    c.N = p.N;
+    c.act = p.act;
+    c.has_residual = p.has_residual;
+    c.ebuf0 = base + S::OFF_EPI + e * 2 * kEpiBufBytes;
+    c.ebuf_ptr0 = base_ptr + S::OFF_EPI + e * 2 * kEpiBufBytes;
+    c.rbar0 = bar(S::BAR_RES + e * 2);
+    c.pol_stream = make_l2_policy_evict_first();
     uint32_t it = 0;
     int local = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x, ++local) {
+    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
       const int b = local & 1;
       const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
       if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
       tc_fence_after();
       int mb, nb;
       umma_tile_coords(p, t, mb, nb);
-      const int m0 = mb * S::BM, n0 = nb * BN;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c, ++it) {
-        const int buf = it & 1;
-        const uint32_t ebuf = ebuf0 + buf * S::EPI_BUF_BYTES;
-        uint8_t* const ebp = ebuf_ptr0 + buf * S::EPI_BUF_BYTES;
-        const int n_c = n0 + 32 * c;
-        // The store issued two chunks ago from this buffer must have read it.
-        if (lane == 0) bulk_wait_group_read<1>();
-        __syncwarp();
-        const uint32_t rbar = bar(S::BAR_RES + e * 2 + buf);
-        if (p.has_residual && lane == 0) {
-          mbar_arrive_expect_tx(rbar, S::EPI_BUF_BYTES);
-          tma_load_2d(&tmR, ebuf, rbar, n_c, m0 + q * 32);
-        }
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(tmem_base + static_cast<uint32_t>(b * BN + 32 * c) +
-                               (static_cast<uint32_t>(q * 32) << 16),
-                           r);
-        tmem_wait_ld();
-        if (c == BN / 32 - 1) {
-          // Accumulator fully read: hand it back to the MMA warp.
-          tc_fence_before();
-          __syncwarp();
-          if (lane == 0) mbar_arrive(bar(S::BAR_TEMPTY + b));
-        }
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-        if (bias != nullptr) {
-          if (bias_vec_ok && n_c + 32 <= p.N) {
-            const uint4* bp = reinterpret_cast<const uint4*>(bias + n_c);
-#pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              const uint4 w = __ldg(bp + j);
-              const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-              for (int h = 0; h < 4; ++h) {
-                const float2 f = Tr::unpack2(wv[h]);
-                v[8 * j + 2 * h] += f.x;
-                v[8 * j + 2 * h + 1] += f.y;
-              }
-            }
-          } else {
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (n_c + j < p.N) v[j] += Tr::to_float(bias[n_c + j]);
-          }
-        }
-        if (p.act != kActNone) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = act_apply(v[j], p.act);
-        }
-        if (p.has_residual) {
-          if (!mbar_wait(rbar, (it >> 1) & 1u, abort_flag)) {
-            mbar_wait_drain(rbar, (it >> 1) & 1u);  // the load still lands here
-            ok = false;
-            break;
-          }
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const uint4 w =
-                *reinterpret_cast<const uint4*>(ebp + row_off + ((static_cast<uint32_t>(j) ^ row_sw) << 4));
-            const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int h = 0; h < 4; ++h) {
-              const float2 f = Tr::unpack2(wv[h]);
-              v[8 * j + 2 * h] += f.x;
-              v[8 * j + 2 * h + 1] += f.y;
-            }
-          }
-        }
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          uint4 w;
-          w.x = Tr::pack2(v[8 * j + 0], v[8 * j + 1]);
-          w.y = Tr::pack2(v[8 * j + 2], v[8 * j + 3]);
-          w.z = Tr::pack2(v[8 * j + 4], v[8 * j + 5]);
-          w.w = Tr::pack2(v[8 * j + 6], v[8 * j + 7]);
-          *reinterpret_cast<uint4*>(ebp + row_off + ((static_cast<uint32_t>(j) ^ row_sw) << 4)) = w;
-        }
-        fence_proxy_async_smem();
-        __syncwarp();
-        if (lane == 0) {
-          tma_store_2d(&tmY, ebuf, n_c, m0 + q * 32);
-          bulk_commit_group();
-        }
-      }
+      const uint32_t tempty = bar(S::BAR_TEMPTY + b);
+      if (!epilogue_tile<BN, T>(c, tmem_base + static_cast<uint32_t>(b * BN), q, lane,
+                                mb * S::BM, nb * BN, it, abort_flag,
+                                [tempty] { mbar_arrive(tempty); }))
+        break;
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
@@ -324,6 +391,223 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, S::TMEM_COLS);
+  }
+}
+
+// =====================================================================
+// CTA-pair kernel: 256 x BN tiles, tcgen05.mma.cta_group::2.
+// =====================================================================
+template <int BN>
+struct Umma2Shape {
+  static constexpr int BM = 128;      // rows per CTA (256 per pair)
+  static constexpr int BK = 64;
+  static constexpr int BN_CTA = BN / 2;  // W columns staged by each CTA
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BOX_BYTES = BK * 64 * 2;
+  static constexpr int B_BYTES = BK * BN_CTA * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // per CTA
+  static constexpr int STAGES = (BN == 256) ? 6 : 8;
+  static constexpr int TMEM_COLS = 2 * BN;  // per CTA: two accumulators of BN fp32 columns
+  static constexpr int THREADS = 64 + 32 * kEpiWarps;
+  static constexpr int OFF_A = 0;
+  static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
+  static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
+  static constexpr int OFF_BAR = OFF_EPI + kEpiWarps * 2 * kEpiBufBytes;
+  static constexpr int BAR_FULL = 0;              // leader only: both CTAs' bytes
+  static constexpr int BAR_EMPTY = STAGES;        // both CTAs
+  static constexpr int BAR_TFULL = 2 * STAGES;    // both CTAs
+  static constexpr int BAR_TEMPTY = 2 * STAGES + 2;  // leader only: 8 warp arrivals
+  static constexpr int BAR_RES = 2 * STAGES + 4;
+  static constexpr int BAR_DRAIN = BAR_RES + 2 * kEpiWarps;
+  static constexpr int NUM_BARS = BAR_DRAIN + 1;
+  static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
+  static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 16;
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(BN == 128 || BN == 256, "pair tile N");
+};
+
+template <int BN, typename T>
+__global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
+    umma2_fused_linear_kernel(const __grid_constant__ CUtensorMap tmA,
+                              const __grid_constant__ CUtensorMap tmB,
+                              const __grid_constant__ CUtensorMap tmY,
+                              const __grid_constant__ CUtensorMap tmR, const UmmaParams p) {
+  using S = Umma2Shape<BN>;
+  using Tr = ElemTraits<T>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw_u32 = smem_u32(smem_raw);
+  const uint32_t base = (raw_u32 + 1023u) & ~1023u;
+  uint8_t* const base_ptr = smem_raw + (base - raw_u32);
+
+  const uint32_t sA = base + S::OFF_A;
+  const uint32_t sB = base + S::OFF_B;
+  const uint32_t bars = base + S::OFF_BAR;
+  uint32_t* const tmem_word = reinterpret_cast<uint32_t*>(base_ptr + S::OFF_MISC);
+  volatile int* const abort_flag = reinterpret_cast<volatile int*>(base_ptr + S::OFF_MISC + 4);
+  auto bar = [bars](int i) { return bars + 8u * static_cast<uint32_t>(i); };
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader of the pair
+  const bool leader = rank == 0;
+  const int pair = static_cast<int>(blockIdx.x >> 1);
+  const int npairs = static_cast<int>(gridDim.x >> 1);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S::STAGES; ++s) {
+      mbar_init(bar(S::BAR_FULL + s), 1);
+      mbar_init(bar(S::BAR_EMPTY + s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(bar(S::BAR_TFULL + b), 1);
+      mbar_init(bar(S::BAR_TEMPTY + b), 2 * kEpiWarps);
+    }
+    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(bar(S::BAR_RES + i), 1);
+    mbar_init(bar(S::BAR_DRAIN), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+    tma_prefetch_desc(&tmY);
+    if (p.has_residual) tma_prefetch_desc(&tmR);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_word), S::TMEM_COLS);
+    tmem_relinquish_pair();
+  }
+  // Both CTAs' barriers exist and TMEM is allocated before anyone signals
+  // across the pair.
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_word;
+
+  if (warp == 0) {
+    // ------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      const uint64_t pol = make_l2_policy_evict_normal();
+      int s = 0;
+      uint32_t ph = 0, issued = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < p.num_tiles; t += npairs) {
+        int mb, nb;
+        umma_tile_coords(p, t, mb, nb);
+        const int m0 = mb * 2 * S::BM + static_cast<int>(rank) * S::BM;
+        const int n0 = nb * BN + static_cast<int>(rank) * S::BN_CTA;
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(bar(S::BAR_EMPTY + s), ph ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          // The leader's full barrier counts both CTAs' bytes.
+          if (leader) mbar_arrive_expect_tx(bar(S::BAR_FULL + s), 2 * S::STAGE_BYTES);
+          const uint32_t fb = mapa_shared(bar(S::BAR_FULL + s), 0);
+          tma_load_2d_pair(&tmA, sA + s * S::A_BYTES, fb, kb * S::BK, m0, pol);
+#pragma unroll
+          for (int j = 0; j < S::BN_CTA / 64; ++j)
+            tma_load_2d_pair(&tmB, sB + s * S::B_BYTES + j * S::B_BOX_BYTES, fb, n0 + 64 * j,
+                             kb * S::BK, pol);
+          ++issued;
+          if (++s == S::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+      }
+      // The leader observes both CTAs' copies through its full barriers.
+      if (leader) {
+        const uint32_t n_drain = issued < (uint32_t)S::STAGES ? issued : (uint32_t)S::STAGES;
+        for (uint32_t i = issued - n_drain; i < issued; ++i)
+          mbar_wait_drain(bar(S::BAR_FULL + (int)(i % S::STAGES)), (i / S::STAGES) & 1u);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ----------------------------------------------- MMA issuer (leader)
+    if (leader && lane == 0) {
+      constexpr uint32_t idesc = umma_idesc_f16(Tr::kIsBf16, 256, BN, false, true);
+      int s = 0, local = 0;
+      uint32_t ph = 0;
+      bool ok = true;
+      for (int t = pair; ok && t < p.num_tiles; t += npairs, ++local) {
+        const int b = local & 1;
+        const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
+        if (!mbar_wait(bar(S::BAR_TEMPTY + b), use_ph ^ 1u, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BN);
+        for (int kb = 0; kb < p.k_blocks; ++kb) {
+          if (!mbar_wait(bar(S::BAR_FULL + s), ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t ad = smem_desc_sw128(sA + s * S::A_BYTES, 16, 1024);
+          const uint64_t bd = smem_desc_sw128(sB + s * S::B_BYTES, S::B_BOX_BYTES, 1024);
+#pragma unroll
+          for (int k = 0; k < S::BK / 16; ++k)
+            umma_f16_pair(d_tmem, ad + 2ull * k, bd + 128ull * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          // Stage s is free in both CTAs once these MMAs have read it.
+          umma_commit_pair(mapa_shared(bar(S::BAR_EMPTY + s), 0));
+          umma_commit_pair(mapa_shared(bar(S::BAR_EMPTY + s), 1));
+          if (++s == S::STAGES) {
+            s = 0;
+            ph ^= 1u;
+          }
+        }
+        if (ok) {
+          umma_commit_pair(mapa_shared(bar(S::BAR_TFULL + b), 0));
+          umma_commit_pair(mapa_shared(bar(S::BAR_TFULL + b), 1));
+        }
+      }
+      umma_commit_pair(mapa_shared(bar(S::BAR_DRAIN), 0));
+      mbar_wait_drain(bar(S::BAR_DRAIN), 0);
+    }
+    __syncwarp();
+  } else {
+    // --------------------------------------------- epilogue (both CTAs)
+    const int e = warp - 2;
+    const int q = warp & 3;
+    EpilogueCtx<T> c;
+    c.tmY = &tmY;
+    c.tmR = &tmR;
+    c.bias = static_cast<const T*>(p.bias);
+    c.bias_vec_ok = c.bias != nullptr && (reinterpret_cast<uintptr_t>(c.bias) & 15u) == 0;
+    c.M = p.M;
+    c.N = p.N;
+    c.act = p.act;
+    c.has_residual = p.has_residual;
+    c.ebuf0 = base + S::OFF_EPI + e * 2 * kEpiBufBytes;
+    c.ebuf_ptr0 = base_ptr + S::OFF_EPI + e * 2 * kEpiBufBytes;
+    c.rbar0 = bar(S::BAR_RES + e * 2);
+    c.pol_stream = make_l2_policy_evict_first();
+    uint32_t it = 0;
+    int local = 0;
+    for (int t = pair; t < p.num_tiles; t += npairs, ++local) {
+      const int b = local & 1;
+      const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
+      if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
+      tc_fence_after();
+      int mb, nb;
+      umma_tile_coords(p, t, mb, nb);
+      const uint32_t tempty_leader = mapa_shared(bar(S::BAR_TEMPTY + b), 0);
+      if (!epilogue_tile<BN, T>(c, tmem_base + static_cast<uint32_t>(b * BN), q, lane,
+                                mb * 2 * S::BM + static_cast<int>(rank) * S::BM, nb * BN, it,
+                                abort_flag,
+                                [tempty_leader] { mbar_arrive_cluster(tempty_leader); }))
+        break;
+    }
+    if (lane == 0) bulk_wait_group<0>();
+    __syncwarp();
+  }
+
+  // No CTA of the pair leaves while the other may still signal it.
+  tc_fence_before();
+  cluster_sync();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, S::TMEM_COLS);
   }
 }
 

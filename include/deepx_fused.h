@@ -64,9 +64,11 @@ extern "C" {
 
 /* ---- kernel variants --------------------------------------------------- */
 #define DX_KERNEL_AUTO    0  /* pick by shape, dtype and alignment           */
-#define DX_KERNEL_UMMA    1  /* persistent tcgen05 + TMEM + TMA GEMM         */
+#define DX_KERNEL_UMMA    1  /* persistent tcgen05 + TMEM + TMA GEMM (CTA
+                                pairs with cta_group::2 when M >= 256)      */
 #define DX_KERNEL_DECODE  2  /* swap-AB split-K tcgen05 kernel, M <= 64      */
 #define DX_KERNEL_SIMT    3  /* CUDA-core FFMA kernel (fp32, odd strides)    */
+#define DX_KERNEL_UMMA_1CTA 4 /* the tcgen05 GEMM with single-CTA tiles only */
 
 /* Device status bits reported by dx_device_status. */
 #define DX_DEVICE_STATUS_TIMEOUT  1
@@ -111,6 +113,10 @@ int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype);
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* dx_last_error_string(void);
+
+/* Description of the kernel launch made by the last successful call on this
+ * thread: variant, tile shape, pipeline depth, grid ("" if none). */
+const char* dx_last_launch_plan(void);
 
 /* Synchronises `stream`, then reads and clears the calling device's status
  * word (DX_DEVICE_STATUS_* bits) into *status. */

@@ -24,7 +24,7 @@ DEV = torch.device("cuda:0")
 def _variants(case):
     if case["dtype"] == "f32":
         return ["auto", "simt"]
-    out = ["auto", "simt", "umma"]
+    out = ["auto", "simt", "umma", "umma_1cta"]
     if case["M"] <= 64:
         out.append("decode")
     return out
@@ -87,7 +87,7 @@ def test_shapes_all_variants(M, K, N, dtype):
     X, W, b, _ = _rand(M, K, N, dtype, seed=M * 7 + K * 3 + N)
     ref = oracle.fused_linear_f64(X, W, b, "gelu_erf")
     Xd, Wd, bd = X.to(DEV), W.to(DEV), b.to(DEV)
-    variants = ["auto", "umma", "simt"] + (["decode"] if M <= 64 else [])
+    variants = ["auto", "umma", "umma_1cta", "simt"] + (["decode"] if M <= 64 else [])
     for kern in variants:
         Y = fused_linear(Xd, Wd, bd, "gelu_erf", kernel=kern)
         torch.cuda.synchronize()
@@ -96,9 +96,9 @@ def test_shapes_all_variants(M, K, N, dtype):
 
 
 @pytest.mark.parametrize("act", [None, "relu", "gelu", "gelu_erf", "silu", "swish"])
-@pytest.mark.parametrize("kern", ["umma", "decode"])
+@pytest.mark.parametrize("kern", ["umma", "umma_1cta", "decode"])
 def test_activations_with_residual(act, kern):
-    M = 48 if kern == "decode" else 200
+    M = 48 if kern == "decode" else 600
     X, W, b, R = _rand(M, 256, 320, torch.bfloat16, seed=11, residual=True)
     ref = oracle.fused_linear_f64(X, W, b, act, residual=R)
     Y = fused_linear(X.to(DEV), W.to(DEV), b.to(DEV), act, residual=R.to(DEV), kernel=kern)
@@ -106,7 +106,7 @@ def test_activations_with_residual(act, kern):
     _assert_close(Y, ref, torch.bfloat16, f"{act} residual [{kern}]")
 
 
-@pytest.mark.parametrize("kern", ["umma", "decode", "simt"])
+@pytest.mark.parametrize("kern", ["umma", "umma_1cta", "decode", "simt"])
 def test_no_bias(kern):
     X, W, _, _ = _rand(32, 128, 256, torch.float16, seed=5)
     ref = oracle.fused_linear_f64(X, W, None, "relu")
@@ -115,10 +115,11 @@ def test_no_bias(kern):
     _assert_close(Y, ref, torch.float16, f"no bias [{kern}]")
 
 
-@pytest.mark.parametrize("kern", ["umma", "decode", "simt"])
-def test_strided_views(kern):
+@pytest.mark.parametrize("kern,M", [("umma", 300), ("umma_1cta", 40), ("decode", 40),
+                                    ("simt", 40)])
+def test_strided_views(kern, M):
     """Row pitches larger than the row length (column slices of wider buffers)."""
-    M, K, N = 40, 192, 256
+    K, N = 192, 256
     X, W, b, R = _rand(M, K, N, torch.bfloat16, seed=9, residual=True)
     Xb = torch.zeros(M, K + 64, dtype=X.dtype)
     Xb[:, 32:32 + K] = X
@@ -182,7 +183,7 @@ def test_decode_without_workspace_is_rejected():
     _assert_close(Y, oracle.fused_linear_f64(X, W, b, None), torch.float16, "auto w/o workspace")
 
 
-@pytest.mark.parametrize("kern,M", [("umma", 1000), ("decode", 16)])
+@pytest.mark.parametrize("kern,M", [("umma", 1000), ("umma_1cta", 1000), ("decode", 16)])
 def test_bitwise_deterministic(kern, M):
     X, W, b, _ = _rand(M, 2048, 1536, torch.bfloat16, seed=21)
     Xd, Wd, bd = X.to(DEV), W.to(DEV), b.to(DEV)
@@ -210,3 +211,17 @@ def test_nonzero_stream():
         Y = fused_linear(X.to(DEV), W.to(DEV), b.to(DEV), "relu")
     s.synchronize()
     _assert_close(Y, oracle.fused_linear_f64(X, W, b, "relu"), torch.bfloat16, "side stream")
+
+
+@pytest.mark.parametrize("M,N", [(256, 128), (512, 512), (768, 1280), (1280, 384)])
+def test_pair_and_single_cta_agree(M, N):
+    """The CTA-pair and single-CTA tensor-core kernels accumulate in the same
+    k order, so they agree to the last bit."""
+    X, W, b, R = _rand(M, 1024, N, torch.bfloat16, seed=M + N, residual=True)
+    Xd, Wd, bd, Rd = X.to(DEV), W.to(DEV), b.to(DEV), R.to(DEV)
+    Y2 = fused_linear(Xd, Wd, bd, "gelu", residual=Rd, kernel="umma")
+    Y1 = fused_linear(Xd, Wd, bd, "gelu", residual=Rd, kernel="umma_1cta")
+    torch.cuda.synchronize()
+    _assert_close(Y2, oracle.fused_linear_f64(X, W, b, "gelu", residual=R), torch.bfloat16,
+                  f"pair {M}x{N}")
+    assert torch.equal(Y1, Y2)
