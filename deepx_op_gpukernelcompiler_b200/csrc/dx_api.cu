@@ -149,6 +149,11 @@ struct Problem {
 
 // ----------------------------------------------------------- decode plan
 constexpr int kDecodeMaxM = 64;
+// Tickets live in a fixed slab at the start of every decode workspace, so the
+// partial sums of one problem never overlap the tickets of another problem
+// that reuses the same workspace later; the kernel leaves the slab zeroed.
+constexpr size_t kTicketSlabBytes = size_t(64) << 10;
+constexpr int64_t kDecodeMaxTiles = static_cast<int64_t>(kTicketSlabBytes / (4 * sizeof(int)));
 
 int decode_mn(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
 
@@ -180,7 +185,7 @@ DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sms) {
     ms = std::max<int>(ms, static_cast<int>(l - f + 1));
   }
   d.max_seg = ms;
-  d.ticket_bytes = ((static_cast<size_t>(d.n_tiles) * 4 * sizeof(int)) + 255) & ~size_t(255);
+  d.ticket_bytes = kTicketSlabBytes;
   d.bytes = d.ticket_bytes +
             static_cast<size_t>(d.n_tiles) * d.max_seg * d.mn * 128 * sizeof(float);
   return d;
@@ -445,6 +450,7 @@ bool umma_eligible(const Problem& p) {
 
 bool decode_eligible(const Problem& p) {
   if (p.dtype == DX_DTYPE_F32 || p.K == 0 || p.M > kDecodeMaxM) return false;
+  if ((p.N + 127) / 128 > kDecodeMaxTiles) return false;
   return tma_ok(p.X, p.ldx) && tma_ok(p.W, p.ldw);
 }
 
@@ -508,9 +514,9 @@ int run(const Problem& p, int kernel) {
   if (variant == DX_KERNEL_DECODE) {
     if (!decode_eligible(p))
       return fail(DX_ERR_UNSUPPORTED,
-                  "decode kernel needs fp16/bf16, 0 < K, M <= %d, and 16-byte-aligned X/W "
-                  "with row pitches that are multiples of 16 bytes",
-                  kDecodeMaxM);
+                  "decode kernel needs fp16/bf16, 0 < K, M <= %d, N <= %lld, and "
+                  "16-byte-aligned X/W with row pitches that are multiples of 16 bytes",
+                  kDecodeMaxM, (long long)(kDecodeMaxTiles * 128));
     const DecodePlan d = decode_plan(p.M, p.N, p.K, sms);
     if (p.ws == nullptr || p.ws_bytes < d.bytes || !aligned16(p.ws))
       return fail(DX_ERR_WORKSPACE, "decode kernel needs a 16-byte-aligned workspace of %zu bytes",
@@ -554,7 +560,7 @@ size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K, int dtype
   if (M <= 0 || N <= 0 || K <= 0 || dtype == DX_DTYPE_F32) return 0;
   if (kernel == DX_KERNEL_UMMA || kernel == DX_KERNEL_SIMT || kernel == DX_KERNEL_UMMA_1CTA)
     return 0;
-  if (M > kDecodeMaxM) return 0;
+  if (M > kDecodeMaxM || (N + 127) / 128 > kDecodeMaxTiles) return 0;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || device_sms(dev, &sms) != DX_OK) return 0;
   return decode_plan(M, N, K, sms).bytes;
@@ -563,7 +569,7 @@ size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K, int dtype
 int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype) {
   if (dtype == DX_DTYPE_F32 || K <= 0) return DX_KERNEL_SIMT;
   if ((K * 2) % 16 != 0 || (N * 2) % 16 != 0) return DX_KERNEL_SIMT;
-  if (M <= kDecodeMaxM) return DX_KERNEL_DECODE;
+  if (M <= kDecodeMaxM && (N + 127) / 128 <= kDecodeMaxTiles) return DX_KERNEL_DECODE;
   return DX_KERNEL_UMMA;
 }
 
@@ -591,3 +597,4 @@ int dx_device_status(void* stream, int* status) {
 int dx_version(void) { return 100; }
 
 }  // extern "C"
+

@@ -81,8 +81,10 @@ extern "C" {
  * (doc/kvlang-to-tilelang-interface.md:92) with the shape passed explicitly.
  * `workspace` may be NULL when dx_fused_linear_workspace_size() returns 0 for
  * the call; otherwise it must hold that many bytes, have been zero-filled
- * before its first use, and not be used by two calls at once (the kernels
- * leave it zero-filled again on success).
+ * before its first use, and not be used by two calls at once.  Its first
+ * 64 KiB hold split-K tickets that every successful call leaves at zero, so a
+ * workspace can be reused by later calls of any shape; after a call that
+ * reported DX_DEVICE_STATUS_TIMEOUT, zero it again.
  */
 int dx_fused_linear(const void* X, const void* W, const void* bias,
                     const void* R, void* Y,

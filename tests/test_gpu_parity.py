@@ -194,8 +194,11 @@ def test_bitwise_deterministic(kern, M):
 
 
 def test_decode_tickets_reset_across_shapes():
-    """The split-K workspace is reused across calls of different shapes."""
-    for (M, K, N) in [(16, 4096, 1024), (3, 640, 2048), (64, 8192, 256), (16, 4096, 1024)]:
+    """The split-K workspace is reused across calls of different shapes: the
+    partial sums of a narrow problem must not land on the tickets a wider
+    problem uses later (24 n-tiles, then 8, then 24 again)."""
+    for (M, K, N) in [(16, 4096, 3072), (16, 4096, 1024), (3, 640, 2048), (64, 8192, 256),
+                      (16, 8192, 3072), (16, 1024, 3072), (16, 4096, 1024)]:
         X, W, b, _ = _rand(M, K, N, torch.float16, seed=M + K + N)
         Y = fused_linear(X.to(DEV), W.to(DEV), b.to(DEV), "gelu_erf", kernel="decode")
         torch.cuda.synchronize()
