@@ -60,6 +60,7 @@ _LINEAR_ARGS = [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i64, _i6
 SIGNATURES = {
     "dx_fused_linear": (ctypes.c_int, _LINEAR_ARGS + [_vp, ctypes.c_size_t, _vp]),
     "dx_fused_linear_ex": (ctypes.c_int, _LINEAR_ARGS + [ctypes.c_int, _vp, ctypes.c_size_t, _vp]),
+    "dx_fused_linear_decode_noalloc": (ctypes.c_int, _LINEAR_ARGS + [_vp]),
     "dx_fused_linear_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, ctypes.c_int, ctypes.c_int]),
     "dx_select_kernel": (ctypes.c_int, [_i64, _i64, _i64, ctypes.c_int]),
     "dx_last_error_string": (ctypes.c_char_p, []),

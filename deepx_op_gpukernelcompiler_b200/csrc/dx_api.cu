@@ -598,3 +598,96 @@ int dx_version(void) { return 100; }
 
 }  // extern "C"
 
+// =========================================================================
+// Decode entry point that allocates nothing.
+//
+// The decode kernel needs split-K scratch (per-tile tickets and fp32 partial
+// sums).  dx_fused_linear takes it from the caller as a workspace; some
+// callers have none to give and may not allocate: a runtime that owns every
+// device buffer through its own heap manager and hands a kernel only raw
+// pointers and a stream (the `kernel_fn(x, W, b, out, stream)` shape of the
+// kvlang dispatcher) cannot call cudaMalloc behind its allocator's back.  For
+// them the scratch lives in one fixed device array inside this library,
+// kStaticScratchBytes large; every GPU that loads the library holds it until
+// the process exits.
+//
+// Set-up: the first call on a device resolves the array's device address
+// with cudaGetSymbolAddress while that device is current, and caches it.
+// Make that first call before any stream capture.
+// All calls on a device share the array and it keeps the last call's
+// contents; the tickets are cleared on the caller's stream at every call.
+// Calls that overlap on the GPU (different streams, or concurrent host
+// threads) race on the shared scratch — serialise them.
+// =========================================================================
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB per device
+static __device__ __align__(256) unsigned char g_static_decode_scratch[kStaticScratchBytes];
+
+std::mutex g_static_scratch_mu;
+std::map<int, void*> g_static_scratch_addr;
+
+// Device address of the static scratch on device `dev` (current device).
+int static_scratch_address(int dev, void** out) {
+  std::lock_guard<std::mutex> lk(g_static_scratch_mu);
+  auto it = g_static_scratch_addr.find(dev);
+  if (it != g_static_scratch_addr.end()) {
+    *out = it->second;
+    return DX_OK;
+  }
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_decode_scratch);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static decode scratch)");
+  if (ptr == nullptr) return fail(DX_ERR_CUDA, "static decode scratch has no device address");
+  g_static_scratch_addr[dev] = ptr;
+  *out = ptr;
+  return DX_OK;
+}
+
+}  // namespace
+
+extern "C" int dx_fused_linear_decode_noalloc(const void* X, const void* W, const void* bias,
+                                              const void* R, void* Y, int64_t M, int64_t N,
+                                              int64_t K, int64_t ldx, int64_t ldw, int64_t ldr,
+                                              int64_t ldy, int dtype, int act, void* stream) {
+  t_last_error.clear();
+  Problem p{X,   W,   bias, R,     Y,   M,       N, K, ldx, ldw, ldr, ldy,
+            dtype, act, nullptr, 0, static_cast<cudaStream_t>(stream)};
+  int rc = validate(p, DX_KERNEL_DECODE);
+  if (rc) return rc;
+  if (M == 0 || N == 0) return DX_OK;
+  if (!decode_eligible(p))
+    return fail(DX_ERR_UNSUPPORTED,
+                "dx_fused_linear_decode_noalloc needs fp16/bf16, 0 < K, M <= %d, and "
+                "16-byte-aligned X/W with row pitches that are multiples of 16 bytes",
+                kDecodeMaxM);
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  int sms = 0;
+  if ((rc = device_sms(dev, &sms))) return rc;
+  const DecodePlan d = decode_plan(M, N, K, sms);
+  if (d.bytes > kStaticScratchBytes)
+    return fail(DX_ERR_WORKSPACE,
+                "dx_fused_linear_decode_noalloc: this problem needs %zu bytes of split-K scratch "
+                "but the library's static scratch holds %zu; use dx_fused_linear with a workspace",
+                d.bytes, kStaticScratchBytes);
+  if (!load_encode_fn())
+    return fail(DX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  void* scratch = nullptr;
+  if ((rc = static_scratch_address(dev, &scratch))) return rc;
+  // The tickets must start at zero (an aborted earlier call may have left
+  // some set); the partial sums are always written before they are read.
+  e = cudaMemsetAsync(scratch, 0, d.ticket_bytes, p.stream);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(static decode scratch tickets)");
+  p.ws = scratch;
+  p.ws_bytes = kStaticScratchBytes;
+  if (dtype == DX_DTYPE_F16) {
+    if (d.mn == 16) return launch_decode<16, __half>(p, dev, sms, d);
+    if (d.mn == 32) return launch_decode<32, __half>(p, dev, sms, d);
+    return launch_decode<64, __half>(p, dev, sms, d);
+  }
+  if (d.mn == 16) return launch_decode<16, __nv_bfloat16>(p, dev, sms, d);
+  if (d.mn == 32) return launch_decode<32, __nv_bfloat16>(p, dev, sms, d);
+  return launch_decode<64, __nv_bfloat16>(p, dev, sms, d);
+}

@@ -104,6 +104,23 @@ int dx_fused_linear_ex(const void* X, const void* W, const void* bias,
                        void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/* Skinny-M (decode) fused linear that allocates nothing.  No counterpart in
+ * the reference: it exists for callers that cannot allocate device memory at
+ * call time — a runtime whose own heap manager owns every device buffer and
+ * hands kernels only raw pointers and a stream, so it has no workspace to pass
+ * and may not call cudaMalloc.  Same arguments and result as dx_fused_linear
+ * with DX_KERNEL_DECODE (fp16/bf16, M <= 64, TMA-aligned X and W), but the
+ * split-K scratch is a fixed 8 MiB device array inside the library; problems
+ * whose scratch (the same bytes dx_fused_linear_workspace_size reports for
+ * DX_KERNEL_DECODE) exceeds it return DX_ERR_WORKSPACE.  The first call on a device resolves that
+ * array's address and should precede any stream capture; calls that overlap on
+ * the GPU race on the shared array. */
+int dx_fused_linear_decode_noalloc(const void* X, const void* W, const void* bias,
+                                   const void* R, void* Y,
+                                   int64_t M, int64_t N, int64_t K,
+                                   int64_t ldx, int64_t ldw, int64_t ldr, int64_t ldy,
+                                   int dtype, int act, void* stream);
+
 /* Workspace bytes that dx_fused_linear(_ex) needs for this problem and
  * variant (DX_KERNEL_AUTO resolves as dx_select_kernel does). */
 size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K,

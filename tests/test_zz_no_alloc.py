@@ -1,0 +1,79 @@
+"""The decode entry point that allocates nothing (gpu).
+
+Some callers cannot allocate device memory when they launch a kernel: a
+runtime whose own heap manager owns every device buffer hands the kernel only
+raw pointers and a stream, so it has no workspace to pass and may not call
+cudaMalloc behind its allocator's back.  ``dx_fused_linear_decode_noalloc``
+serves them: it runs the split-K decode kernel with its scratch in a fixed
+array inside the library.  Its output must match the workspace-taking entry
+point (``dx_fused_linear`` via ``fused_linear(kernel="decode")``) within the
+fp16/bf16 tolerance the parity tests use, on consecutive calls that reuse the
+shared scratch.
+
+This file is collected last so that a failure here comes after every other
+test has run.
+"""
+import pytest
+import torch
+
+from deepx_op_gpukernelcompiler_b200 import _native as nat
+from deepx_op_gpukernelcompiler_b200 import fused_linear
+
+pytestmark = pytest.mark.gpu
+
+DEV = torch.device("cuda:0")
+RTOL = ATOL = 2e-2  # fp16/bf16 with fp32 accumulation, as in test_gpu_parity
+DTYPES = {torch.float16: nat.DX_DTYPE_F16, torch.bfloat16: nat.DX_DTYPE_BF16}
+_ACT = {None: nat.DX_ACT_NONE, "relu": nat.DX_ACT_RELU, "gelu_erf": nat.DX_ACT_GELU_ERF,
+        "silu": nat.DX_ACT_SILU}
+
+
+def _inputs(M, K, N, dtype, seed, residual=False):
+    g = torch.Generator(device=DEV)
+    g.manual_seed(seed)
+    X = torch.randn(M, K, generator=g, device=DEV).to(dtype)
+    W = (torch.randn(K, N, generator=g, device=DEV) / K ** 0.5).to(dtype)
+    b = (torch.rand(N, generator=g, device=DEV) * 0.2 - 0.1).to(dtype)
+    R = torch.randn(M, N, generator=g, device=DEV).to(dtype) if residual else None
+    return X, W, b, R
+
+
+def _noalloc(X, W, b, R, act):
+    M, K = X.shape
+    N = W.shape[1]
+    Y = torch.empty(M, N, dtype=X.dtype, device=DEV)
+    rc = nat.load().dx_fused_linear_decode_noalloc(
+        X.data_ptr(), W.data_ptr(), b.data_ptr(), R.data_ptr() if R is not None else None,
+        Y.data_ptr(), M, N, K, K, N, N if R is not None else 0, N, DTYPES[X.dtype],
+        _ACT[act], torch.cuda.current_stream(DEV).cuda_stream)
+    nat.check("dx_fused_linear_decode_noalloc", rc)
+    return Y
+
+
+def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
+    # Consecutive calls with different shapes share the static scratch; the
+    # third repeats the first to show nothing stale carries over.
+    calls = [
+        (16, 4096, 3072, torch.float16, "gelu_erf", 1, False),
+        (5, 2048, 1536, torch.bfloat16, "silu", 2, True),
+        (16, 4096, 3072, torch.float16, "gelu_erf", 1, False),
+    ]
+    for M, K, N, dtype, act, seed, residual in calls:
+        X, W, b, R = _inputs(M, K, N, dtype, seed, residual)
+        got = _noalloc(X, W, b, R, act)
+        want = fused_linear(X, W, b, act, residual=R, kernel="decode")
+        torch.cuda.synchronize()
+        assert torch.allclose(got.float(), want.float(), rtol=RTOL, atol=ATOL), (
+            f"{M}x{K}x{N} {dtype}: max |diff| {(got.float() - want.float()).abs().max().item()}")
+    assert nat.device_status(torch.cuda.current_stream(DEV).cuda_stream) == 0
+
+
+def test_noalloc_rejects_problems_beyond_its_scratch():
+    # 512 n-tiles of 64 padded rows: 16 MiB of partial sums > the 8 MiB array.
+    X, W, b, _ = _inputs(64, 64, 65536, torch.float16, 3)
+    Y = torch.empty(64, 65536, dtype=torch.float16, device=DEV)
+    rc = nat.load().dx_fused_linear_decode_noalloc(
+        X.data_ptr(), W.data_ptr(), b.data_ptr(), None, Y.data_ptr(), 64, 65536, 64, 64, 65536,
+        0, 65536, nat.DX_DTYPE_F16, nat.DX_ACT_NONE, torch.cuda.current_stream(DEV).cuda_stream)
+    assert rc == nat.DX_ERR_WORKSPACE
+    assert "static scratch" in nat.last_error()
