@@ -1,0 +1,68 @@
+"""Worker for tests/test_gpu_multi.py: one process per GPU under torchrun.
+
+Checks, on every rank, the sharded engine against the single-GPU engine on
+the same seeded inputs: the column-parallel layer (gathered) and the
+column -> row MLP with its NCCL all-reduce.  Exits non-zero on a mismatch.
+"""
+import os
+import sys
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+import torch.distributed as dist
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+
+from deepx_op_gpukernelcompiler_b200 import _native, fused_linear, mlp_residual  # noqa: E402
+from deepx_op_gpukernelcompiler_b200.shard import ColumnParallelLinear, ParallelMLP  # noqa: E402
+
+
+def main() -> int:
+    local = int(os.environ["LOCAL_RANK"])
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
+    rank, world = dist.get_rank(), dist.get_world_size()
+    failures = []
+    try:
+        g = torch.Generator(device=dev)
+        g.manual_seed(7)
+        M, K, N = 1024, 1024, 2560
+        X = torch.randn(M, K, generator=g, device=dev).bfloat16()
+        W = (torch.randn(K, N, generator=g, device=dev) / K ** 0.5).bfloat16()
+        b = (torch.rand(N, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
+        full = fused_linear(X, W, b, "silu")
+        col = ColumnParallelLinear(W, b, "silu", gather_output=True)
+        got = col(X)
+        torch.cuda.synchronize()
+        if not torch.equal(got, full):
+            failures.append(f"column-parallel differs: max {(got.float() - full.float()).abs().max()}")
+
+        H = 4096
+        W1 = (torch.randn(K, H, generator=g, device=dev) / K ** 0.5).bfloat16()
+        b1 = (torch.rand(H, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
+        W2 = (torch.randn(H, K, generator=g, device=dev) / H ** 0.5).bfloat16()
+        b2 = (torch.rand(K, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
+        ref = mlp_residual(X, W1, b1, W2, b2, "gelu").float()
+        for chunks in (1, 4):
+            mlp = ParallelMLP(W1, b1, W2, b2, "gelu", chunks=chunks)
+            out = mlp(X).float()
+            torch.cuda.synchronize()
+            err = (out - ref).abs()
+            tol = 2e-2 + 2e-2 * ref.abs()
+            if bool((err > tol).any()):
+                failures.append(f"MLP (chunks={chunks}) off by up to {err.max().item():.4g}")
+        status = _native.device_status(torch.cuda.current_stream(dev).cuda_stream)
+        if status:
+            failures.append(f"device status {status}")
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+    for f in failures:
+        print(f"rank {rank}/{world}: {f}", flush=True)
+    return 1 if failures else 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
