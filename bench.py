@@ -267,6 +267,9 @@ def run_gpu(args) -> None:
     peaks, peak_kind = _peaks()
     w = WORKLOADS[args.workload]
     n0, n1 = shard_bounds(w.N, world, rank, 64)
+    if args.shard_of > 1:
+        # One GPU running rank 0's share of an N-way column split.
+        n0, n1 = shard_bounds(w.N, args.shard_of, 0, 64)
     n_loc = n1 - n0
 
     # Inputs: X replicated, this rank's W/bias column shard; seeded on device.
@@ -549,6 +552,8 @@ def main() -> None:
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
     ap.add_argument("--profile", action="store_true",
                     help="run only W warm-up and K timed launches of the workload (for ncu)")
+    ap.add_argument("--shard-of", type=int, default=1,
+                    help="with --profile: run rank 0's column shard of an N-way split on one GPU")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

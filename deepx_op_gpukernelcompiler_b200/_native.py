@@ -65,6 +65,7 @@ SIGNATURES = {
     "dx_select_kernel": (ctypes.c_int, [_i64, _i64, _i64, ctypes.c_int]),
     "dx_last_error_string": (ctypes.c_char_p, []),
     "dx_last_launch_plan": (ctypes.c_char_p, []),
+    "dx_set_trace_buffer": (ctypes.c_int, [_vp, ctypes.c_size_t]),
     "dx_device_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int)]),
     "dx_version": (ctypes.c_int, []),
 }

@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -38,6 +39,10 @@ using dx::UmmaShape;
 
 thread_local std::string t_last_error;
 thread_local std::string t_last_plan;
+
+// Timeline buffer for the tensor-core kernels (dx_set_trace_buffer).
+std::atomic<unsigned long long*> g_trace{nullptr};
+std::atomic<size_t> g_trace_bytes{0};
 
 int fail(int code, const char* fmt, ...) {
   char buf[512];
@@ -196,27 +201,6 @@ CUtensorMapDataType tma_dtype(int dtype) {
   return dtype == DX_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
 }
 
-int pick_bn(int64_t M, int64_t N, int sms) {
-  if (N <= 128) return 128;
-  const int64_t mt = (M + 127) / 128;
-  const int64_t t256 = mt * ((N + 255) / 256);
-  const int64_t t128 = mt * ((N + 127) / 128);
-  const double c256 = static_cast<double>((t256 + sms - 1) / sms) * 256.0;
-  const double c128 = static_cast<double>((t128 + sms - 1) / sms) * 128.0 * 1.1;
-  return c128 < c256 ? 128 : 256;
-}
-
-// Pair tiles are 256 x BN; pick BN by estimated waves over the resident pairs.
-int pick_pair_bn(int64_t M, int64_t N, int pair_slots) {
-  if (N <= 128) return 128;
-  const int64_t mt = (M + 255) / 256;
-  const int64_t t256 = mt * ((N + 255) / 256);
-  const int64_t t128 = mt * ((N + 127) / 128);
-  const double c256 = static_cast<double>((t256 + pair_slots - 1) / pair_slots) * 256.0;
-  const double c128 = static_cast<double>((t128 + pair_slots - 1) / pair_slots) * 128.0 * 1.1;
-  return c128 < c256 ? 128 : 256;
-}
-
 // Rows of X per raster group: keep group_m x rows x K x 2 bytes within ~48 MB
 // (about a third of L2), with groups of equal size.
 int pick_group_m(int m_tiles, int64_t rows_per_tile, int64_t K) {
@@ -249,34 +233,118 @@ int make_umma_maps(const Problem& pr, CUtensorMap* tA, CUtensorMap* tB, CUtensor
   return DX_OK;
 }
 
-UmmaParams umma_params(const Problem& pr, int rows_per_tile, int bn) {
+// ------------------------------------------------------------ UMMA plan
+// One launch of a tensor-core GEMM: kernel (CTA pairs or single CTAs), tile
+// width BN, and the schedule: full waves of whole tiles, then the tiles of
+// the last partial wave split `splits` ways along K when a workspace allows.
+struct UmmaPlan {
+  bool pair = false;
+  int bn = 256;
+  int rows = 128;  // tile rows: 256 for pairs
+  int workers = 0;
+  int num_tiles = 0, dp_tiles = 0, splits = 1, k_blocks = 0;
+  size_t bytes = 0;  // workspace bytes the plan needs (0: none)
+};
+
+// Relative throughput of each kernel/tile shape per SM, measured on B200
+// (single-CTA 128x128 at 0.93 and the pair kernel at 256x128 at 0.80 of the
+// pair kernel at 256x256).
+double umma_efficiency(bool pair, int bn) {
+  if (pair) return bn == 256 ? 1.00 : 0.80;
+  return bn == 256 ? 0.97 : 0.93;
+}
+
+UmmaPlan plan_umma(int64_t M, int64_t N, int64_t K, int sms, int pair_slots, bool allow_split,
+                   bool single_cta_only) {
+  UmmaPlan best;
+  double best_cost = 1e300;
+  const int kb = static_cast<int>((K + 63) / 64);
+  for (int use_pair = 0; use_pair < 2; ++use_pair) {
+    if (use_pair && (single_cta_only || M < 256 || pair_slots <= 0)) continue;
+    for (int bn : {256, 128}) {
+      if (bn == 256 && N <= 128) continue;
+      UmmaPlan pl;
+      pl.pair = use_pair != 0;
+      pl.bn = bn;
+      pl.rows = pl.pair ? 256 : 128;
+      pl.workers = pl.pair ? pair_slots : sms;
+      pl.k_blocks = kb;
+      const int64_t tiles = ((M + pl.rows - 1) / pl.rows) * ((N + bn - 1) / bn);
+      pl.num_tiles = static_cast<int>(tiles);
+      const int64_t full = tiles / pl.workers, rem = tiles % pl.workers;
+      int splits = 1;
+      if (allow_split && rem > 0) {
+        // Each piece finishes a share of the tile's 32-column chunks, so at
+        // most BN / 32 pieces; each piece keeps at least 8 k-blocks.
+        splits = static_cast<int>(
+            std::min<int64_t>(std::min<int64_t>(pl.workers / rem, kb / 8), bn / 32));
+        if (splits < 2) splits = 1;
+      }
+      pl.splits = splits;
+      pl.dp_tiles = splits > 1 ? static_cast<int>(tiles - rem) : pl.num_tiles;
+      pl.bytes = splits > 1 ? kTicketSlabBytes + static_cast<size_t>(rem) * splits *
+                                                     (pl.pair ? 2 : 1) * 128 * bn * sizeof(float)
+                            : 0;
+      const double tail = rem == 0 ? 0.0 : (splits > 1 ? 1.0 / splits + 0.05 : 1.0);
+      const double cost = (static_cast<double>(full) + tail) * bn / umma_efficiency(pl.pair, bn);
+      if (cost < best_cost) {
+        best_cost = cost;
+        best = pl;
+      }
+    }
+  }
+  return best;
+}
+
+UmmaParams umma_params(const Problem& pr, const UmmaPlan& pl) {
   UmmaParams p{};
   p.M = static_cast<int>(pr.M);
   p.N = static_cast<int>(pr.N);
   p.K = static_cast<int>(pr.K);
-  p.m_tiles = static_cast<int>((pr.M + rows_per_tile - 1) / rows_per_tile);
-  p.n_tiles = static_cast<int>((pr.N + bn - 1) / bn);
-  p.k_blocks = static_cast<int>((pr.K + 63) / 64);
+  p.m_tiles = static_cast<int>((pr.M + pl.rows - 1) / pl.rows);
+  p.n_tiles = static_cast<int>((pr.N + pl.bn - 1) / pl.bn);
+  p.k_blocks = pl.k_blocks;
   p.num_tiles = p.m_tiles * p.n_tiles;
-  p.group_m = pick_group_m(p.m_tiles, rows_per_tile, pr.K);
+  p.group_m = pick_group_m(p.m_tiles, pl.rows, pr.K);
   p.bias = pr.bias;
   p.act = pr.act;
   p.has_residual = pr.R != nullptr ? 1 : 0;
+  p.workers = pl.workers;
+  p.dp_tiles = pl.dp_tiles;
+  p.splits = pl.splits;
+  p.tickets = pl.splits > 1 ? static_cast<int*>(pr.ws) : nullptr;
+  {
+    unsigned long long* tr = g_trace.load();
+    const size_t need = static_cast<size_t>(pl.workers) * (pl.pair ? 2 : 1) * dx::kTraceSlots * 8;
+    p.trace = (tr != nullptr && g_trace_bytes.load() >= need) ? tr : nullptr;
+  }
+  p.partials = pl.splits > 1
+                   ? reinterpret_cast<float*>(static_cast<char*>(pr.ws) + kTicketSlabBytes)
+                   : nullptr;
   return p;
 }
 
+// Launch grid: no more workers than work items.
+int umma_grid_workers(const UmmaPlan& pl) {
+  const int64_t items = static_cast<int64_t>(pl.dp_tiles) +
+                        static_cast<int64_t>(pl.num_tiles - pl.dp_tiles) * pl.splits;
+  return static_cast<int>(std::min<int64_t>(pl.workers, items));
+}
+
 template <int BN, typename T>
-int launch_umma(const Problem& pr, int dev, int sms) {
+int launch_umma(const Problem& pr, int dev, const UmmaPlan& pl) {
   using S = UmmaShape<BN>;
   auto kern = dx::umma_fused_linear_kernel<BN, T>;
   int rc = ensure_smem_attr(dev, reinterpret_cast<const void*>(kern), S::SMEM_BYTES, false);
   if (rc) return rc;
   CUtensorMap tA, tB, tY, tR;
   if ((rc = make_umma_maps(pr, &tA, &tB, &tY, &tR))) return rc;
-  const UmmaParams p = umma_params(pr, 128, BN);
-  const int grid = std::min(p.num_tiles, sms);
-  set_plan("umma_1cta tile=128x%d stages=%d grid=%d tiles=%d group_m=%d smem=%d", BN, S::STAGES,
-           grid, p.num_tiles, p.group_m, S::SMEM_BYTES);
+  const UmmaParams p = umma_params(pr, pl);
+  const int grid = umma_grid_workers(pl);
+  set_plan("umma_1cta tile=128x%d stages=%d grid=%d tiles=%d dp_tiles=%d splits=%d group_m=%d "
+           "smem=%d workspace=%zu",
+           BN, S::STAGES, grid, p.num_tiles, p.dp_tiles, p.splits, p.group_m, S::SMEM_BYTES,
+           pl.bytes);
   kern<<<grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tA, tB, tY, tR, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch umma_fused_linear_kernel");
@@ -326,17 +394,19 @@ int pair_slots(int dev, int sms) {
 }
 
 template <int BN, typename T>
-int launch_umma2(const Problem& pr, int dev, int slots) {
+int launch_umma2(const Problem& pr, int dev, const UmmaPlan& pl) {
   using S = Umma2Shape<BN>;
   auto kern = dx::umma2_fused_linear_kernel<BN, T>;
   int rc = ensure_smem_attr(dev, reinterpret_cast<const void*>(kern), S::SMEM_BYTES, false);
   if (rc) return rc;
   CUtensorMap tA, tB, tY, tR;
   if ((rc = make_umma_maps(pr, &tA, &tB, &tY, &tR))) return rc;
-  const UmmaParams p = umma_params(pr, 256, BN);
-  const int grid = 2 * std::min(p.num_tiles, slots);
-  set_plan("umma_pair tile=256x%d stages=%d grid=%d pair_slots=%d tiles=%d group_m=%d smem=%d", BN,
-           S::STAGES, grid, slots, p.num_tiles, p.group_m, S::SMEM_BYTES);
+  const UmmaParams p = umma_params(pr, pl);
+  const int grid = 2 * umma_grid_workers(pl);
+  set_plan("umma_pair tile=256x%d stages=%d grid=%d pair_slots=%d tiles=%d dp_tiles=%d splits=%d "
+           "group_m=%d smem=%d workspace=%zu",
+           BN, S::STAGES, grid, pl.workers, p.num_tiles, p.dp_tiles, p.splits, p.group_m,
+           S::SMEM_BYTES, pl.bytes);
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pair_launch_config(grid, S::THREADS, S::SMEM_BYTES, pr.stream, attr);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tY, tR, p);
@@ -465,20 +535,25 @@ int select_variant(const Problem& p, int sms, bool ws_known) {
   return DX_KERNEL_SIMT;
 }
 
+// The plan for this call: with the split tail when the caller's workspace
+// holds it, else whole tiles only.
+UmmaPlan umma_plan_for(const Problem& p, int dev, int sms, bool single_cta_only) {
+  const int slots = (p.M >= 256 && !single_cta_only) ? pair_slots<256, __nv_bfloat16>(dev, sms) : 0;
+  UmmaPlan pl = plan_umma(p.M, p.N, p.K, sms, slots, true, single_cta_only);
+  if (pl.bytes > 0 && (p.ws == nullptr || p.ws_bytes < pl.bytes || !aligned16(p.ws)))
+    pl = plan_umma(p.M, p.N, p.K, sms, slots, false, single_cta_only);
+  return pl;
+}
+
 template <typename T>
 int dispatch_typed(const Problem& p, int variant, int dev, int sms) {
   switch (variant) {
     case DX_KERNEL_UMMA:
     case DX_KERNEL_UMMA_1CTA: {
-      // CTA pairs for M >= 256 (256-row tiles), single CTAs below that.
-      const int slots =
-          (p.M >= 256 && variant == DX_KERNEL_UMMA) ? pair_slots<256, T>(dev, sms) : 0;
-      if (slots > 0) {
-        const int bn = pick_pair_bn(p.M, p.N, slots);
-        return bn == 256 ? launch_umma2<256, T>(p, dev, slots) : launch_umma2<128, T>(p, dev, slots);
-      }
-      const int bn = pick_bn(p.M, p.N, sms);
-      return bn == 256 ? launch_umma<256, T>(p, dev, sms) : launch_umma<128, T>(p, dev, sms);
+      const UmmaPlan pl = umma_plan_for(p, dev, sms, variant == DX_KERNEL_UMMA_1CTA);
+      if (pl.pair)
+        return pl.bn == 256 ? launch_umma2<256, T>(p, dev, pl) : launch_umma2<128, T>(p, dev, pl);
+      return pl.bn == 256 ? launch_umma<256, T>(p, dev, pl) : launch_umma<128, T>(p, dev, pl);
     }
     case DX_KERNEL_DECODE: {
       const DecodePlan d = decode_plan(p.M, p.N, p.K, sms);
@@ -557,13 +632,20 @@ int dx_fused_linear(const void* X, const void* W, const void* bias, const void* 
 
 size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K, int dtype, int kernel) {
   t_last_error.clear();
-  if (M <= 0 || N <= 0 || K <= 0 || dtype == DX_DTYPE_F32) return 0;
-  if (kernel == DX_KERNEL_UMMA || kernel == DX_KERNEL_SIMT || kernel == DX_KERNEL_UMMA_1CTA)
-    return 0;
-  if (M > kDecodeMaxM || (N + 127) / 128 > kDecodeMaxTiles) return 0;
+  if (M <= 0 || N <= 0 || K <= 0 || dtype == DX_DTYPE_F32 || kernel == DX_KERNEL_SIMT) return 0;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || device_sms(dev, &sms) != DX_OK) return 0;
-  return decode_plan(M, N, K, sms).bytes;
+  if (kernel == DX_KERNEL_AUTO) kernel = dx_select_kernel(M, N, K, dtype);
+  if (kernel == DX_KERNEL_DECODE) {
+    if (M > kDecodeMaxM || (N + 127) / 128 > kDecodeMaxTiles) return 0;
+    return decode_plan(M, N, K, sms).bytes;
+  }
+  if (kernel == DX_KERNEL_UMMA || kernel == DX_KERNEL_UMMA_1CTA) {
+    const bool single = kernel == DX_KERNEL_UMMA_1CTA;
+    const int slots = (M >= 256 && !single) ? pair_slots<256, __nv_bfloat16>(dev, sms) : 0;
+    return plan_umma(M, N, K, sms, slots, true, single).bytes;
+  }
+  return 0;
 }
 
 int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype) {
@@ -576,6 +658,15 @@ int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype) {
 const char* dx_last_error_string(void) { return t_last_error.c_str(); }
 
 const char* dx_last_launch_plan(void) { return t_last_plan.c_str(); }
+
+int dx_set_trace_buffer(void* device_buffer, size_t bytes) {
+  t_last_error.clear();
+  if (device_buffer != nullptr && (reinterpret_cast<uintptr_t>(device_buffer) & 7u) != 0)
+    return fail(DX_ERR_INVALID_ARGUMENT, "trace buffer must be 8-byte aligned");
+  g_trace_bytes.store(device_buffer != nullptr ? bytes : 0);
+  g_trace.store(static_cast<unsigned long long*>(device_buffer));
+  return DX_OK;
+}
 
 int dx_device_status(void* stream, int* status) {
   t_last_error.clear();

@@ -8,7 +8,11 @@
 //                                                   kernel_tilelang.py:17)
 //   silu / swish    x * sigmoid(x)                 (fusion.py:90-91,
 //                                                   kernel_triton.py:63)
-// The transcendental parts call CUDA's own tanhf / erff / expf.
+// The exact forms call CUDA's tanhf / erff / expf and IEEE division (used
+// for fp32 outputs).  For fp16/bf16 outputs (kFast) GELU-tanh uses the
+// hardware tanh (tanh.approx.f32, max relative error about 2^-11) and SiLU
+// the fast exponential and division intrinsics — far inside the output
+// rounding; GELU-erf keeps erff.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -19,6 +23,13 @@ namespace dx {
 
 enum Act : int { kActNone = 0, kActRelu = 1, kActGeluTanh = 2, kActGeluErf = 3, kActSilu = 4 };
 
+__device__ __forceinline__ float tanh_hw(float x) {
+  float y;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+template <bool kFast = true>
 __device__ __forceinline__ float act_apply(float x, int act) {
   switch (act) {
     case kActRelu:
@@ -26,12 +37,12 @@ __device__ __forceinline__ float act_apply(float x, int act) {
     case kActGeluTanh: {
       // sqrt(2/pi) * (x + 0.044715 x^3)
       const float u = 0.7978845608028654f * fmaf(0.044715f * x, x * x, x);
-      return 0.5f * x * (1.0f + tanhf(u));
+      return 0.5f * x * (1.0f + (kFast ? tanh_hw(u) : tanhf(u)));
     }
     case kActGeluErf:
       return 0.5f * x * (1.0f + erff(x * 0.7071067811865476f));
     case kActSilu:
-      return x / (1.0f + expf(-x));
+      return kFast ? __fdividef(x, 1.0f + __expf(-x)) : x / (1.0f + expf(-x));
     default:
       return x;
   }

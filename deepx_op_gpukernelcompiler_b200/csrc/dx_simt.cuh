@@ -10,6 +10,8 @@
 // thread (ty, tx) owns rows ty + 16 i and columns tx + 16 j.
 #pragma once
 
+#include <type_traits>
+
 #include "dx_epilogue.cuh"
 
 namespace dx {
@@ -74,7 +76,7 @@ __global__ void __launch_bounds__(256)
       if (n >= N) continue;
       float v = acc[i][j];
       if (bias != nullptr) v += Tr::to_float(bias[n]);
-      v = act_apply(v, act);
+      v = act_apply<!std::is_same<T, float>::value>(v, act);
       if (R != nullptr) v += Tr::to_float(R[m * ldr + n]);
       Y[m * ldy + n] = Tr::from_float(v);
     }

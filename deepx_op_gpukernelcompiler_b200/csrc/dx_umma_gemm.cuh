@@ -46,7 +46,51 @@ struct UmmaParams {
   const void* bias;                           // N elements, or nullptr
   int act;
   int has_residual;
+  // Schedule.  Work items are dealt round-robin to `workers` (CTA pairs or
+  // CTAs): first the tiles [0, dp_tiles) whole, then every remaining tile as
+  // `splits` pieces of its K range, so the last partial wave of tiles is
+  // spread over otherwise idle SMs.  Split pieces leave fp32 partial sums in
+  // `partials`; the last piece of a 32-row slab to finish (per-warp ticket)
+  // adds them in split order and runs the epilogue.
+  int workers;
+  int dp_tiles;
+  int splits;
+  float* partials;  // [tail tile][split][CTA of the tile][128][BN]
+  int* tickets;     // [tail tile][CTA of the tile][4 warps][2]; zero between calls
+  // Optional timeline (dx_set_trace_buffer): per CTA kTraceSlots device-time
+  // stamps: [0] after set-up, [1 + i] when the epilogue finished work item i
+  // (first kTraceSlots - 2 items), [kTraceSlots - 1] at exit.
+  unsigned long long* trace;
 };
+
+constexpr int kTraceSlots = 16;
+
+__device__ __forceinline__ void trace_mark(const UmmaParams& p, int slot) {
+  if (p.trace != nullptr && slot < kTraceSlots)
+    p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + slot] = global_timer_ns();
+}
+
+struct WorkItem {
+  int tile, kb0, kb1, split;  // split < 0: the whole K range of the tile
+};
+
+__device__ __forceinline__ bool umma_item(const UmmaParams& p, int worker, int i, WorkItem& w) {
+  const long long idx = static_cast<long long>(worker) + static_cast<long long>(i) * p.workers;
+  if (idx < p.dp_tiles) {
+    w.tile = static_cast<int>(idx);
+    w.kb0 = 0;
+    w.kb1 = p.k_blocks;
+    w.split = -1;
+    return true;
+  }
+  const long long j = idx - p.dp_tiles;
+  if (j >= static_cast<long long>(p.num_tiles - p.dp_tiles) * p.splits) return false;
+  w.tile = p.dp_tiles + static_cast<int>(j / p.splits);
+  w.split = static_cast<int>(j % p.splits);
+  w.kb0 = static_cast<int>((static_cast<long long>(w.split) * p.k_blocks) / p.splits);
+  w.kb1 = static_cast<int>((static_cast<long long>(w.split + 1) * p.k_blocks) / p.splits);
+  return true;
+}
 
 __device__ __forceinline__ void umma_tile_coords(const UmmaParams& p, int t, int& mb, int& nb) {
   const int per_group = p.group_m * p.n_tiles;
@@ -75,6 +119,97 @@ struct EpilogueCtx {
   uint64_t pol_stream; // evict-first policy for Y stores and R loads
 };
 
+// Staging-buffer half of a 32-column chunk: waits until the store that last
+// used this buffer has read it, and starts the residual tile's TMA load.
+template <typename T>
+__device__ __forceinline__ void epi_chunk_begin(const EpilogueCtx<T>& c, int n_c, int row_base,
+                                                int lane, uint32_t it) {
+  const int buf = it & 1;
+  if (lane == 0) bulk_wait_group_read<1>();
+  __syncwarp();
+  if (c.has_residual && lane == 0) {
+    const uint32_t rbar = c.rbar0 + 8u * buf;
+    mbar_arrive_expect_tx(rbar, kEpiBufBytes);
+    tma_load_2d_hint(c.tmR, c.ebuf0 + buf * kEpiBufBytes, rbar, n_c, row_base, c.pol_stream);
+  }
+}
+
+// Finishes a 32-column chunk whose fp32 sums are in v: bias, activation,
+// residual, convert, stage (64-byte swizzle) and TMA-store.  Returns false
+// if the residual wait gave up.
+template <typename T>
+__device__ __forceinline__ bool epi_chunk_end(const EpilogueCtx<T>& c, float (&v)[32], int n_c,
+                                              int row_base, int lane, uint32_t& it,
+                                              volatile int* abort_flag) {
+  using Tr = ElemTraits<T>;
+  const int buf = it & 1;
+  const uint32_t ebuf = c.ebuf0 + buf * kEpiBufBytes;
+  uint8_t* const ebp = c.ebuf_ptr0 + buf * kEpiBufBytes;
+  const uint32_t row_off = static_cast<uint32_t>(lane) * 64u;
+  const uint32_t row_sw = (static_cast<uint32_t>(lane) >> 1) & 3u;  // 64-byte swizzle phase
+  if (c.bias != nullptr) {
+    if (c.bias_vec_ok && n_c + 32 <= c.N) {
+      const uint4* bp = reinterpret_cast<const uint4*>(c.bias + n_c);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint4 w = __ldg(bp + j);
+        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+          const float2 f = Tr::unpack2(wv[h]);
+          v[8 * j + 2 * h] += f.x;
+          v[8 * j + 2 * h + 1] += f.y;
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (n_c + j < c.N) v[j] += Tr::to_float(c.bias[n_c + j]);
+    }
+  }
+  if (c.act != kActNone) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = act_apply(v[j], c.act);
+  }
+  if (c.has_residual) {
+    const uint32_t rbar = c.rbar0 + 8u * buf;
+    const uint32_t par = (it >> 1) & 1u;
+    if (!mbar_wait(rbar, par, abort_flag)) {
+      mbar_wait_drain(rbar, par);  // the load still lands in this buffer
+      return false;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint4 w = *reinterpret_cast<const uint4*>(
+          ebp + row_off + ((static_cast<uint32_t>(j) ^ row_sw) << 4));
+      const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = Tr::unpack2(wv[h]);
+        v[8 * j + 2 * h] += f.x;
+        v[8 * j + 2 * h + 1] += f.y;
+      }
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    uint4 w;
+    w.x = Tr::pack2(v[8 * j + 0], v[8 * j + 1]);
+    w.y = Tr::pack2(v[8 * j + 2], v[8 * j + 3]);
+    w.z = Tr::pack2(v[8 * j + 4], v[8 * j + 5]);
+    w.w = Tr::pack2(v[8 * j + 6], v[8 * j + 7]);
+    *reinterpret_cast<uint4*>(ebp + row_off + ((static_cast<uint32_t>(j) ^ row_sw) << 4)) = w;
+  }
+  fence_proxy_async_smem();
+  __syncwarp();
+  if (lane == 0) {
+    tma_store_2d_hint(c.tmY, ebuf, n_c, row_base, c.pol_stream);
+    bulk_commit_group();
+  }
+  ++it;
+  return true;
+}
+
 // Drains one 128 x BN accumulator: this warp handles TMEM lanes
 // [32q, 32q+32), i.e. global rows row0 + 32q + lane, columns n0 .. n0+BN.
 // `release()` is called (lane 0, after the last TMEM read) to hand the
@@ -84,34 +219,70 @@ template <int BN, typename T, typename Release>
 __device__ __forceinline__ bool epilogue_tile(const EpilogueCtx<T>& c, uint32_t tmem_acc, int q,
                                               int lane, int row0, int n0, uint32_t& it,
                                               volatile int* abort_flag, Release release) {
-  using Tr = ElemTraits<T>;
-  const uint32_t row_off = static_cast<uint32_t>(lane) * 64u;
-  const uint32_t row_sw = (static_cast<uint32_t>(lane) >> 1) & 3u;  // 64-byte swizzle phase
   const int row_base = row0 + q * 32;
   const bool rows_live = row_base < c.M;
 #pragma unroll 1
   for (int ch = 0; ch < BN / 32; ++ch) {
     const int n_c = n0 + 32 * ch;
     const bool live = rows_live && n_c < c.N;  // warp-uniform
-    if (!live) {
+    if (live) epi_chunk_begin(c, n_c, row_base, lane, it);
+    if (live || ch == BN / 32 - 1) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(tmem_acc + static_cast<uint32_t>(32 * ch) +
+                             (static_cast<uint32_t>(q * 32) << 16),
+                         r);
+      tmem_wait_ld();
       if (ch == BN / 32 - 1) {
         tc_fence_before();
         __syncwarp();
         if (lane == 0) release();
       }
-      continue;
+      if (!live) continue;
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+      if (!epi_chunk_end(c, v, n_c, row_base, lane, it, abort_flag)) return false;
     }
-    const int buf = it & 1;
-    const uint32_t ebuf = c.ebuf0 + buf * kEpiBufBytes;
-    uint8_t* const ebp = c.ebuf_ptr0 + buf * kEpiBufBytes;
-    const uint32_t rbar = c.rbar0 + 8u * buf;
-    // The store issued two chunks ago from this buffer must have read it.
-    if (lane == 0) bulk_wait_group_read<1>();
-    __syncwarp();
-    if (c.has_residual && lane == 0) {
-      mbar_arrive_expect_tx(rbar, kEpiBufBytes);
-      tma_load_2d_hint(c.tmR, ebuf, rbar, n_c, row_base, c.pol_stream);
+  }
+  return true;
+}
+
+// Bounded wait until *ctr reaches `target` (other CTAs of this launch add to
+// it; all CTAs of the launch are resident).  Returns false on timeout.
+__device__ __forceinline__ bool wait_counter(const int* ctr, int target, volatile int* abort_flag) {
+  if (*reinterpret_cast<const volatile int*>(ctr) >= target) return true;
+  const uint64_t t0 = global_timer_ns();
+  uint32_t spins = 0;
+  while (*reinterpret_cast<const volatile int*>(ctr) < target) {
+    __nanosleep(64);
+    if ((++spins & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicOr(&g_device_status, 1);
+        return false;
+      }
     }
+  }
+  return true;
+}
+
+// One K-split piece of a tail tile, for this warp's 32-row slab.  Every
+// piece publishes its fp32 partial sums, waits until all `splits` pieces of
+// the slab have published, then adds the pieces in split order (a fixed
+// order: results do not depend on timing) for its own share of the columns —
+// chunks ch with ch % splits == split — and runs the epilogue on them.  The
+// last piece to leave resets the slab's two counters (`ctr[0]` arrivals,
+// `ctr[1]` departures) to zero.  Returns false if a bounded wait gave up.
+template <int BN, typename T, typename Release, typename PartBase>
+__device__ __forceinline__ bool epilogue_split(const EpilogueCtx<T>& c, uint32_t tmem_acc, int q,
+                                               int lane, int row0, int n0, int split, int splits,
+                                               int* ctr, PartBase part_base, uint32_t& it,
+                                               volatile int* abort_flag, Release release) {
+  const int row = q * 32 + lane;  // row within this CTA's 128
+  float* const mine = part_base(split) + static_cast<size_t>(row) * BN;
+#pragma unroll 1
+  for (int ch = 0; ch < BN / 32; ++ch) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(tmem_acc + static_cast<uint32_t>(32 * ch) +
                            (static_cast<uint32_t>(q * 32) << 16),
@@ -122,68 +293,77 @@ __device__ __forceinline__ bool epilogue_tile(const EpilogueCtx<T>& c, uint32_t 
       __syncwarp();
       if (lane == 0) release();
     }
+    float4* dst = reinterpret_cast<float4*>(mine + 32 * ch);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                           __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+  }
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) atomicAdd(ctr, 1);
+  bool ok = true;
+  if (lane == 0) ok = wait_counter(ctr, splits, abort_flag);
+  ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+  if (!ok) return false;
+  __threadfence();
+  const int row_base = row0 + q * 32;
+  const bool rows_live = row_base < c.M;
+#pragma unroll 1
+  for (int ch = split; ch < BN / 32; ch += splits) {
+    const int n_c = n0 + 32 * ch;
+    if (!(rows_live && n_c < c.N)) continue;
+    epi_chunk_begin(c, n_c, row_base, lane, it);
     float v[32];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-    if (c.bias != nullptr) {
-      if (c.bias_vec_ok && n_c + 32 <= c.N) {
-        const uint4* bp = reinterpret_cast<const uint4*>(c.bias + n_c);
+    for (int j = 0; j < 32; ++j) v[j] = 0.0f;
+    // Two splits per step with all 16 loads issued before the adds.
+    int sp = 0;
+    for (; sp + 1 < splits; sp += 2) {
+      const float4* a =
+          reinterpret_cast<const float4*>(part_base(sp) + static_cast<size_t>(row) * BN + 32 * ch);
+      const float4* b = reinterpret_cast<const float4*>(part_base(sp + 1) +
+                                                        static_cast<size_t>(row) * BN + 32 * ch);
+      float4 fa[8], fb[8];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const uint4 w = __ldg(bp + j);
-          const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-          for (int h = 0; h < 4; ++h) {
-            const float2 f = Tr::unpack2(wv[h]);
-            v[8 * j + 2 * h] += f.x;
-            v[8 * j + 2 * h + 1] += f.y;
-          }
-        }
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j)
-          if (n_c + j < c.N) v[j] += Tr::to_float(c.bias[n_c + j]);
-      }
-    }
-    if (c.act != kActNone) {
-#pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = act_apply(v[j], c.act);
-    }
-    if (c.has_residual) {
-      const uint32_t par = (it >> 1) & 1u;
-      if (!mbar_wait(rbar, par, abort_flag)) {
-        mbar_wait_drain(rbar, par);  // the load still lands in this buffer
-        return false;
+      for (int j = 0; j < 8; ++j) {
+        fa[j] = __ldcg(a + j);
+        fb[j] = __ldcg(b + j);
       }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 w = *reinterpret_cast<const uint4*>(
-            ebp + row_off + ((static_cast<uint32_t>(j) ^ row_sw) << 4));
-        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const float2 f = Tr::unpack2(wv[h]);
-          v[8 * j + 2 * h] += f.x;
-          v[8 * j + 2 * h + 1] += f.y;
-        }
+      for (int j = 0; j < 8; ++j) {
+        v[4 * j] += fa[j].x;
+        v[4 * j + 1] += fa[j].y;
+        v[4 * j + 2] += fa[j].z;
+        v[4 * j + 3] += fa[j].w;
+        v[4 * j] += fb[j].x;
+        v[4 * j + 1] += fb[j].y;
+        v[4 * j + 2] += fb[j].z;
+        v[4 * j + 3] += fb[j].w;
       }
     }
+    if (sp < splits) {
+      const float4* a =
+          reinterpret_cast<const float4*>(part_base(sp) + static_cast<size_t>(row) * BN + 32 * ch);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      uint4 w;
-      w.x = Tr::pack2(v[8 * j + 0], v[8 * j + 1]);
-      w.y = Tr::pack2(v[8 * j + 2], v[8 * j + 3]);
-      w.z = Tr::pack2(v[8 * j + 4], v[8 * j + 5]);
-      w.w = Tr::pack2(v[8 * j + 6], v[8 * j + 7]);
-      *reinterpret_cast<uint4*>(ebp + row_off + ((static_cast<uint32_t>(j) ^ row_sw) << 4)) = w;
+      for (int j = 0; j < 8; ++j) {
+        const float4 f = __ldcg(a + j);
+        v[4 * j] += f.x;
+        v[4 * j + 1] += f.y;
+        v[4 * j + 2] += f.z;
+        v[4 * j + 3] += f.w;
+      }
     }
-    fence_proxy_async_smem();
-    __syncwarp();
-    if (lane == 0) {
-      tma_store_2d_hint(c.tmY, ebuf, n_c, row_base, c.pol_stream);
-      bulk_commit_group();
+    if (!epi_chunk_end(c, v, n_c, row_base, lane, it, abort_flag)) return false;
+  }
+  __syncwarp();
+  if (lane == 0) {
+    const int left = atomicAdd(ctr + 1, 1);
+    if (left == splits - 1) {
+      // Every piece has seen ctr[0] == splits and finished reading.
+      ctr[0] = 0;
+      ctr[1] = 0;
     }
-    ++it;
   }
   return true;
 }
@@ -272,6 +452,7 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_word;
+  if (threadIdx.x == 0) trace_mark(p, 0);
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -280,11 +461,13 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
       int s = 0;
       uint32_t ph = 0, issued = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x) {
+      for (int i = 0; ok; ++i) {
+        WorkItem w;
+        if (!umma_item(p, blockIdx.x, i, w)) break;
         int mb, nb;
-        umma_tile_coords(p, t, mb, nb);
+        umma_tile_coords(p, w.tile, mb, nb);
         const int m0 = mb * S::BM, n0 = nb * BN;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(bar(S::BAR_EMPTY + s), ph ^ 1u, abort_flag)) {
             ok = false;
             break;
@@ -317,13 +500,15 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
       int s = 0, local = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.num_tiles; t += gridDim.x, ++local) {
+      for (int i = 0; ok; ++i, ++local) {
+        WorkItem w;
+        if (!umma_item(p, blockIdx.x, i, w)) break;
         const int b = local & 1;
         const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
         if (!mbar_wait(bar(S::BAR_TEMPTY + b), use_ph ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(bar(S::BAR_FULL + s), ph, abort_flag)) {
             ok = false;
             break;
@@ -336,7 +521,8 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
           const uint64_t bd = smem_desc_sw128(sB + s * S::B_BYTES, S::B_BOX_BYTES, 1024);
 #pragma unroll
           for (int k = 0; k < S::BK / 16; ++k)
-            umma_f16(d_tmem, ad + 2ull * k, bd + 128ull * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16(d_tmem, ad + 2ull * k, bd + 128ull * k, idesc,
+                     (kb != w.kb0 || k != 0) ? 1u : 0u);
           umma_commit(bar(S::BAR_EMPTY + s));
           if (++s == S::STAGES) {
             s = 0;
@@ -369,18 +555,34 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
     c.pol_stream = make_l2_policy_evict_first();
     uint32_t it = 0;
     int local = 0;
-    for (int t = blockIdx.x; t < p.num_tiles; t += gridDim.x, ++local) {
+    for (int i = 0;; ++i, ++local) {
+      WorkItem w;
+      if (!umma_item(p, blockIdx.x, i, w)) break;
       const int b = local & 1;
       const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
       if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
       tc_fence_after();
       int mb, nb;
-      umma_tile_coords(p, t, mb, nb);
+      umma_tile_coords(p, w.tile, mb, nb);
       const uint32_t tempty = bar(S::BAR_TEMPTY + b);
-      if (!epilogue_tile<BN, T>(c, tmem_base + static_cast<uint32_t>(b * BN), q, lane,
-                                mb * S::BM, nb * BN, it, abort_flag,
-                                [tempty] { mbar_arrive(tempty); }))
-        break;
+      const uint32_t acc = tmem_base + static_cast<uint32_t>(b * BN);
+      auto release = [tempty] { mbar_arrive(tempty); };
+      bool done;
+      if (w.split < 0) {
+        done = epilogue_tile<BN, T>(c, acc, q, lane, mb * S::BM, nb * BN, it, abort_flag, release);
+      } else {
+        const int tail = w.tile - p.dp_tiles;
+        float* const partials = p.partials;
+        const int splits = p.splits;
+        auto part_base = [partials, tail, splits](int sp) {
+          return partials + static_cast<size_t>(tail * splits + sp) * 128 * BN;
+        };
+        done = epilogue_split<BN, T>(c, acc, q, lane, mb * S::BM, nb * BN, w.split, splits,
+                                     p.tickets + (tail * 4 + q) * 2, part_base, it, abort_flag,
+                                     release);
+      }
+      if (!done) break;
+      if (e == 0 && lane == 0) trace_mark(p, 1 + i);
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
@@ -388,6 +590,7 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace_mark(p, kTraceSlots - 1);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, S::TMEM_COLS);
@@ -451,7 +654,6 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
   const uint32_t rank = cluster_ctarank();  // 0 = leader of the pair
   const bool leader = rank == 0;
   const int pair = static_cast<int>(blockIdx.x >> 1);
-  const int npairs = static_cast<int>(gridDim.x >> 1);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S::STAGES; ++s) {
@@ -483,6 +685,7 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_word;
+  if (threadIdx.x == 0) trace_mark(p, 0);
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -491,12 +694,14 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
       int s = 0;
       uint32_t ph = 0, issued = 0;
       bool ok = true;
-      for (int t = pair; ok && t < p.num_tiles; t += npairs) {
+      for (int i = 0; ok; ++i) {
+        WorkItem w;
+        if (!umma_item(p, pair, i, w)) break;
         int mb, nb;
-        umma_tile_coords(p, t, mb, nb);
+        umma_tile_coords(p, w.tile, mb, nb);
         const int m0 = mb * 2 * S::BM + static_cast<int>(rank) * S::BM;
         const int n0 = nb * BN + static_cast<int>(rank) * S::BN_CTA;
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(bar(S::BAR_EMPTY + s), ph ^ 1u, abort_flag)) {
             ok = false;
             break;
@@ -531,13 +736,15 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
       int s = 0, local = 0;
       uint32_t ph = 0;
       bool ok = true;
-      for (int t = pair; ok && t < p.num_tiles; t += npairs, ++local) {
+      for (int i = 0; ok; ++i, ++local) {
+        WorkItem w;
+        if (!umma_item(p, pair, i, w)) break;
         const int b = local & 1;
         const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
         if (!mbar_wait(bar(S::BAR_TEMPTY + b), use_ph ^ 1u, abort_flag)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * BN);
-        for (int kb = 0; kb < p.k_blocks; ++kb) {
+        for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(bar(S::BAR_FULL + s), ph, abort_flag)) {
             ok = false;
             break;
@@ -547,7 +754,8 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
           const uint64_t bd = smem_desc_sw128(sB + s * S::B_BYTES, S::B_BOX_BYTES, 1024);
 #pragma unroll
           for (int k = 0; k < S::BK / 16; ++k)
-            umma_f16_pair(d_tmem, ad + 2ull * k, bd + 128ull * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_f16_pair(d_tmem, ad + 2ull * k, bd + 128ull * k, idesc,
+                          (kb != w.kb0 || k != 0) ? 1u : 0u);
           // Stage s is free in both CTAs once these MMAs have read it.
           umma_commit_pair(mapa_shared(bar(S::BAR_EMPTY + s), 0));
           umma_commit_pair(mapa_shared(bar(S::BAR_EMPTY + s), 1));
@@ -584,19 +792,36 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
     c.pol_stream = make_l2_policy_evict_first();
     uint32_t it = 0;
     int local = 0;
-    for (int t = pair; t < p.num_tiles; t += npairs, ++local) {
+    for (int i = 0;; ++i, ++local) {
+      WorkItem w;
+      if (!umma_item(p, pair, i, w)) break;
       const int b = local & 1;
       const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
       if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
       tc_fence_after();
       int mb, nb;
-      umma_tile_coords(p, t, mb, nb);
+      umma_tile_coords(p, w.tile, mb, nb);
       const uint32_t tempty_leader = mapa_shared(bar(S::BAR_TEMPTY + b), 0);
-      if (!epilogue_tile<BN, T>(c, tmem_base + static_cast<uint32_t>(b * BN), q, lane,
-                                mb * 2 * S::BM + static_cast<int>(rank) * S::BM, nb * BN, it,
-                                abort_flag,
-                                [tempty_leader] { mbar_arrive_cluster(tempty_leader); }))
-        break;
+      const uint32_t acc = tmem_base + static_cast<uint32_t>(b * BN);
+      const int row0 = mb * 2 * S::BM + static_cast<int>(rank) * S::BM;
+      auto release = [tempty_leader] { mbar_arrive_cluster(tempty_leader); };
+      bool done;
+      if (w.split < 0) {
+        done = epilogue_tile<BN, T>(c, acc, q, lane, row0, nb * BN, it, abort_flag, release);
+      } else {
+        const int tail = w.tile - p.dp_tiles;
+        float* const partials = p.partials;
+        const int splits = p.splits;
+        const int r = static_cast<int>(rank);
+        auto part_base = [partials, tail, splits, r](int sp) {
+          return partials + (static_cast<size_t>(tail * splits + sp) * 2 + r) * 128 * BN;
+        };
+        done = epilogue_split<BN, T>(c, acc, q, lane, row0, nb * BN, w.split, splits,
+                                     p.tickets + ((tail * 2 + r) * 4 + q) * 2, part_base, it,
+                                     abort_flag, release);
+      }
+      if (!done) break;
+      if (e == 0 && lane == 0) trace_mark(p, 1 + i);
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
@@ -605,6 +830,7 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
   // No CTA of the pair leaves while the other may still signal it.
   tc_fence_before();
   cluster_sync();
+  if (threadIdx.x == 0) trace_mark(p, kTraceSlots - 1);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc_pair(tmem_base, S::TMEM_COLS);

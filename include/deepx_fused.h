@@ -137,6 +137,15 @@ const char* dx_last_error_string(void);
  * thread: variant, tile shape, pipeline depth, grid ("" if none). */
 const char* dx_last_launch_plan(void);
 
+/* Timeline tracing of the tensor-core GEMM kernels (profiling aid).  With a
+ * device buffer set, every later launch records %globaltimer stamps (ns) per
+ * CTA: 16 uint64 slots per CTA in blockIdx order — slot 0 after set-up,
+ * slot 1+i when work item i's epilogue finished (i < 14), slot 15 at exit.
+ * The buffer must hold 16 * 8 bytes per CTA of the grid (148 SMs: 18,944 B);
+ * launches whose grid does not fit are not traced.  NULL turns tracing off.
+ * Process-wide setting; the caller owns the buffer. */
+int dx_set_trace_buffer(void* device_buffer, size_t bytes);
+
 /* Synchronises `stream`, then reads and clears the calling device's status
  * word (DX_DEVICE_STATUS_* bits) into *status. */
 int dx_device_status(void* stream, int* status);

@@ -216,15 +216,67 @@ def test_nonzero_stream():
     _assert_close(Y, oracle.fused_linear_f64(X, W, b, "relu"), torch.bfloat16, "side stream")
 
 
+def _call_abi(X, W, b, R, act, kernel, workspace):
+    """dx_fused_linear_ex with an explicit workspace (None: whole tiles only)."""
+    lib = nat.load()
+    M, K = X.shape
+    N = W.shape[1]
+    Y = torch.empty(M, N, dtype=X.dtype, device=DEV)
+    ws_ptr = workspace.data_ptr() if workspace is not None else None
+    ws_len = workspace.numel() if workspace is not None else 0
+    rc = lib.dx_fused_linear_ex(X.data_ptr(), W.data_ptr(), b.data_ptr(),
+                                R.data_ptr() if R is not None else None, Y.data_ptr(),
+                                M, N, K, K, N, N if R is not None else 0, N,
+                                nat.DX_DTYPE_BF16 if X.dtype == torch.bfloat16 else nat.DX_DTYPE_F16,
+                                {"gelu": nat.DX_ACT_GELU_TANH, "silu": nat.DX_ACT_SILU}[act],
+                                nat.KERNEL_NAMES[kernel], ws_ptr, ws_len,
+                                torch.cuda.current_stream().cuda_stream)
+    nat.check("dx_fused_linear_ex", rc)
+    return Y, nat.last_launch_plan()
+
+
 @pytest.mark.parametrize("M,N", [(256, 128), (512, 512), (768, 1280), (1280, 384)])
 def test_pair_and_single_cta_agree(M, N):
-    """The CTA-pair and single-CTA tensor-core kernels accumulate in the same
-    k order, so they agree to the last bit."""
+    """Without a workspace (whole tiles only) the CTA-pair and single-CTA
+    kernels accumulate in the same k order, so they agree to the last bit."""
     X, W, b, R = _rand(M, 1024, N, torch.bfloat16, seed=M + N, residual=True)
     Xd, Wd, bd, Rd = X.to(DEV), W.to(DEV), b.to(DEV), R.to(DEV)
-    Y2 = fused_linear(Xd, Wd, bd, "gelu", residual=Rd, kernel="umma")
-    Y1 = fused_linear(Xd, Wd, bd, "gelu", residual=Rd, kernel="umma_1cta")
+    Y2, plan2 = _call_abi(Xd, Wd, bd, Rd, "gelu", "umma", None)
+    Y1, plan1 = _call_abi(Xd, Wd, bd, Rd, "gelu", "umma_1cta", None)
     torch.cuda.synchronize()
+    assert "splits=1" in plan2 and "splits=1" in plan1
     _assert_close(Y2, oracle.fused_linear_f64(X, W, b, "gelu", residual=R), torch.bfloat16,
                   f"pair {M}x{N}")
     assert torch.equal(Y1, Y2)
+
+
+SPLIT_SHAPES = [  # (M, K, N): a partial last wave of tiles, K long enough to split
+    (8192, 4096, 1792), (1024, 4096, 1792), (512, 2048, 640), (300, 1024, 264), (4096, 4096, 4096),
+    (2048, 8192, 1024),
+]
+# Shapes whose plan must split (the planner may prefer whole tiles elsewhere).
+MUST_SPLIT = {(8192, 4096, 1792), (512, 2048, 640), (4096, 4096, 4096)}
+
+
+@pytest.mark.parametrize("kern", ["umma", "umma_1cta"])
+@pytest.mark.parametrize("M,K,N", SPLIT_SHAPES)
+def test_split_tail(M, K, N, kern):
+    """Tiles of the last partial wave are split along K over idle SMs; the
+    partial sums are reduced in fixed order, so results are deterministic and
+    match the oracle."""
+    X, W, b, R = _rand(M, K, N, torch.bfloat16, seed=M + 3 * N, residual=True)
+    Xd, Wd, bd, Rd = X.to(DEV), W.to(DEV), b.to(DEV), R.to(DEV)
+    ws = torch.zeros(nat.load().dx_fused_linear_workspace_size(M, N, K, nat.DX_DTYPE_BF16,
+                                                               nat.KERNEL_NAMES[kern]),
+                     dtype=torch.uint8, device=DEV)
+    Ya, plan = _call_abi(Xd, Wd, bd, Rd, "silu", kern, ws)
+    Yb, _ = _call_abi(Xd, Wd, bd, Rd, "silu", kern, ws)
+    torch.cuda.synchronize()
+    if (M, K, N) in MUST_SPLIT:
+        assert "splits=1 " not in plan, plan
+    ref = oracle.fused_linear_f32(X, W, b, "silu", residual=R) if M * N * K > 2**31 else \
+        oracle.fused_linear_f64(X, W, b, "silu", residual=R)
+    _assert_close(Ya, ref, torch.bfloat16, f"split {M}x{K}x{N} [{kern}] {plan}")
+    assert torch.equal(Ya, Yb), "split reduction is not deterministic"
+    assert int(ws[:65536].view(torch.int32).abs().sum().item()) == 0, "tickets not reset"
+    _status_clean()
