@@ -46,12 +46,11 @@ struct UmmaParams {
   const void* bias;                           // N elements, or nullptr
   int act;
   int has_residual;
-  // Schedule.  Work items are dealt round-robin to `workers` (CTA pairs or
-  // CTAs): first the tiles [0, dp_tiles) whole, then every remaining tile as
-  // `splits` pieces of its K range, so the last partial wave of tiles is
-  // spread over otherwise idle SMs.  Split pieces leave fp32 partial sums in
-  // `partials`; the last piece of a 32-row slab to finish (per-warp ticket)
-  // adds them in split order and runs the epilogue.
+  // Schedule.  The tiles [dp_tiles, num_tiles) that would form a last,
+  // partial wave are cut into `splits` pieces along K, one piece per worker
+  // (CTA pair or CTA) on workers 0..; each worker processes its piece first,
+  // then whole tiles dealt round-robin from [0, dp_tiles).  Pieces leave fp32
+  // partial sums in `partials` and finish the tile cooperatively.
   int workers;
   int dp_tiles;
   int splits;
@@ -75,20 +74,26 @@ struct WorkItem {
 };
 
 __device__ __forceinline__ bool umma_item(const UmmaParams& p, int worker, int i, WorkItem& w) {
-  const long long idx = static_cast<long long>(worker) + static_cast<long long>(i) * p.workers;
-  if (idx < p.dp_tiles) {
-    w.tile = static_cast<int>(idx);
-    w.kb0 = 0;
-    w.kb1 = p.k_blocks;
-    w.split = -1;
-    return true;
+  // Split pieces (at most one per worker) come first, so their partial-sum
+  // traffic and fix-up overlap the whole tiles that follow.
+  const int tail_items = (p.num_tiles - p.dp_tiles) * p.splits;
+  int j = i;
+  if (worker < tail_items) {
+    if (i == 0) {
+      w.tile = p.dp_tiles + worker / p.splits;
+      w.split = worker % p.splits;
+      w.kb0 = static_cast<int>((static_cast<long long>(w.split) * p.k_blocks) / p.splits);
+      w.kb1 = static_cast<int>((static_cast<long long>(w.split + 1) * p.k_blocks) / p.splits);
+      return true;
+    }
+    j = i - 1;
   }
-  const long long j = idx - p.dp_tiles;
-  if (j >= static_cast<long long>(p.num_tiles - p.dp_tiles) * p.splits) return false;
-  w.tile = p.dp_tiles + static_cast<int>(j / p.splits);
-  w.split = static_cast<int>(j % p.splits);
-  w.kb0 = static_cast<int>((static_cast<long long>(w.split) * p.k_blocks) / p.splits);
-  w.kb1 = static_cast<int>((static_cast<long long>(w.split + 1) * p.k_blocks) / p.splits);
+  const long long idx = static_cast<long long>(worker) + static_cast<long long>(j) * p.workers;
+  if (idx >= p.dp_tiles) return false;
+  w.tile = static_cast<int>(idx);
+  w.kb0 = 0;
+  w.kb1 = p.k_blocks;
+  w.split = -1;
   return true;
 }
 
@@ -137,10 +142,30 @@ __device__ __forceinline__ void epi_chunk_begin(const EpilogueCtx<T>& c, int n_c
 // Finishes a 32-column chunk whose fp32 sums are in v: bias, activation,
 // residual, convert, stage (64-byte swizzle) and TMA-store.  Returns false
 // if the residual wait gave up.
+// Bias of one tile, spread over a warp: lane l holds the 8 values
+// bias[n0 + 8l .. n0 + 8l + 8) (zeros past N), loaded before the accumulator
+// is ready so its latency is hidden; chunks fetch theirs by warp shuffle.
+template <typename T>
+__device__ __forceinline__ uint4 epi_load_bias(const EpilogueCtx<T>& c, int n0, int bn, int lane) {
+  using Tr = ElemTraits<T>;
+  uint4 w = make_uint4(0u, 0u, 0u, 0u);
+  const int n = n0 + 8 * lane;
+  if (c.bias == nullptr || 8 * lane >= bn || n >= c.N) return w;
+  if (c.bias_vec_ok && n + 8 <= c.N) return __ldg(reinterpret_cast<const uint4*>(c.bias + n));
+  uint32_t u[4];
+#pragma unroll
+  for (int h = 0; h < 4; ++h) {
+    const float lo = n + 2 * h < c.N ? Tr::to_float(c.bias[n + 2 * h]) : 0.0f;
+    const float hi = n + 2 * h + 1 < c.N ? Tr::to_float(c.bias[n + 2 * h + 1]) : 0.0f;
+    u[h] = Tr::pack2(lo, hi);
+  }
+  return make_uint4(u[0], u[1], u[2], u[3]);
+}
+
 template <typename T>
 __device__ __forceinline__ bool epi_chunk_end(const EpilogueCtx<T>& c, float (&v)[32], int n_c,
                                               int row_base, int lane, uint32_t& it,
-                                              volatile int* abort_flag) {
+                                              volatile int* abort_flag, uint4 bias_reg, int ch) {
   using Tr = ElemTraits<T>;
   const int buf = it & 1;
   const uint32_t ebuf = c.ebuf0 + buf * kEpiBufBytes;
@@ -148,23 +173,19 @@ __device__ __forceinline__ bool epi_chunk_end(const EpilogueCtx<T>& c, float (&v
   const uint32_t row_off = static_cast<uint32_t>(lane) * 64u;
   const uint32_t row_sw = (static_cast<uint32_t>(lane) >> 1) & 3u;  // 64-byte swizzle phase
   if (c.bias != nullptr) {
-    if (c.bias_vec_ok && n_c + 32 <= c.N) {
-      const uint4* bp = reinterpret_cast<const uint4*>(c.bias + n_c);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint4 w = __ldg(bp + j);
-        const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+    for (int j = 0; j < 4; ++j) {
+      const int src = 4 * ch + j;  // lane holding columns n_c + 8j .. n_c + 8j + 8
+      const uint32_t wv[4] = {__shfl_sync(0xffffffffu, bias_reg.x, src),
+                              __shfl_sync(0xffffffffu, bias_reg.y, src),
+                              __shfl_sync(0xffffffffu, bias_reg.z, src),
+                              __shfl_sync(0xffffffffu, bias_reg.w, src)};
 #pragma unroll
-        for (int h = 0; h < 4; ++h) {
-          const float2 f = Tr::unpack2(wv[h]);
-          v[8 * j + 2 * h] += f.x;
-          v[8 * j + 2 * h + 1] += f.y;
-        }
+      for (int h = 0; h < 4; ++h) {
+        const float2 f = Tr::unpack2(wv[h]);
+        v[8 * j + 2 * h] += f.x;
+        v[8 * j + 2 * h + 1] += f.y;
       }
-    } else {
-#pragma unroll
-      for (int j = 0; j < 32; ++j)
-        if (n_c + j < c.N) v[j] += Tr::to_float(c.bias[n_c + j]);
     }
   }
   if (c.act != kActNone) {
@@ -217,31 +238,45 @@ __device__ __forceinline__ bool epi_chunk_end(const EpilogueCtx<T>& c, float (&v
 // Returns false if a bounded wait gave up.
 template <int BN, typename T, typename Release>
 __device__ __forceinline__ bool epilogue_tile(const EpilogueCtx<T>& c, uint32_t tmem_acc, int q,
-                                              int lane, int row0, int n0, uint32_t& it,
-                                              volatile int* abort_flag, Release release) {
+                                              int lane, int row0, int n0, uint4 bias_reg,
+                                              uint32_t& it, volatile int* abort_flag,
+                                              Release release) {
   const int row_base = row0 + q * 32;
   const bool rows_live = row_base < c.M;
+  const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(q * 32) << 16);
+  int n_chunks = 0;  // live chunks: a prefix of the tile's columns
+  if (rows_live) {
+    const int cols = min(BN, c.N - n0);
+    n_chunks = cols > 0 ? (cols + 31) / 32 : 0;
+  }
+  if (n_chunks == 0) {
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) release();
+    return true;
+  }
+  // The TMEM load of chunk ch + 1 is in flight while chunk ch is finished.
+  uint32_t r[32];
+  tmem_ld_32x32b_x32(lane_addr, r);
 #pragma unroll 1
-  for (int ch = 0; ch < BN / 32; ++ch) {
+  for (int ch = 0; ch < n_chunks; ++ch) {
     const int n_c = n0 + 32 * ch;
-    const bool live = rows_live && n_c < c.N;  // warp-uniform
-    if (live) epi_chunk_begin(c, n_c, row_base, lane, it);
-    if (live || ch == BN / 32 - 1) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(tmem_acc + static_cast<uint32_t>(32 * ch) +
-                             (static_cast<uint32_t>(q * 32) << 16),
-                         r);
-      tmem_wait_ld();
-      if (ch == BN / 32 - 1) {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) release();
-      }
-      if (!live) continue;
-      float v[32];
+    epi_chunk_begin(c, n_c, row_base, lane, it);
+    tmem_wait_ld();
+    float v[32];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-      if (!epi_chunk_end(c, v, n_c, row_base, lane, it, abort_flag)) return false;
+    for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
+    if (ch + 1 < n_chunks) {
+      tmem_ld_32x32b_x32(lane_addr + static_cast<uint32_t>(32 * (ch + 1)), r);
+    } else {
+      // Accumulator fully read: hand it back to the MMA issuer.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) release();
+    }
+    if (!epi_chunk_end(c, v, n_c, row_base, lane, it, abort_flag, bias_reg, ch)) {
+      if (ch + 1 < n_chunks) tmem_wait_ld();
+      return false;
     }
   }
   return true;
@@ -274,13 +309,19 @@ __device__ __forceinline__ bool wait_counter(const int* ctr, int target, volatil
 // chunks ch with ch % splits == split — and runs the epilogue on them.  The
 // last piece to leave resets the slab's two counters (`ctr[0]` arrivals,
 // `ctr[1]` departures) to zero.  Returns false if a bounded wait gave up.
+// A slab's partials are stored column-quad-major — float offset
+// ((col / 4) * 32 + row) * 4 + col % 4 — so each warp-wide float4 access
+// covers 512 contiguous bytes.
 template <int BN, typename T, typename Release, typename PartBase>
 __device__ __forceinline__ bool epilogue_split(const EpilogueCtx<T>& c, uint32_t tmem_acc, int q,
-                                               int lane, int row0, int n0, int split, int splits,
-                                               int* ctr, PartBase part_base, uint32_t& it,
+                                               int lane, int row0, int n0, uint4 bias_reg,
+                                               int split, int splits, int* ctr,
+                                               PartBase part_base, uint32_t& it,
                                                volatile int* abort_flag, Release release) {
-  const int row = q * 32 + lane;  // row within this CTA's 128
-  float* const mine = part_base(split) + static_cast<size_t>(row) * BN;
+  const size_t slab = static_cast<size_t>(q) * 32 * BN;  // this warp's 32 rows
+  // float4 index of (column quad j4, this lane's row) within a slab
+  auto quad = [lane](int j4) { return static_cast<size_t>(j4) * 32 + lane; };
+  float4* const mine = reinterpret_cast<float4*>(part_base(split) + slab);
 #pragma unroll 1
   for (int ch = 0; ch < BN / 32; ++ch) {
     uint32_t r[32];
@@ -293,11 +334,11 @@ __device__ __forceinline__ bool epilogue_split(const EpilogueCtx<T>& c, uint32_t
       __syncwarp();
       if (lane == 0) release();
     }
-    float4* dst = reinterpret_cast<float4*>(mine + 32 * ch);
 #pragma unroll
     for (int j = 0; j < 8; ++j)
-      dst[j] = make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
-                           __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
+      mine[quad(8 * ch + j)] =
+          make_float4(__uint_as_float(r[4 * j]), __uint_as_float(r[4 * j + 1]),
+                      __uint_as_float(r[4 * j + 2]), __uint_as_float(r[4 * j + 3]));
   }
   __threadfence();
   __syncwarp();
@@ -320,15 +361,13 @@ __device__ __forceinline__ bool epilogue_split(const EpilogueCtx<T>& c, uint32_t
     // Two splits per step with all 16 loads issued before the adds.
     int sp = 0;
     for (; sp + 1 < splits; sp += 2) {
-      const float4* a =
-          reinterpret_cast<const float4*>(part_base(sp) + static_cast<size_t>(row) * BN + 32 * ch);
-      const float4* b = reinterpret_cast<const float4*>(part_base(sp + 1) +
-                                                        static_cast<size_t>(row) * BN + 32 * ch);
+      const float4* a = reinterpret_cast<const float4*>(part_base(sp) + slab);
+      const float4* b = reinterpret_cast<const float4*>(part_base(sp + 1) + slab);
       float4 fa[8], fb[8];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        fa[j] = __ldcg(a + j);
-        fb[j] = __ldcg(b + j);
+        fa[j] = __ldcg(a + quad(8 * ch + j));
+        fb[j] = __ldcg(b + quad(8 * ch + j));
       }
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
@@ -343,18 +382,17 @@ __device__ __forceinline__ bool epilogue_split(const EpilogueCtx<T>& c, uint32_t
       }
     }
     if (sp < splits) {
-      const float4* a =
-          reinterpret_cast<const float4*>(part_base(sp) + static_cast<size_t>(row) * BN + 32 * ch);
+      const float4* a = reinterpret_cast<const float4*>(part_base(sp) + slab);
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float4 f = __ldcg(a + j);
+        const float4 f = __ldcg(a + quad(8 * ch + j));
         v[4 * j] += f.x;
         v[4 * j + 1] += f.y;
         v[4 * j + 2] += f.z;
         v[4 * j + 3] += f.w;
       }
     }
-    if (!epi_chunk_end(c, v, n_c, row_base, lane, it, abort_flag)) return false;
+    if (!epi_chunk_end(c, v, n_c, row_base, lane, it, abort_flag, bias_reg, ch)) return false;
   }
   __syncwarp();
   if (lane == 0) {
@@ -560,16 +598,18 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
       if (!umma_item(p, blockIdx.x, i, w)) break;
       const int b = local & 1;
       const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
-      if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
-      tc_fence_after();
       int mb, nb;
       umma_tile_coords(p, w.tile, mb, nb);
+      const uint4 bias_reg = epi_load_bias(c, nb * BN, BN, lane);
+      if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
+      tc_fence_after();
       const uint32_t tempty = bar(S::BAR_TEMPTY + b);
       const uint32_t acc = tmem_base + static_cast<uint32_t>(b * BN);
       auto release = [tempty] { mbar_arrive(tempty); };
       bool done;
       if (w.split < 0) {
-        done = epilogue_tile<BN, T>(c, acc, q, lane, mb * S::BM, nb * BN, it, abort_flag, release);
+        done = epilogue_tile<BN, T>(c, acc, q, lane, mb * S::BM, nb * BN, bias_reg, it, abort_flag,
+                                    release);
       } else {
         const int tail = w.tile - p.dp_tiles;
         float* const partials = p.partials;
@@ -577,7 +617,7 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
         auto part_base = [partials, tail, splits](int sp) {
           return partials + static_cast<size_t>(tail * splits + sp) * 128 * BN;
         };
-        done = epilogue_split<BN, T>(c, acc, q, lane, mb * S::BM, nb * BN, w.split, splits,
+        done = epilogue_split<BN, T>(c, acc, q, lane, mb * S::BM, nb * BN, bias_reg, w.split, splits,
                                      p.tickets + (tail * 4 + q) * 2, part_base, it, abort_flag,
                                      release);
       }
@@ -797,17 +837,19 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
       if (!umma_item(p, pair, i, w)) break;
       const int b = local & 1;
       const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
-      if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
-      tc_fence_after();
       int mb, nb;
       umma_tile_coords(p, w.tile, mb, nb);
+      const uint4 bias_reg = epi_load_bias(c, nb * BN, BN, lane);
+      if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
+      tc_fence_after();
       const uint32_t tempty_leader = mapa_shared(bar(S::BAR_TEMPTY + b), 0);
       const uint32_t acc = tmem_base + static_cast<uint32_t>(b * BN);
       const int row0 = mb * 2 * S::BM + static_cast<int>(rank) * S::BM;
       auto release = [tempty_leader] { mbar_arrive_cluster(tempty_leader); };
       bool done;
       if (w.split < 0) {
-        done = epilogue_tile<BN, T>(c, acc, q, lane, row0, nb * BN, it, abort_flag, release);
+        done = epilogue_tile<BN, T>(c, acc, q, lane, row0, nb * BN, bias_reg, it, abort_flag,
+                                    release);
       } else {
         const int tail = w.tile - p.dp_tiles;
         float* const partials = p.partials;
@@ -816,7 +858,7 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
         auto part_base = [partials, tail, splits, r](int sp) {
           return partials + (static_cast<size_t>(tail * splits + sp) * 2 + r) * 128 * BN;
         };
-        done = epilogue_split<BN, T>(c, acc, q, lane, row0, nb * BN, w.split, splits,
+        done = epilogue_split<BN, T>(c, acc, q, lane, row0, nb * BN, bias_reg, w.split, splits,
                                      p.tickets + ((tail * 2 + r) * 4 + q) * 2, part_base, it,
                                      abort_flag, release);
       }

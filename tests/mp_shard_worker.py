@@ -32,12 +32,15 @@ def main() -> int:
         X = torch.randn(M, K, generator=g, device=dev).bfloat16()
         W = (torch.randn(K, N, generator=g, device=dev) / K ** 0.5).bfloat16()
         b = (torch.rand(N, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
-        full = fused_linear(X, W, b, "silu")
+        full = fused_linear(X, W, b, "silu").float()
         col = ColumnParallelLinear(W, b, "silu", gather_output=True)
-        got = col(X)
+        got = col(X).float()
         torch.cuda.synchronize()
-        if not torch.equal(got, full):
-            failures.append(f"column-parallel differs: max {(got.float() - full.float()).abs().max()}")
+        # A shard may be scheduled with a different K split of its last tiles
+        # than the full problem, so compare within the bf16 tolerance.
+        err = (got - full).abs()
+        if bool((err > 2e-2 + 2e-2 * full.abs()).any()):
+            failures.append(f"column-parallel differs: max {err.max().item():.4g}")
 
         H = 4096
         W1 = (torch.randn(K, H, generator=g, device=dev) / K ** 0.5).bfloat16()
