@@ -154,6 +154,7 @@ struct Problem {
 
 // ----------------------------------------------------------- decode plan
 constexpr int kDecodeMaxM = 64;
+constexpr int kDecodeTileN = 256;  // W columns per decode work unit
 // Tickets live in a fixed slab at the start of every decode workspace, so the
 // partial sums of one problem never overlap the tickets of another problem
 // that reuses the same workspace later; the kernel leaves the slab zeroed.
@@ -177,10 +178,10 @@ struct DecodePlan {
 DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sms) {
   DecodePlan d;
   d.mn = decode_mn(M);
-  d.n_tiles = static_cast<int>((N + 127) / 128);
+  d.n_tiles = static_cast<int>((N + kDecodeTileN - 1) / kDecodeTileN);
   d.kbt = static_cast<int>((K + 63) / 64);
   d.units = static_cast<long long>(d.n_tiles) * d.kbt;
-  const long long want = 2LL * sms;
+  const long long want = sms;  // one CTA per SM
   d.grid = static_cast<int>(std::max<long long>(1, std::min<long long>(d.units, want)));
   int ms = 1;
   for (int t = 0; t < d.n_tiles; ++t) {
@@ -192,7 +193,7 @@ DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sms) {
   d.max_seg = ms;
   d.ticket_bytes = kTicketSlabBytes;
   d.bytes = d.ticket_bytes +
-            static_cast<size_t>(d.n_tiles) * d.max_seg * d.mn * 128 * sizeof(float);
+            static_cast<size_t>(d.n_tiles) * d.max_seg * d.mn * kDecodeTileN * sizeof(float);
   return d;
 }
 
@@ -520,7 +521,7 @@ bool umma_eligible(const Problem& p) {
 
 bool decode_eligible(const Problem& p) {
   if (p.dtype == DX_DTYPE_F32 || p.K == 0 || p.M > kDecodeMaxM) return false;
-  if ((p.N + 127) / 128 > kDecodeMaxTiles) return false;
+  if ((p.N + kDecodeTileN - 1) / kDecodeTileN > kDecodeMaxTiles) return false;
   return tma_ok(p.X, p.ldx) && tma_ok(p.W, p.ldw);
 }
 
@@ -591,7 +592,7 @@ int run(const Problem& p, int kernel) {
       return fail(DX_ERR_UNSUPPORTED,
                   "decode kernel needs fp16/bf16, 0 < K, M <= %d, N <= %lld, and "
                   "16-byte-aligned X/W with row pitches that are multiples of 16 bytes",
-                  kDecodeMaxM, (long long)(kDecodeMaxTiles * 128));
+                  kDecodeMaxM, (long long)(kDecodeMaxTiles * kDecodeTileN));
     const DecodePlan d = decode_plan(p.M, p.N, p.K, sms);
     if (p.ws == nullptr || p.ws_bytes < d.bytes || !aligned16(p.ws))
       return fail(DX_ERR_WORKSPACE, "decode kernel needs a 16-byte-aligned workspace of %zu bytes",
@@ -637,7 +638,7 @@ size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K, int dtype
   if (cudaGetDevice(&dev) != cudaSuccess || device_sms(dev, &sms) != DX_OK) return 0;
   if (kernel == DX_KERNEL_AUTO) kernel = dx_select_kernel(M, N, K, dtype);
   if (kernel == DX_KERNEL_DECODE) {
-    if (M > kDecodeMaxM || (N + 127) / 128 > kDecodeMaxTiles) return 0;
+    if (M > kDecodeMaxM || (N + kDecodeTileN - 1) / kDecodeTileN > kDecodeMaxTiles) return 0;
     return decode_plan(M, N, K, sms).bytes;
   }
   if (kernel == DX_KERNEL_UMMA || kernel == DX_KERNEL_UMMA_1CTA) {
@@ -651,7 +652,7 @@ size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K, int dtype
 int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype) {
   if (dtype == DX_DTYPE_F32 || K <= 0) return DX_KERNEL_SIMT;
   if ((K * 2) % 16 != 0 || (N * 2) % 16 != 0) return DX_KERNEL_SIMT;
-  if (M <= kDecodeMaxM && (N + 127) / 128 <= kDecodeMaxTiles) return DX_KERNEL_DECODE;
+  if (M <= kDecodeMaxM && (N + kDecodeTileN - 1) / kDecodeTileN <= kDecodeMaxTiles) return DX_KERNEL_DECODE;
   return DX_KERNEL_UMMA;
 }
 

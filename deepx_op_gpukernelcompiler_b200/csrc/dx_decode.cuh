@@ -7,10 +7,14 @@
 //     the 128-wide UMMA M dimension runs over N (W's contiguous axis, read
 //     by TMA straight from its row-major layout as an MN-major operand) and
 //     the UMMA N dimension is the padded batch MN = 16/32/64 (X as a K-major
-//     operand).  D lives in TMEM: 128 lanes x MN fp32 columns.
+//     operand).  A work unit is 256 columns of W by 64 rows of K: two UMMAs
+//     (one per 128-column half) per K=16 step into two TMEM accumulators of
+//     128 lanes x MN fp32 columns.  Each W row segment read is 512 B long and
+//     each 2 KB X tile serves 32 KB of W.
 //   * split-K with an even partition of the (n-tile, k-block) work units
-//     over all CTAs (2 per SM), so every SM streams the same number of bytes
-//     regardless of N/K; a CTA's range crosses at most a few n-tiles.
+//     over all CTAs (one per SM, deep pipeline), so every SM streams the
+//     same number of bytes regardless of N/K; a CTA's range crosses at most
+//     a few n-tiles.
 //   * partial sums of a tile that several CTAs share go to a workspace as
 //     fp32; the last CTA to finish a tile (atomic ticket) sums the partials
 //     in fixed segment order — deterministic, no float atomics — applies
@@ -25,7 +29,7 @@ namespace dx {
 
 struct DecodeParams {
   int M, N, K;
-  int n_tiles;          // ceil(N / 128)
+  int n_tiles;          // ceil(N / 256)
   int kbt;              // k-blocks (64 deep) per tile
   long long units;      // n_tiles * kbt
   int grid;             // CTAs
@@ -34,20 +38,24 @@ struct DecodeParams {
   const void* bias;     // N elements or nullptr
   const void* residual; // [M, N] (ldr) or nullptr
   void* Y;
-  float* partials;      // [n_tiles][max_seg][MN][128] fp32
+  float* partials;      // [n_tiles][max_seg][MN][256] fp32
   int* tickets;         // [n_tiles][4] (per warp quarter), zero between calls
   int act;
 };
 
 template <int MN>
 struct DecodeShape {
+  static constexpr int NT = 256;                   // W columns per work unit
   static constexpr int BK = 64;
   static constexpr int W_BOX_BYTES = 64 * BK * 2;  // [64 k x 64 n]
-  static constexpr int W_BYTES = 2 * W_BOX_BYTES;  // 128 n per stage
+  static constexpr int W_BYTES = 4 * W_BOX_BYTES;  // 256 n per stage
+  static constexpr int HALF_BYTES = 2 * W_BOX_BYTES;
   static constexpr int X_BYTES = MN * BK * 2;      // MN rows x 128 B
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
-  static constexpr int STAGES = MN <= 16 ? 6 : (MN <= 32 ? 5 : 4);
-  static constexpr int TMEM_COLS = (2 * MN < 32) ? 32 : 2 * MN;
+  static constexpr int STAGES = MN <= 32 ? 6 : 5;
+  // two buffers x two halves x MN fp32 columns, as a power of two >= 32
+  static constexpr int ACC_COLS = 2 * MN;
+  static constexpr int TMEM_COLS = 4 * MN < 32 ? 32 : 4 * MN;
   static constexpr int THREADS = 192;
   static constexpr int OFF_W = 0;
   static constexpr int OFF_X = OFF_W + STAGES * W_BYTES;
@@ -62,6 +70,7 @@ struct DecodeShape {
   static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 16;
   static_assert(MN == 16 || MN == 32 || MN == 64, "decode batch tile");
   static_assert(X_BYTES % 1024 == 0, "X stage alignment");
+  static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
 
 // CTA whose work range holds unit u (ranges are [g*U/G, (g+1)*U/G)).
@@ -72,7 +81,7 @@ __device__ __forceinline__ int decode_cta_of(long long u, long long U, int G) {
 }
 
 template <int MN, typename T>
-__global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 2)
+__global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
     decode_fused_linear_kernel(const __grid_constant__ CUtensorMap tmW,
                                const __grid_constant__ CUtensorMap tmX, const DecodeParams p) {
   using S = DecodeShape<MN>;
@@ -139,8 +148,10 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 2)
           }
           const uint32_t fb = bar(S::BAR_FULL + s);
           mbar_arrive_expect_tx(fb, S::STAGE_BYTES);
-          tma_load_2d(&tmW, sW + s * S::W_BYTES, fb, t * 128, kb * S::BK);
-          tma_load_2d(&tmW, sW + s * S::W_BYTES + S::W_BOX_BYTES, fb, t * 128 + 64, kb * S::BK);
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tma_load_2d(&tmW, sW + s * S::W_BYTES + j * S::W_BOX_BYTES, fb, t * S::NT + 64 * j,
+                        kb * S::BK);
           tma_load_2d(&tmX, sX + s * S::X_BYTES, fb, kb * S::BK, 0);
           ++issued;
           if (++s == S::STAGES) {
@@ -171,22 +182,26 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 2)
         const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
         if (!mbar_wait(bar(S::BAR_TEMPTY + b), use_ph ^ 1u, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * MN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(b * S::ACC_COLS);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(bar(S::BAR_FULL + s), ph, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          // W^T tile: MN-major (n contiguous), two 64-wide n groups one box
-          // apart, 8-row k groups 1024 B apart; +2048 B per K=16 step.
-          const uint64_t ad = smem_desc_sw128(sW + s * S::W_BYTES, S::W_BOX_BYTES, 1024);
           // X tile: K-major rows of 128 B, 8-row groups 1024 B apart.
           const uint64_t bd = smem_desc_sw128(sX + s * S::X_BYTES, 16, 1024);
 #pragma unroll
-          for (int k = 0; k < S::BK / 16; ++k)
-            umma_f16(d_tmem, ad + 128ull * k, bd + 2ull * k, idesc,
-                     (kb != kb0 || k != 0) ? 1u : 0u);
+          for (int h = 0; h < 2; ++h) {
+            // W^T half: MN-major (n contiguous), two 64-wide n groups one box
+            // apart, 8-row k groups 1024 B apart; +2048 B per K=16 step.
+            const uint64_t ad =
+                smem_desc_sw128(sW + s * S::W_BYTES + h * S::HALF_BYTES, S::W_BOX_BYTES, 1024);
+#pragma unroll
+            for (int k = 0; k < S::BK / 16; ++k)
+              umma_f16(d_tmem + static_cast<uint32_t>(h * MN), ad + 128ull * k, bd + 2ull * k,
+                       idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+          }
           umma_commit(bar(S::BAR_EMPTY + s));
           if (++s == S::STAGES) {
             s = 0;
@@ -217,23 +232,26 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 2)
       const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
       if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
       tc_fence_after();
-      float acc[MN];
-      const uint32_t taddr =
-          tmem_base + static_cast<uint32_t>(b * MN) + (static_cast<uint32_t>(q * 32) << 16);
-      if constexpr (MN == 16) {
-        uint32_t r[16];
-        tmem_ld_32x32b_x16(taddr, r);
-        tmem_wait_ld();
+      float acc[2][MN];
 #pragma unroll
-        for (int j = 0; j < 16; ++j) acc[j] = __uint_as_float(r[j]);
-      } else {
-#pragma unroll
-        for (int h = 0; h < MN / 32; ++h) {
-          uint32_t r[32];
-          tmem_ld_32x32b_x32(taddr + 32u * h, r);
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t taddr = tmem_base + static_cast<uint32_t>(b * S::ACC_COLS + h * MN) +
+                               (static_cast<uint32_t>(q * 32) << 16);
+        if constexpr (MN == 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(taddr, r);
           tmem_wait_ld();
 #pragma unroll
-          for (int j = 0; j < 32; ++j) acc[32 * h + j] = __uint_as_float(r[j]);
+          for (int j = 0; j < 16; ++j) acc[h][j] = __uint_as_float(r[j]);
+        } else {
+#pragma unroll
+          for (int c = 0; c < MN / 32; ++c) {
+            uint32_t r[32];
+            tmem_ld_32x32b_x32(taddr + 32u * c, r);
+            tmem_wait_ld();
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[h][32 * c + j] = __uint_as_float(r[j]);
+          }
         }
       }
       tc_fence_before();
@@ -241,18 +259,21 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 2)
       if (lane == 0) mbar_arrive(bar(S::BAR_TEMPTY + b));
 
       if (!(kb0 == 0 && kb1 == p.kbt)) {
-        // Tile shared with other CTAs: publish this segment's partial sums.
+        // Tile shared with other CTAs: publish this segment's partial sums
+        // ([MN][256] fp32, lanes contiguous in n).
         const int first = decode_cta_of(static_cast<long long>(t) * p.kbt, U, p.grid);
         const int last = decode_cta_of(static_cast<long long>(t + 1) * p.kbt - 1, U, p.grid);
         const int nseg = last - first + 1;
-        float* const part_t = p.partials + static_cast<size_t>(t) * p.max_seg * MN * 128;
-        float* const mine = part_t + static_cast<size_t>(g - first) * MN * 128;
+        float* const part_t = p.partials + static_cast<size_t>(t) * p.max_seg * MN * S::NT;
+        float* const mine = part_t + static_cast<size_t>(g - first) * MN * S::NT;
 #pragma unroll
-        for (int m = 0; m < MN; ++m)
-          if (m < M) mine[m * 128 + n_local] = acc[m];
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int m = 0; m < MN; ++m)
+            if (m < M) mine[m * S::NT + h * 128 + n_local] = acc[h][m];
         __threadfence();
         __syncwarp();
-        // One ticket per (tile, warp quarter): each warp finishes its own 32
+        // One ticket per (tile, warp quarter): each warp finishes its own 2 x 32
         // columns, so no cross-warp barrier can be left waiting on an exit.
         int ticket = 0;
         if (lane == 0) ticket = atomicAdd(p.tickets + t * 4 + q, 1);
@@ -260,26 +281,39 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 2)
         if (ticket != nseg - 1) continue;
         __threadfence();
         // Fixed summation order over segments: bitwise identical results
-        // whichever CTA finishes last.
+        // whichever CTA finishes last.  All loads of a segment are issued
+        // before they are added.
 #pragma unroll
-        for (int m = 0; m < MN; ++m) acc[m] = 0.0f;
+        for (int h = 0; h < 2; ++h)
+#pragma unroll
+          for (int m = 0; m < MN; ++m) acc[h][m] = 0.0f;
         for (int sg = 0; sg < nseg; ++sg) {
-          const float* src = part_t + static_cast<size_t>(sg) * MN * 128;
+          const float* src = part_t + static_cast<size_t>(sg) * MN * S::NT;
+          float f[2][MN];
 #pragma unroll
-          for (int m = 0; m < MN; ++m)
-            if (m < M) acc[m] += __ldcg(src + m * 128 + n_local);
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int m = 0; m < MN; ++m)
+              f[h][m] = m < M ? __ldcg(src + m * S::NT + h * 128 + n_local) : 0.0f;
+#pragma unroll
+          for (int h = 0; h < 2; ++h)
+#pragma unroll
+            for (int m = 0; m < MN; ++m) acc[h][m] += f[h][m];
         }
         if (lane == 0) p.tickets[t * 4 + q] = 0;
       }
-      const int n = t * 128 + n_local;
-      if (n < p.N) {
-        const float bv = bias != nullptr ? Tr::to_float(bias[n]) : 0.0f;
 #pragma unroll
-        for (int m = 0; m < MN; ++m) {
-          if (m < M) {
-            float y = act_apply(acc[m] + bv, p.act);
-            if (res != nullptr) y += Tr::to_float(res[m * p.ldr + n]);
-            Y[m * p.ldy + n] = Tr::from_float(y);
+      for (int h = 0; h < 2; ++h) {
+        const int n = t * S::NT + h * 128 + n_local;
+        if (n < p.N) {
+          const float bv = bias != nullptr ? Tr::to_float(bias[n]) : 0.0f;
+#pragma unroll
+          for (int m = 0; m < MN; ++m) {
+            if (m < M) {
+              float y = act_apply(acc[h][m] + bv, p.act);
+              if (res != nullptr) y += Tr::to_float(res[m * p.ldr + n]);
+              Y[m * p.ldy + n] = Tr::from_float(y);
+            }
           }
         }
       }

@@ -69,7 +69,7 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
-    # 512 n-tiles of 64 padded rows: 16 MiB of partial sums > the 8 MiB array.
+    # 64 padded rows x 65536 columns of partial sums: 16 MiB > the 8 MiB array.
     X, W, b, _ = _inputs(64, 64, 65536, torch.float16, 3)
     Y = torch.empty(64, 65536, dtype=torch.float16, device=DEV)
     rc = nat.load().dx_fused_linear_decode_noalloc(
