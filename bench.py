@@ -521,8 +521,8 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
     H = torch.empty(w.M, h_loc, dtype=dt, device=dev)
     Yo = torch.empty(w.M, w.K, dtype=dt, device=dev)
     if world > 1:
-        mlp = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, chunks=4)
-        run = lambda: mlp(X, hidden=H, out=Yo)  # noqa: E731
+        mlp = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, mode="fused")
+        run = lambda: mlp(X, hidden=H)  # noqa: E731
     else:
         from deepx_op_gpukernelcompiler_b200 import mlp_residual
         run = lambda: mlp_residual(X, W1, b1, W2, b2, w.act, hidden=H, out=Yo)  # noqa: E731
@@ -536,8 +536,23 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
     tf = w.flops / (ms * 1e-3) / 1e12
     out[w.name] = {"value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
                    "frac_of_peak": round(tf / world / tflops_peak, 4),
-                   "parallelism": f"column->row x{world}" + (" + NCCL all-reduce" if world > 1 else ""),
-                   "gpu_launches_per_step": 2 if world == 1 else 1 + 4}
+                   "parallelism": f"column->row x{world}" + (
+                       " + NVLink reduce-broadcast (symmetric memory)" if world > 1 else ""),
+                   "gpu_launches_per_step": 2 if world == 1 else 3}
+    if world > 1:
+        # The same chain with an NCCL all-reduce of Y in 4 asynchronous chunks.
+        mlp_n = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, chunks=4, mode="nccl")
+        run_n = lambda: mlp_n(X, hidden=H, out=Yo)  # noqa: E731
+        for _ in range(3):
+            run_n()
+        torch.cuda.synchronize()
+        _barrier(world)
+        t = _time_launches(run_n, msteps, flush, stream)
+        ms = _max_over_ranks(sum(t), world, dev) / msteps
+        tf = w.flops / (ms * 1e-3) / 1e12
+        out[w.name + "_nccl"] = {"value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+                                 "frac_of_peak": round(tf / world / tflops_peak, 4),
+                                 "parallelism": f"column->row x{world} + NCCL all-reduce (4 chunks)"}
     return out
 
 

@@ -61,6 +61,10 @@ SIGNATURES = {
     "dx_fused_linear": (ctypes.c_int, _LINEAR_ARGS + [_vp, ctypes.c_size_t, _vp]),
     "dx_fused_linear_ex": (ctypes.c_int, _LINEAR_ARGS + [ctypes.c_int, _vp, ctypes.c_size_t, _vp]),
     "dx_fused_linear_decode_noalloc": (ctypes.c_int, _LINEAR_ARGS + [_vp]),
+    "dx_reduce_broadcast": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), ctypes.c_int,
+                                           ctypes.c_int, _i64, _i64, _i64, _vp, _vp, _i64,
+                                           ctypes.POINTER(ctypes.c_void_p), _i64, ctypes.c_int,
+                                           _vp]),
     "dx_fused_linear_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, ctypes.c_int, ctypes.c_int]),
     "dx_select_kernel": (ctypes.c_int, [_i64, _i64, _i64, ctypes.c_int]),
     "dx_last_error_string": (ctypes.c_char_p, []),
@@ -68,6 +72,13 @@ SIGNATURES = {
     "dx_set_trace_buffer": (ctypes.c_int, [_vp, ctypes.c_size_t]),
     "dx_device_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int)]),
     "dx_version": (ctypes.c_int, []),
+    "dx_plan_create": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), _i64, _i64, _i64,
+                                      ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int]),
+    "dx_plan_workspace_size": (ctypes.c_size_t, [_vp]),
+    "dx_plan_set_workspace": (ctypes.c_int, [_vp, _vp, ctypes.c_size_t]),
+    "dx_plan_call": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp]),
+    "dx_plan_call_residual": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
+    "dx_plan_destroy": (ctypes.c_int, [_vp]),
 }
 
 _lock = threading.Lock()

@@ -19,10 +19,12 @@
 #include <cstring>
 #include <map>
 #include <mutex>
+#include <new>
 #include <string>
 #include <utility>
 
 #include "deepx_fused.h"
+#include "dx_collective.cuh"
 #include "dx_decode.cuh"
 #include "dx_epilogue.cuh"
 #include "dx_ptx.cuh"
@@ -150,6 +152,7 @@ struct Problem {
   void* ws;
   size_t ws_bytes;
   cudaStream_t stream;
+  float alpha = 1.0f;  // Y = act(alpha * X W + bias) + R
 };
 
 // ----------------------------------------------------------- decode plan
@@ -310,6 +313,7 @@ UmmaParams umma_params(const Problem& pr, const UmmaPlan& pl) {
   p.bias = pr.bias;
   p.act = pr.act;
   p.has_residual = pr.R != nullptr ? 1 : 0;
+  p.alpha = pr.alpha;
   p.workers = pl.workers;
   p.dp_tiles = pl.dp_tiles;
   p.splits = pl.splits;
@@ -447,6 +451,7 @@ int launch_decode(const Problem& pr, int dev, int sms, const DecodePlan& d) {
   p.tickets = static_cast<int*>(pr.ws);
   p.partials = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + d.ticket_bytes);
   p.act = pr.act;
+  p.alpha = pr.alpha;
   (void)sms;
   set_plan("decode mn=%d stages=%d grid=%d n_tiles=%d kbt=%d max_seg=%d workspace=%zu", MN,
            S::STAGES, d.grid, d.n_tiles, d.kbt, d.max_seg, d.bytes);
@@ -471,12 +476,12 @@ int launch_simt(const Problem& pr, int sms) {
     if ((pr.M + 63) / 64 > 65535) return fail(DX_ERR_UNSUPPORTED, "M too large for the SIMT kernel");
     dim3 grid(static_cast<unsigned>((pr.N + 63) / 64), static_cast<unsigned>((pr.M + 63) / 64));
     dx::simt_fused_linear_kernel<T, 64, 64><<<grid, 256, 0, pr.stream>>>(
-        X, W, b, R, Y, M, N, K, pr.ldx, pr.ldw, pr.ldr, pr.ldy, pr.act);
+        X, W, b, R, Y, M, N, K, pr.ldx, pr.ldw, pr.ldr, pr.ldy, pr.act, pr.alpha);
   } else {
     if ((pr.M + 31) / 32 > 65535) return fail(DX_ERR_UNSUPPORTED, "M too large for the SIMT kernel");
     dim3 grid(static_cast<unsigned>((pr.N + 31) / 32), static_cast<unsigned>((pr.M + 31) / 32));
     dx::simt_fused_linear_kernel<T, 32, 32><<<grid, 256, 0, pr.stream>>>(
-        X, W, b, R, Y, M, N, K, pr.ldx, pr.ldw, pr.ldr, pr.ldy, pr.act);
+        X, W, b, R, Y, M, N, K, pr.ldx, pr.ldw, pr.ldr, pr.ldy, pr.act, pr.alpha);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch simt_fused_linear_kernel");
@@ -654,6 +659,119 @@ int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype) {
   if ((K * 2) % 16 != 0 || (N * 2) % 16 != 0) return DX_KERNEL_SIMT;
   if (M <= kDecodeMaxM && (N + kDecodeTileN - 1) / kDecodeTileN <= kDecodeMaxTiles) return DX_KERNEL_DECODE;
   return DX_KERNEL_UMMA;
+}
+
+int dx_reduce_broadcast(void* const* P, int world, int rank, int64_t rows_per_rank, int64_t N,
+                        int64_t ldp, const void* bias, const void* R, int64_t ldr,
+                        void* const* Y, int64_t ldy, int dtype, void* stream) {
+  t_last_error.clear();
+  if (P == nullptr || Y == nullptr || world < 1 || world > 8 || rank < 0 || rank >= world)
+    return fail(DX_ERR_INVALID_ARGUMENT, "reduce_broadcast: bad P/Y/world/rank");
+  if (dtype != DX_DTYPE_F16 && dtype != DX_DTYPE_BF16)
+    return fail(DX_ERR_UNSUPPORTED, "reduce_broadcast supports fp16/bf16");
+  if (rows_per_rank <= 0 || N <= 0 || N % 8 != 0 || ldp < N || ldy < N || ldp % 8 != 0 ||
+      ldy % 8 != 0 || (R != nullptr && (ldr < N || ldr % 8 != 0)))
+    return fail(DX_ERR_INVALID_ARGUMENT, "reduce_broadcast needs N %% 8 == 0 and pitches >= N, "
+                "multiples of 8");
+  if ((bias != nullptr && !aligned16(bias)) || (R != nullptr && !aligned16(R)))
+    return fail(DX_ERR_INVALID_ARGUMENT, "reduce_broadcast needs 16-byte-aligned buffers");
+  dx::RankPtrs pp{}, yp{};
+  for (int r = 0; r < world; ++r) {
+    if (P[r] == nullptr || !aligned16(P[r]) || Y[r] == nullptr || !aligned16(Y[r]))
+      return fail(DX_ERR_INVALID_ARGUMENT, "buffer of rank %d is NULL or not 16-byte aligned", r);
+    pp.p[r] = P[r];
+    yp.p[r] = Y[r];
+  }
+  int dev = 0, sms = 0, rc;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if ((rc = device_sms(dev, &sms))) return rc;
+  const long long work = rows_per_rank * (N / 8);
+  const int grid = static_cast<int>(std::max<long long>(
+      1, std::min<long long>((work + 255) / 256, 4LL * sms)));
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  set_plan("reduce_broadcast world=%d rows=%lld N=%lld grid=%d", world, (long long)rows_per_rank,
+           (long long)N, grid);
+  if (dtype == DX_DTYPE_F16)
+    dx::reduce_broadcast_kernel<__half><<<grid, 256, 0, s>>>(
+        pp, world, rank, static_cast<int>(rows_per_rank), static_cast<int>(N), ldp,
+        static_cast<const __half*>(bias), static_cast<const __half*>(R), ldr, yp, ldy);
+  else
+    dx::reduce_broadcast_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>(
+        pp, world, rank, static_cast<int>(rows_per_rank), static_cast<int>(N), ldp,
+        static_cast<const __nv_bfloat16*>(bias), static_cast<const __nv_bfloat16*>(R), ldr, yp,
+        ldy);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch reduce_broadcast_kernel");
+  return DX_OK;
+}
+
+// ------------------------------------------------------------- plans
+// A plan fixes everything the reference's compile step fixes (shape, dtype,
+// op sequence; doc/kvlang-to-tilelang-interface.md:60-77) so that a call
+// needs only the docs' runtime arguments: pointers and a stream.
+struct dx_plan {
+  int64_t M, N, K;
+  int dtype, act, kernel;
+  float alpha;
+  void* ws;
+  size_t ws_bytes;
+};
+
+int dx_plan_create(dx_plan** out, int64_t M, int64_t N, int64_t K, int dtype, int act, float alpha,
+                   int kernel) {
+  t_last_error.clear();
+  if (out == nullptr) return fail(DX_ERR_INVALID_ARGUMENT, "plan output pointer is NULL");
+  *out = nullptr;
+  Problem probe{nullptr, nullptr, nullptr, nullptr, nullptr, M, N, K, std::max<int64_t>(K, 1), N,
+                0, N, dtype, act, nullptr, 0, nullptr};
+  // Shape/enum checks only (pointers are supplied per call).
+  if (M < 0 || N < 0 || K < 0)
+    return fail(DX_ERR_INVALID_ARGUMENT, "negative shape M=%lld N=%lld K=%lld", (long long)M,
+                (long long)N, (long long)K);
+  probe.M = 0;  // skip the pointer checks of validate()
+  int rc = validate(probe, kernel);
+  if (rc) return rc;
+  if (M > 0x7fffffffLL || N > 0x7fffffffLL || K > 0x7fffffffLL)
+    return fail(DX_ERR_UNSUPPORTED, "dimension above 2^31-1");
+  dx_plan* pl = new (std::nothrow) dx_plan{M, N, K, dtype, act, kernel, alpha, nullptr, 0};
+  if (pl == nullptr) return fail(DX_ERR_UNSUPPORTED, "out of host memory");
+  *out = pl;
+  return DX_OK;
+}
+
+size_t dx_plan_workspace_size(const dx_plan* plan) {
+  if (plan == nullptr) return 0;
+  return dx_fused_linear_workspace_size(plan->M, plan->N, plan->K, plan->dtype, plan->kernel);
+}
+
+int dx_plan_set_workspace(dx_plan* plan, void* workspace, size_t bytes) {
+  t_last_error.clear();
+  if (plan == nullptr) return fail(DX_ERR_INVALID_ARGUMENT, "plan is NULL");
+  plan->ws = workspace;
+  plan->ws_bytes = workspace != nullptr ? bytes : 0;
+  return DX_OK;
+}
+
+int dx_plan_call_residual(const dx_plan* plan, const void* x, const void* W, const void* b,
+                          const void* r, void* out, void* stream) {
+  t_last_error.clear();
+  if (plan == nullptr) return fail(DX_ERR_INVALID_ARGUMENT, "plan is NULL");
+  Problem p{x,          W,           b, r,        out, plan->M, plan->N, plan->K,
+            std::max<int64_t>(plan->K, 1), plan->N, plan->N, plan->N, plan->dtype, plan->act,
+            plan->ws,   plan->ws_bytes, static_cast<cudaStream_t>(stream)};
+  p.alpha = plan->alpha;
+  return run(p, plan->kernel);
+}
+
+int dx_plan_call(const dx_plan* plan, const void* x, const void* W, const void* b, void* out,
+                 void* stream) {
+  return dx_plan_call_residual(plan, x, W, b, nullptr, out, stream);
+}
+
+int dx_plan_destroy(dx_plan* plan) {
+  delete plan;
+  return DX_OK;
 }
 
 const char* dx_last_error_string(void) { return t_last_error.c_str(); }

@@ -41,6 +41,7 @@ struct DecodeParams {
   float* partials;      // [n_tiles][max_seg][MN][256] fp32
   int* tickets;         // [n_tiles][4] (per warp quarter), zero between calls
   int act;
+  float alpha;          // Y = act(alpha * acc + bias) + R
 };
 
 template <int MN>
@@ -310,7 +311,7 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
 #pragma unroll
           for (int m = 0; m < MN; ++m) {
             if (m < M) {
-              float y = act_apply(acc[h][m] + bv, p.act);
+              float y = act_apply(fmaf(p.alpha, acc[h][m], bv), p.act);
               if (res != nullptr) y += Tr::to_float(res[m * p.ldr + n]);
               Y[m * p.ldy + n] = Tr::from_float(y);
             }

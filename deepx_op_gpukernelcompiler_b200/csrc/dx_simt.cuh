@@ -21,7 +21,7 @@ __global__ void __launch_bounds__(256)
     simt_fused_linear_kernel(const T* __restrict__ X, const T* __restrict__ W,
                              const T* __restrict__ bias, const T* __restrict__ R,
                              T* __restrict__ Y, int M, int N, int K, long long ldx, long long ldw,
-                             long long ldr, long long ldy, int act) {
+                             long long ldr, long long ldy, int act, float alpha) {
   using Tr = ElemTraits<T>;
   constexpr int BK = 16;
   constexpr int TM = BM / 16;
@@ -74,7 +74,7 @@ __global__ void __launch_bounds__(256)
     for (int j = 0; j < TN; ++j) {
       const int n = n0 + tx + 16 * j;
       if (n >= N) continue;
-      float v = acc[i][j];
+      float v = alpha == 1.0f ? acc[i][j] : alpha * acc[i][j];
       if (bias != nullptr) v += Tr::to_float(bias[n]);
       v = act_apply<!std::is_same<T, float>::value>(v, act);
       if (R != nullptr) v += Tr::to_float(R[m * ldr + n]);

@@ -46,6 +46,7 @@ struct UmmaParams {
   const void* bias;                           // N elements, or nullptr
   int act;
   int has_residual;
+  float alpha;                                // Y = act(alpha * acc + bias) + R
   // Schedule.  The tiles [dp_tiles, num_tiles) that would form a last,
   // partial wave are cut into `splits` pieces along K, one piece per worker
   // (CTA pair or CTA) on workers 0..; each worker processes its piece first,
@@ -118,6 +119,7 @@ struct EpilogueCtx {
   const T* bias;
   bool bias_vec_ok;
   int M, N, act, has_residual;
+  float alpha;
   uint32_t ebuf0;      // this warp's two staging buffers (shared address)
   uint8_t* ebuf_ptr0;  // same, generic pointer
   uint32_t rbar0;      // this warp's two residual-load barriers (8 B apart)
@@ -172,6 +174,10 @@ __device__ __forceinline__ bool epi_chunk_end(const EpilogueCtx<T>& c, float (&v
   uint8_t* const ebp = c.ebuf_ptr0 + buf * kEpiBufBytes;
   const uint32_t row_off = static_cast<uint32_t>(lane) * 64u;
   const uint32_t row_sw = (static_cast<uint32_t>(lane) >> 1) & 3u;  // 64-byte swizzle phase
+  if (c.alpha != 1.0f) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] *= c.alpha;
+  }
   if (c.bias != nullptr) {
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -586,6 +592,7 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
     c.M = p.M;
     c.N = p.N;
     c.act = p.act;
+    c.alpha = p.alpha;
     c.has_residual = p.has_residual;
     c.ebuf0 = base + S::OFF_EPI + e * 2 * kEpiBufBytes;
     c.ebuf_ptr0 = base_ptr + S::OFF_EPI + e * 2 * kEpiBufBytes;
@@ -825,6 +832,7 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
     c.M = p.M;
     c.N = p.N;
     c.act = p.act;
+    c.alpha = p.alpha;
     c.has_residual = p.has_residual;
     c.ebuf0 = base + S::OFF_EPI + e * 2 * kEpiBufBytes;
     c.ebuf_ptr0 = base_ptr + S::OFF_EPI + e * 2 * kEpiBufBytes;

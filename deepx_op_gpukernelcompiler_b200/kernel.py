@@ -9,7 +9,11 @@ over 200 calls).  It returns ``CompileResult(success, diff, tl_ms, pt_ms,
 error)`` with success = ``diff < 0.5``.
 
 The only engine is the B200 one (``ENGINES = {"b200": ...}``): there is no
-multi-backend dispatch and no CPU path.  Extra keyword arguments over the
+multi-backend dispatch and no CPU path.  Besides the compilable patterns it
+runs the two single-GEMM patterns the reference lists as needs_template
+(fusion.py:24-25): ``attention_output`` (template ``gemm``: a @ b) and
+``attention_score`` (template ``gemm_elem``: (a @ b) * scale, with
+scale = 1/sqrt(K)), through compiled plans (plan.py).  Extra keyword arguments over the
 reference: ``dtype`` (default fp16 as in the reference), ``seed`` (default
 unseeded, as in the reference), ``n_iter`` and ``warmup``.  ``block`` is
 accepted for signature compatibility; the engine chooses its own tiles.
@@ -22,6 +26,7 @@ from .fusion import ACTIVATION_PT, classify
 from .kernel_b200 import make_linear_kernel
 from .kvfunc import read_func
 from .mlp import mlp_residual
+from .plan import CompileRequest, Plan
 
 DEFAULT_SHAPE = {"M": 512, "N": 512, "K": 256}
 DEFAULT_BLOCK = {"BM": 128, "BN": 128, "BK": 32}
@@ -29,6 +34,9 @@ DEFAULT_BLOCK = {"BM": 128, "BN": 128, "BK": 32}
 ENGINES = {
     "b200": make_linear_kernel,
 }
+
+# needs_template rows (fusion.py:24-25) whose template the engine implements.
+ENGINE_TEMPLATES = {"gemm", "gemm_elem"}
 
 
 class CompileResult:
@@ -76,7 +84,7 @@ def compile_and_test(kv, func_path: str, fusion: str = "b200", shape: dict | Non
     if status == "not_matched":
         opcodes = " → ".join(o["op"] for o in tensor_ops)
         return CompileResult(False, 0, 0, 0, f"no fusion pattern for: {opcodes}")
-    if status != "compilable":
+    if status != "compilable" and template not in ENGINE_TEMPLATES:
         return CompileResult(False, 0, 0, 0, f"{status}: {pattern}")
     if not torch.cuda.is_available():
         raise RuntimeError("compile_and_test needs a CUDA device (the B200 engine has no CPU path)")
@@ -91,7 +99,25 @@ def compile_and_test(kv, func_path: str, fusion: str = "b200", shape: dict | Non
     def randn(*shape_):
         return torch.randn(shape_, dtype=dtype, device=dev, generator=gen)
 
-    if template == "mlp_chain":
+    if template in ENGINE_TEMPLATES:
+        a, b = randn(M, K), randn(K, N)
+        scale = 1.0 / K ** 0.5 if template == "gemm_elem" else 1.0
+        dtype_name = {torch.float16: "float16", torch.bfloat16: "bfloat16",
+                      torch.float32: "float32"}[dtype]
+        spec = {"pattern": pattern, "ops": [o["op"] for o in tensor_ops], "scale": scale,
+                "inputs": [{"shape": [M, K], "dtype": dtype_name},
+                           {"shape": [K, N], "dtype": dtype_name}]
+                + ([{"shape": [1], "dtype": dtype_name}] if template == "gemm_elem" else []),
+                "outputs": [{"shape": [M, N], "dtype": dtype_name}]}
+        plan = Plan(CompileRequest.from_json(spec))
+
+        def run():
+            return plan(a, b)
+
+        def ref_fn():
+            out = a @ b
+            return out * scale if template == "gemm_elem" else out
+    elif template == "mlp_chain":
         # X[M,K] -> H[M,N] -> Y[M,K]; residual is X itself.
         a, w1, b1, w2, b2 = randn(M, K), randn(K, N), randn(N), randn(N, K), randn(K)
         w1 /= K ** 0.5

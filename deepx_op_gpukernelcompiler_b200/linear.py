@@ -149,3 +149,30 @@ def selected_kernel(M: int, N: int, K: int, dtype: torch.dtype) -> str:
     """Name of the kernel variant the engine picks for this problem."""
     code = nat.load().dx_select_kernel(M, N, K, DTYPE_CODES[dtype])
     return {v: k for k, v in nat.KERNEL_NAMES.items()}[code]
+
+
+def _ptr_array(ptrs):
+    import ctypes
+    arr = (ctypes.c_void_p * len(ptrs))(*ptrs)
+    return arr
+
+
+def reduce_broadcast(partial: torch.Tensor, p_ptrs, rank: int, rows_per_rank: int,
+                     bias: torch.Tensor | None, residual: torch.Tensor | None, y_ptrs,
+                     ldy: int) -> None:
+    """This rank's rows of sum_s partial_s + bias + residual, written to every
+    rank's output (dx_reduce_broadcast).  `partial` is this rank's partial
+    buffer (its shape and dtype describe all of them); `p_ptrs` / `y_ptrs`
+    are the peer-mapped addresses of every rank's partial / output buffer."""
+    N = partial.shape[1]
+    world = len(p_ptrs)
+    lib = nat.load()
+    with torch.cuda.device(partial.device):
+        stream = torch.cuda.current_stream(partial.device).cuda_stream
+        rc = lib.dx_reduce_broadcast(
+            _ptr_array(p_ptrs), world, rank, rows_per_rank, N, _ld(partial),
+            bias.data_ptr() if bias is not None else None,
+            residual.data_ptr() if residual is not None else None,
+            _ld(residual) if residual is not None else 0, _ptr_array(y_ptrs), ldy,
+            DTYPE_CODES[partial.dtype], stream)
+    nat.check("dx_reduce_broadcast", rc)

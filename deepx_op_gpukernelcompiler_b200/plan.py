@@ -1,0 +1,187 @@
+"""Compiled plans: the compile-request -> plan -> call flow of the reference docs.
+
+The reference design (doc/kvlang-to-tilelang-interface.md:100-129,194-218)
+compiles a fused function once per (pattern, shapes, dtype) from a JSON
+request and calls the result with raw pointers,
+``kernel_fn(x_ptr, W_ptr, b_ptr, out_ptr, cuda_stream)``.  The reference
+never built it.  Here a request such as
+
+    {"func": "__fusion_0", "pattern": "linear_relu", "ops": ["matmul", "add", "relu"],
+     "inputs":  [{"shape": [512, 256], "dtype": "float16"},
+                 {"shape": [256, 512], "dtype": "float16"},
+                 {"shape": [512],      "dtype": "float16"}],
+     "outputs": [{"shape": [512, 512], "dtype": "float16"}],
+     "accum_dtype": "float32"}
+
+is checked against the pattern table (``fusion.FUSION_DB``) and compiled into
+a native plan (``dx_plan_create``), cached by its key.  Supported patterns:
+every ``linear*`` pattern, ``linear_residual``, and the single-GEMM
+``needs_template`` neighbours the engine runs on the same kernels:
+``attention_output`` (a plain GEMM) and ``attention_score`` (GEMM times a
+scale; the request's optional ``"scale"`` gives its value).
+"""
+from __future__ import annotations
+
+import ctypes
+import json
+import threading
+from dataclasses import dataclass
+
+import torch
+
+from . import _native as nat
+from .fusion import FUSION_DB
+from .linear import DTYPE_CODES, _workspace, activation_code
+
+DTYPE_NAMES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
+
+# pattern -> (activation, has bias input, has residual input)
+PLAN_PATTERNS = {
+    "linear": (None, True, False),
+    "linear_relu": ("relu", True, False),
+    "linear_gelu": ("gelu", True, False),
+    "linear_silu": ("silu", True, False),
+    "linear_swish": ("swish", True, False),
+    "linear_residual": (None, True, True),
+    "attention_output": (None, False, False),
+    "attention_score": (None, False, False),
+}
+
+
+class CompileError(ValueError):
+    """The request does not describe a fused linear this engine can plan."""
+
+
+@dataclass(frozen=True)
+class CompileRequest:
+    func: str
+    pattern: str
+    ops: tuple
+    M: int
+    N: int
+    K: int
+    dtype: torch.dtype
+    scale: float = 1.0
+
+    @property
+    def key(self) -> tuple:
+        return (self.pattern, self.M, self.N, self.K, self.dtype, self.scale)
+
+    @classmethod
+    def from_json(cls, request) -> "CompileRequest":
+        req = json.loads(request) if isinstance(request, (str, bytes)) else dict(request)
+        try:
+            pattern = req["pattern"]
+            ops = tuple(req["ops"])
+            inputs = req["inputs"]
+            outputs = req["outputs"]
+        except KeyError as e:
+            raise CompileError(f"compile request lacks {e.args[0]!r}") from None
+        chain = tuple(op if op.startswith("tensor.") else f"tensor.{op}" for op in ops)
+        row = FUSION_DB.get(chain)
+        if row is None or row[0] != pattern:
+            raise CompileError(f"ops {list(ops)} do not form pattern {pattern!r}")
+        if pattern not in PLAN_PATTERNS:
+            raise CompileError(f"pattern {pattern!r} is not a single fused GEMM "
+                               f"(status {row[2]})")
+        if req.get("accum_dtype", "float32") != "float32":
+            raise CompileError("only float32 accumulation is supported")
+        _, has_bias, has_res = PLAN_PATTERNS[pattern]
+        n_in = 2 + int(has_bias) + int(has_res) + (1 if pattern == "attention_score" else 0)
+        if len(inputs) != n_in or len(outputs) != 1:
+            raise CompileError(f"{pattern} takes {n_in} inputs and 1 output, got "
+                               f"{len(inputs)} and {len(outputs)}")
+        dtypes = {t["dtype"] for t in list(inputs[:2]) + list(outputs)}
+        if len(dtypes) != 1 or next(iter(dtypes)) not in DTYPE_NAMES:
+            raise CompileError(f"inputs/outputs must share one of {list(DTYPE_NAMES)}")
+        (M, K), (K2, N) = inputs[0]["shape"], inputs[1]["shape"]
+        if K != K2:
+            raise CompileError(f"inner dimensions differ: {K} vs {K2}")
+        if list(outputs[0]["shape"]) != [M, N]:
+            raise CompileError(f"output shape {outputs[0]['shape']} is not [{M}, {N}]")
+        if has_bias and list(inputs[2]["shape"]) != [N]:
+            raise CompileError(f"bias shape {inputs[2]['shape']} is not [{N}]")
+        if has_res and list(inputs[3]["shape"]) != [M, N]:
+            raise CompileError(f"residual shape {inputs[3]['shape']} is not [{M}, {N}]")
+        return cls(req.get("func", ""), pattern, ops, int(M), int(N), int(K),
+                   DTYPE_NAMES[next(iter(dtypes))], float(req.get("scale", 1.0)))
+
+
+class Plan:
+    """A native plan: call(x, W, b=None, out=None, residual=None) -> out."""
+
+    def __init__(self, request: CompileRequest, kernel: str = "auto"):
+        act, self.has_bias, self.has_residual = PLAN_PATTERNS[request.pattern]
+        self.request = request
+        self._lib = nat.load()
+        handle = ctypes.c_void_p()
+        nat.check("dx_plan_create", self._lib.dx_plan_create(
+            ctypes.byref(handle), request.M, request.N, request.K, DTYPE_CODES[request.dtype],
+            activation_code(act), request.scale, nat.KERNEL_NAMES[kernel]))
+        self._handle = handle
+
+    def __del__(self):
+        handle = getattr(self, "_handle", None)
+        if handle is not None and handle.value:
+            self._lib.dx_plan_destroy(handle)
+            self._handle = None
+
+    def __call__(self, x: torch.Tensor, W: torch.Tensor, b: torch.Tensor | None = None,
+                 out: torch.Tensor | None = None,
+                 residual: torch.Tensor | None = None) -> torch.Tensor:
+        r = self.request
+        for name, t, shape in (("x", x, (r.M, r.K)), ("W", W, (r.K, r.N))):
+            if tuple(t.shape) != shape or t.dtype != r.dtype or not t.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous {r.dtype} tensor of shape {shape}")
+        if (b is not None) != self.has_bias:
+            raise ValueError(f"{r.pattern} {'needs' if self.has_bias else 'takes no'} bias")
+        if (residual is not None) != self.has_residual:
+            raise ValueError(f"{r.pattern} {'needs' if self.has_residual else 'takes no'} residual")
+        if out is None:
+            out = torch.empty((r.M, r.N), dtype=r.dtype, device=x.device)
+        with torch.cuda.device(x.device):
+            stream = torch.cuda.current_stream(x.device).cuda_stream
+            need = self._lib.dx_plan_workspace_size(self._handle)
+            ws = _workspace(x.device, stream, need)
+            nat.check("dx_plan_set_workspace", self._lib.dx_plan_set_workspace(
+                self._handle, ws.data_ptr() if ws is not None else None,
+                ws.numel() if ws is not None else 0))
+            rc = self._lib.dx_plan_call_residual(
+                self._handle, x.data_ptr(), W.data_ptr(), b.data_ptr() if b is not None else None,
+                residual.data_ptr() if residual is not None else None, out.data_ptr(), stream)
+        nat.check("dx_plan_call", rc)
+        return out
+
+
+class PlanCache:
+    """Plans keyed by (pattern, M, N, K, dtype, scale): the docs' shape-keyed
+    compiled-kernel cache (doc/kvlang-to-tilelang-interface.md:194-218)."""
+
+    def __init__(self):
+        self._plans: dict[tuple, Plan] = {}
+        self._lock = threading.Lock()
+        self.hits = 0
+        self.misses = 0
+
+    def get(self, request) -> Plan:
+        req = request if isinstance(request, CompileRequest) else CompileRequest.from_json(request)
+        with self._lock:
+            plan = self._plans.get(req.key)
+            if plan is not None:
+                self.hits += 1
+                return plan
+            self.misses += 1
+            plan = Plan(req)
+            self._plans[req.key] = plan
+            return plan
+
+    def __len__(self) -> int:
+        return len(self._plans)
+
+
+_default_cache = PlanCache()
+
+
+def compile_request(request) -> Plan:
+    """Compile (or fetch from the process-wide cache) the plan for a request."""
+    return _default_cache.get(request)

@@ -10,10 +10,16 @@ standard way, one process per GPU over ``torch.distributed`` (NCCL on GPUs):
 * ``ParallelMLP`` — the two-GEMM chain Y = act(X W1 + b1) W2 + b2 + X:
   W1 column-sharded, W2 row-sharded with the same hidden slice, so
   H_r = act(X W1_r + b1_r) stays local and Y = sum_r H_r W2_r needs one
-  all-reduce (SUM).  b2 and the residual X are added exactly once, inside
-  rank 0's second fused launch.  With ``chunks > 1`` the second GEMM runs in
-  M-chunks and each chunk's all-reduce is issued asynchronously while the
-  next chunk computes.
+  all-reduce.  Two implementations:
+    - ``mode="fused"`` (GPUs, default): the second GEMM writes its partial
+      into a peer-mapped (symmetric-memory) buffer; after a device barrier
+      each rank reads its row slab from every rank's partial over NVLink,
+      sums in rank order, adds b2 and X once and writes the finished rows
+      into every rank's output (one engine kernel, dx_reduce_broadcast) —
+      no NCCL on the path;
+    - ``mode="nccl"``: b2 and X are fused into rank 0's second launch and
+      Y is summed with NCCL all-reduce (in M-chunks issued asynchronously
+      when ``chunks > 1``).  This mode also runs on CPU ranks (gloo).
 
 Shard boundaries are multiples of ``align`` elements (default 64) so every
 slice of a row-major matrix starts on a 128-byte boundary and stays
@@ -93,13 +99,35 @@ class ColumnParallelLinear:
         return torch.cat([p[:, :sz] for p, sz in zip(parts, sizes)], dim=1)
 
 
+class _RowParallelBuffers:
+    """Symmetric (peer-mapped) partial and output buffers of one shape."""
+
+    def __init__(self, M: int, N: int, dtype, device, group):
+        import torch.distributed._symmetric_memory as symm_mem
+        world = dist.get_world_size(group)
+        if M % world:
+            raise ValueError(f"fused row-parallel needs M ({M}) divisible by world ({world})")
+        self.key = (M, N, dtype)
+        self.rows_per_rank = M // world
+        self.part = symm_mem.empty(M, N, dtype=dtype, device=device)
+        self.out = symm_mem.empty(M, N, dtype=dtype, device=device)
+        pg = group if group is not None else dist.group.WORLD
+        self.h_part = symm_mem.rendezvous(self.part, pg)
+        self.h_out = symm_mem.rendezvous(self.out, pg)
+        self.part_ptrs = list(self.h_part.buffer_ptrs)
+        self.out_ptrs = list(self.h_out.buffer_ptrs)
+
+
 class ParallelMLP:
     """Y = act(X W1 + b1) W2 + b2 + X with W1 column- and W2 row-sharded."""
 
     def __init__(self, W1_full, b1_full, W2_full, b2_full, activation="gelu", group=None,
-                 linear_fn=None, chunks: int = 1, align: int = 64):
+                 linear_fn=None, chunks: int = 1, align: int = 64, mode: str | None = None):
         world, rank = _group_info(group)
         self.group, self.world, self.rank = group, world, rank
+        self.mode = mode or ("fused" if (linear_fn is None and W1_full.is_cuda and world > 1)
+                             else "nccl")
+        self._bufs = None
         hidden = W1_full.shape[1]
         if W2_full.shape[0] != hidden:
             raise ValueError("W1 columns and W2 rows must match")
@@ -107,18 +135,23 @@ class ParallelMLP:
         self.W1 = W1_full[:, self.h0:self.h1].contiguous()
         self.b1 = b1_full[self.h0:self.h1].contiguous() if b1_full is not None else None
         self.W2 = W2_full[self.h0:self.h1, :].contiguous()
-        self.b2 = b2_full.contiguous() if (b2_full is not None and rank == 0) else None
+        self.b2_all = b2_full.contiguous() if b2_full is not None else None
+        self.b2 = self.b2_all if rank == 0 else None
         self.activation = activation
         self.linear_fn = linear_fn or _default_linear()
         self.chunks = max(1, int(chunks))
 
     @classmethod
     def from_shards(cls, W1_shard, b1_shard, W2_shard, b2_full, activation="gelu", group=None,
-                    linear_fn=None, chunks: int = 1):
+                    linear_fn=None, chunks: int = 1, mode: str | None = None):
         self = cls.__new__(cls)
         self.group = group
         self.world, self.rank = _group_info(group)
+        self.mode = mode or ("fused" if (linear_fn is None and W1_shard.is_cuda and self.world > 1)
+                             else "nccl")
+        self._bufs = None
         self.W1, self.b1, self.W2 = W1_shard, b1_shard, W2_shard
+        self.b2_all = b2_full
         self.b2 = b2_full if self.rank == 0 else None
         self.activation = activation
         self.linear_fn = linear_fn or _default_linear()
@@ -129,6 +162,8 @@ class ParallelMLP:
                  out: torch.Tensor | None = None) -> torch.Tensor:
         M = X.shape[0]
         H = self.linear_fn(X, self.W1, self.b1, self.activation, out=hidden)
+        if self.mode == "fused":
+            return self._row_parallel_fused(H, X, out)
         Y = out if out is not None else torch.empty((M, self.W2.shape[1]), dtype=X.dtype,
                                                     device=X.device)
         residual_rank = self.rank == 0
@@ -144,3 +179,25 @@ class ParallelMLP:
         for h in handles:
             h.wait()
         return Y
+
+    def _row_parallel_fused(self, H: torch.Tensor, X: torch.Tensor,
+                            out: torch.Tensor | None) -> torch.Tensor:
+        """Y = sum_r H_r W2_r + b2 + X: local partial, then reduce-broadcast."""
+        from .linear import fused_linear, reduce_broadcast
+        M, N = X.shape[0], self.W2.shape[1]
+        key = (M, N, X.dtype)
+        if self._bufs is None or self._bufs.key != key:
+            self._bufs = _RowParallelBuffers(M, N, X.dtype, X.device, self.group)
+        bufs = self._bufs
+        rpr = bufs.rows_per_rank
+        fused_linear(H, self.W2, None, None, out=bufs.part)
+        bufs.h_part.barrier(channel=0)  # every rank's partial is complete
+        reduce_broadcast(bufs.part, bufs.part_ptrs, self.rank, rpr, self.b2_all, X,
+                         bufs.out_ptrs, N)
+        # Every rank's rows have landed, and no rank still reads a partial
+        # that the next call will overwrite.
+        bufs.h_out.barrier(channel=1)
+        if out is None:
+            return bufs.out
+        out.copy_(bufs.out)
+        return out

@@ -104,6 +104,23 @@ int dx_fused_linear_ex(const void* X, const void* W, const void* bias,
                        void* workspace, size_t workspace_bytes,
                        void* stream);
 
+/*
+ * Reduction of a row-parallel linear over `world` ranks (the second layer of
+ * the MLP chain with its hidden dimension sharded; no reference counterpart —
+ * the reference is single-GPU and fusion.py:42-43 marks two-layer FFNs
+ * multi_kernel).  P[s] is rank s's partial Y (M x N, pitch ldp) and Y[s] its
+ * output buffer (pitch ldy), all peer-mapped so this rank can reach them over
+ * NVLink.  This rank handles rows rank*rows_per_rank .. +rows_per_rank: it
+ * sums the world partials in rank order, adds bias[N] and the residual row
+ * R[row] once, rounds to the dtype and writes the row into every Y[s]
+ * (reduce-scatter and all-gather in one pass).  The caller orders it with the
+ * peers: every partial complete before, every rank finished after (device
+ * barriers).  bias and R may be NULL; N % 8 == 0; 16-byte-aligned buffers.
+ */
+int dx_reduce_broadcast(void* const* P, int world, int rank, int64_t rows_per_rank, int64_t N,
+                        int64_t ldp, const void* bias, const void* R, int64_t ldr,
+                        void* const* Y, int64_t ldy, int dtype, void* stream);
+
 /* Skinny-M (decode) fused linear that allocates nothing.  No counterpart in
  * the reference: it exists for callers that cannot allocate device memory at
  * call time — a runtime whose own heap manager owns every device buffer and
@@ -129,6 +146,30 @@ size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K,
 /* The variant DX_KERNEL_AUTO picks for a problem with contiguous rows
  * (ld == row length) and 16-byte-aligned pointers. */
 int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype);
+
+/*
+ * Plans — the compile-then-call runtime of the reference design docs: the
+ * compile step fixes shape, dtype and op sequence
+ * (doc/kvlang-to-tilelang-interface.md:60-77,100-129) and the runtime calls
+ * `kernel_fn(x_ptr, W_ptr, b_ptr, out_ptr, cuda_stream)`
+ * (doc/kvlang-to-tilelang-interface.md:92, doc/kernel-compiler-analysis.md:118-123).
+ * A plan computes out = act(alpha * x @ W + b) (+ r) for contiguous x[M,K],
+ * W[K,N], b[N] (may be NULL), r and out [M,N]; alpha = 1 for the linear
+ * patterns, the attention scale for `attention_score` (fusion.py:24).
+ * `kernel` is a DX_KERNEL_* variant (DX_KERNEL_AUTO normally).  A plan holds
+ * no device memory; give it the workspace dx_plan_workspace_size() asks for
+ * (zero-filled once, one call at a time) with dx_plan_set_workspace.
+ */
+typedef struct dx_plan dx_plan;
+int dx_plan_create(dx_plan** plan, int64_t M, int64_t N, int64_t K, int dtype, int act,
+                   float alpha, int kernel);
+size_t dx_plan_workspace_size(const dx_plan* plan);
+int dx_plan_set_workspace(dx_plan* plan, void* workspace, size_t bytes);
+int dx_plan_call(const dx_plan* plan, const void* x, const void* W, const void* b, void* out,
+                 void* stream);
+int dx_plan_call_residual(const dx_plan* plan, const void* x, const void* W, const void* b,
+                          const void* r, void* out, void* stream);
+int dx_plan_destroy(dx_plan* plan);
 
 /* Message of the last failed call on this thread ("" if none). */
 const char* dx_last_error_string(void);

@@ -48,14 +48,16 @@ def main() -> int:
         W2 = (torch.randn(H, K, generator=g, device=dev) / H ** 0.5).bfloat16()
         b2 = (torch.rand(K, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
         ref = mlp_residual(X, W1, b1, W2, b2, "gelu").float()
-        for chunks in (1, 4):
-            mlp = ParallelMLP(W1, b1, W2, b2, "gelu", chunks=chunks)
-            out = mlp(X).float()
-            torch.cuda.synchronize()
-            err = (out - ref).abs()
-            tol = 2e-2 + 2e-2 * ref.abs()
-            if bool((err > tol).any()):
-                failures.append(f"MLP (chunks={chunks}) off by up to {err.max().item():.4g}")
+        for mode, chunks in (("nccl", 1), ("nccl", 4), ("fused", 1)):
+            mlp = ParallelMLP(W1, b1, W2, b2, "gelu", chunks=chunks, mode=mode)
+            for rep in range(2):  # the fused mode reuses its peer buffers
+                out = mlp(X).float()
+                torch.cuda.synchronize()
+                err = (out - ref).abs()
+                tol = 2e-2 + 2e-2 * ref.abs()
+                if bool((err > tol).any()):
+                    failures.append(f"MLP ({mode}, chunks={chunks}, call {rep}) off by up to "
+                                    f"{err.max().item():.4g}")
         status = _native.device_status(torch.cuda.current_stream(dev).cuda_stream)
         if status:
             failures.append(f"device status {status}")

@@ -1,0 +1,74 @@
+"""Compile requests and plans: parsing, validation and the plan cache (CPU).
+
+The request format is the reference docs' JSON compile request
+(doc/kvlang-to-tilelang-interface.md:100-129); creating a native plan is
+host-only, so the cache is exercised without a GPU.
+"""
+import json
+
+import pytest
+import torch
+
+from deepx_op_gpukernelcompiler_b200 import _build
+from deepx_op_gpukernelcompiler_b200.plan import CompileError, CompileRequest, PlanCache
+
+DOC_REQUEST = {
+    "func": "__fusion_0", "pattern": "linear_relu", "ops": ["matmul", "add", "relu"],
+    "inputs": [{"shape": [512, 256], "dtype": "float16"},
+               {"shape": [256, 512], "dtype": "float16"},
+               {"shape": [512], "dtype": "float16"}],
+    "outputs": [{"shape": [512, 512], "dtype": "float16"}],
+    "accum_dtype": "float32",
+}
+
+
+def test_doc_example_parses():
+    r = CompileRequest.from_json(json.dumps(DOC_REQUEST))
+    assert (r.pattern, r.M, r.N, r.K, r.dtype) == ("linear_relu", 512, 512, 256, torch.float16)
+
+
+@pytest.mark.parametrize("mutate,msg", [
+    (lambda r: r.update(ops=["matmul", "add", "gelu"]), "do not form"),
+    (lambda r: r.update(pattern="ffn_two_layer", ops=["matmul", "add", "relu", "matmul", "add"]),
+     "not a single fused GEMM"),
+    (lambda r: r["inputs"][1].update(shape=[255, 512]), "inner dimensions"),
+    (lambda r: r["outputs"][0].update(shape=[512, 511]), "output shape"),
+    (lambda r: r["inputs"][2].update(shape=[511]), "bias shape"),
+    (lambda r: r["inputs"][0].update(dtype="bfloat16"), "share one of"),
+    (lambda r: r.update(accum_dtype="float16"), "float32 accumulation"),
+    (lambda r: r.pop("inputs"), "lacks 'inputs'"),
+])
+def test_request_validation(mutate, msg):
+    req = json.loads(json.dumps(DOC_REQUEST))
+    mutate(req)
+    with pytest.raises(CompileError, match=msg):
+        CompileRequest.from_json(req)
+
+
+def test_attention_score_request_carries_scale():
+    req = {"pattern": "attention_score", "ops": ["matmul", "mul"], "scale": 0.125,
+           "inputs": [{"shape": [64, 32], "dtype": "bfloat16"},
+                      {"shape": [32, 64], "dtype": "bfloat16"},
+                      {"shape": [1], "dtype": "bfloat16"}],
+           "outputs": [{"shape": [64, 64], "dtype": "bfloat16"}]}
+    r = CompileRequest.from_json(req)
+    assert r.pattern == "attention_score" and r.scale == 0.125
+
+
+def test_plan_cache_keys_by_shape():
+    _build.build()
+    cache = PlanCache()
+    p1 = cache.get(DOC_REQUEST)
+    p2 = cache.get(json.dumps(DOC_REQUEST))
+    assert p1 is p2 and cache.hits == 1 and cache.misses == 1
+    other = json.loads(json.dumps(DOC_REQUEST))
+    other["inputs"][0]["shape"] = [128, 256]
+    other["outputs"][0]["shape"] = [128, 512]
+    assert cache.get(other) is not p1 and len(cache) == 2
+
+
+def test_plan_rejects_wrong_operands_on_cpu():
+    _build.build()
+    plan = PlanCache().get(DOC_REQUEST)
+    with pytest.raises(ValueError, match="x must be"):
+        plan(torch.zeros(4, 4, dtype=torch.float16), torch.zeros(256, 512, dtype=torch.float16))

@@ -20,8 +20,8 @@ def kv():
 def test_compile_and_test_reports_non_compilable(kv):
     r = compile_and_test(kv, "/func/fusion_cases/two_layer_relu")
     assert not r.success and r.error == "multi_kernel: ffn_two_layer"
-    r = compile_and_test(kv, "/func/fusion_cases/scaled_scores")
-    assert not r.success and r.error == "needs_template: attention_score"
+    r = compile_and_test(kv, "/func/fusion_cases/masked_softmax")
+    assert not r.success and r.error == "needs_template: attention_softmax"
 
 
 def test_compile_and_test_reports_unmatched():
