@@ -688,7 +688,7 @@ int dx_reduce_broadcast(void* const* P, int world, int rank, int64_t rows_per_ra
   if ((rc = device_sms(dev, &sms))) return rc;
   const long long work = rows_per_rank * (N / 8);
   const int grid = static_cast<int>(std::max<long long>(
-      1, std::min<long long>((work + 255) / 256, 4LL * sms)));
+      1, std::min<long long>((work + 511) / 512, 8LL * sms)));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   set_plan("reduce_broadcast world=%d rows=%lld N=%lld grid=%d", world, (long long)rows_per_rank,
            (long long)N, grid);
