@@ -14,7 +14,13 @@ never built it.  Here a request such as
      "accum_dtype": "float32"}
 
 is checked against the pattern table (``fusion.FUSION_DB``) and compiled into
-a native plan (``dx_plan_create``), cached by its key.  Supported patterns:
+a native plan (``dx_plan_create``), cached by its key.  A ``PlanCache`` given
+a kvspace store also records each compiled version there, keyed by a hash of
+its shape, as the docs' lazy-compile lifecycle describes
+(doc/kvlang-to-tilelang-interface.md:194-218): the record at
+``/func/<func>_b200/<shape hash>`` names the library, its ABI version, the
+entry point and the kernel variant, so another process (or a non-Python
+dispatcher) sees which versions exist and how to call them.  Supported patterns:
 every ``linear*`` pattern, ``linear_residual``, and the single-GEMM
 ``needs_template`` neighbours the engine runs on the same kernels:
 ``attention_output`` (a plain GEMM) and ``attention_score`` (GEMM times a
@@ -23,6 +29,7 @@ scale; the request's optional ``"scale"`` gives its value).
 from __future__ import annotations
 
 import ctypes
+import hashlib
 import json
 import threading
 from dataclasses import dataclass
@@ -34,6 +41,7 @@ from .fusion import FUSION_DB
 from .linear import DTYPE_CODES, _workspace, activation_code
 
 DTYPE_NAMES = {"float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
+DTYPE_OF = {v: k for k, v in DTYPE_NAMES.items()}
 
 # pattern -> (activation, has bias input, has residual input)
 PLAN_PATTERNS = {
@@ -66,6 +74,28 @@ class CompileRequest:
     @property
     def key(self) -> tuple:
         return (self.pattern, self.M, self.N, self.K, self.dtype, self.scale)
+
+    @property
+    def shape_hash(self) -> str:
+        """16 hex digits identifying (pattern, M, N, K, dtype, scale)."""
+        canon = json.dumps({"pattern": self.pattern, "M": self.M, "N": self.N, "K": self.K,
+                            "dtype": DTYPE_OF[self.dtype], "scale": self.scale}, sort_keys=True)
+        return hashlib.sha1(canon.encode()).hexdigest()[:16]
+
+    def to_json(self) -> dict:
+        """A compile request that parses back to this one."""
+        _, has_bias, has_res = PLAN_PATTERNS[self.pattern]
+        dt = DTYPE_OF[self.dtype]
+        inputs = [{"shape": [self.M, self.K], "dtype": dt}, {"shape": [self.K, self.N], "dtype": dt}]
+        if has_bias:
+            inputs.append({"shape": [self.N], "dtype": dt})
+        if has_res:
+            inputs.append({"shape": [self.M, self.N], "dtype": dt})
+        if self.pattern == "attention_score":
+            inputs.append({"shape": [1], "dtype": dt})
+        return {"func": self.func, "pattern": self.pattern, "ops": list(self.ops),
+                "inputs": inputs, "outputs": [{"shape": [self.M, self.N], "dtype": dt}],
+                "accum_dtype": "float32", "scale": self.scale}
 
     @classmethod
     def from_json(cls, request) -> "CompileRequest":
@@ -153,15 +183,53 @@ class Plan:
         return out
 
 
+def record_key(req: CompileRequest, prefix: str = "/func") -> str:
+    """kvspace key of a compiled version: ``<prefix>/<func>_b200/<shape hash>``."""
+    return f"{prefix.rstrip('/')}/{req.func or req.pattern}_b200/{req.shape_hash}"
+
+
+def plan_record(req: CompileRequest) -> dict:
+    """What a dispatcher needs to call a compiled version without Python."""
+    lib = nat.load()
+    kernel = lib.dx_select_kernel(req.M, req.N, req.K, DTYPE_CODES[req.dtype])
+    names = {v: k for k, v in nat.KERNEL_NAMES.items()}
+    return {"request": req.to_json(), "shape_hash": req.shape_hash,
+            "library": nat.LIB_PATH.name, "abi_version": int(lib.dx_version()),
+            "create": "dx_plan_create",
+            "entry": "dx_plan_call_residual" if PLAN_PATTERNS[req.pattern][2] else "dx_plan_call",
+            "kernel": names.get(kernel, str(kernel))}
+
+
 class PlanCache:
     """Plans keyed by (pattern, M, N, K, dtype, scale): the docs' shape-keyed
-    compiled-kernel cache (doc/kvlang-to-tilelang-interface.md:194-218)."""
+    compiled-kernel cache (doc/kvlang-to-tilelang-interface.md:194-218).
 
-    def __init__(self):
+    With ``kv`` (a kvspace store: ``get``/``set``/``list``), every compiled
+    version is also recorded under ``record_key``; a request whose record is
+    already in the store counts as a kvspace hit (``kv_hits``) and its plan is
+    rebuilt from the stored request, which must match the one asked for."""
+
+    def __init__(self, kv=None, prefix: str = "/func"):
         self._plans: dict[tuple, Plan] = {}
         self._lock = threading.Lock()
+        self.kv = kv
+        self.prefix = prefix
         self.hits = 0
+        self.kv_hits = 0
         self.misses = 0
+
+    def _stored(self, req: CompileRequest) -> dict | None:
+        if self.kv is None:
+            return None
+        try:
+            value = self.kv.get(record_key(req, self.prefix))
+        except KeyError:  # the store's ErrNotFound derives from KeyError
+            return None
+        record = json.loads(value.as_str())
+        if CompileRequest.from_json(record["request"]).key != req.key:
+            raise CompileError(f"kvspace record {record_key(req, self.prefix)} holds another "
+                               f"request (shape-hash collision)")
+        return record
 
     def get(self, request) -> Plan:
         req = request if isinstance(request, CompileRequest) else CompileRequest.from_json(request)
@@ -170,18 +238,45 @@ class PlanCache:
             if plan is not None:
                 self.hits += 1
                 return plan
-            self.misses += 1
+            stored = self._stored(req)
             plan = Plan(req)
+            if stored is not None:
+                self.kv_hits += 1
+            else:
+                self.misses += 1
+                if self.kv is not None:
+                    self.kv.set(record_key(req, self.prefix), json.dumps(plan_record(req)))
             self._plans[req.key] = plan
             return plan
+
+    def records(self, func: str) -> dict[str, dict]:
+        """Compiled versions of ``func`` recorded in the store, by shape hash."""
+        if self.kv is None:
+            return {}
+        base = f"{self.prefix.rstrip('/')}/{func}_b200"
+        try:
+            names = self.kv.list(base)
+        except KeyError:
+            return {}
+        return {h: json.loads(self.kv.get(f"{base}/{h}").as_str()) for h in names}
 
     def __len__(self) -> int:
         return len(self._plans)
 
 
 _default_cache = PlanCache()
+_kv_caches: dict[int, PlanCache] = {}
+_kv_caches_lock = threading.Lock()
 
 
-def compile_request(request) -> Plan:
-    """Compile (or fetch from the process-wide cache) the plan for a request."""
-    return _default_cache.get(request)
+def compile_request(request, kv=None) -> Plan:
+    """Compile (or fetch from a cache) the plan for a request.  Without ``kv``
+    the process-wide cache is used; with a kvspace store, a cache bound to that
+    store (one per store) records the compiled version there."""
+    if kv is None:
+        return _default_cache.get(request)
+    with _kv_caches_lock:
+        cache = _kv_caches.get(id(kv))
+        if cache is None or cache.kv is not kv:
+            cache = _kv_caches[id(kv)] = PlanCache(kv)
+    return cache.get(request)

@@ -72,3 +72,52 @@ def test_plan_rejects_wrong_operands_on_cpu():
     plan = PlanCache().get(DOC_REQUEST)
     with pytest.raises(ValueError, match="x must be"):
         plan(torch.zeros(4, 4, dtype=torch.float16), torch.zeros(256, 512, dtype=torch.float16))
+
+
+def test_request_round_trips_through_json():
+    r = CompileRequest.from_json(DOC_REQUEST)
+    assert CompileRequest.from_json(json.dumps(r.to_json())) == r
+    other = json.loads(json.dumps(DOC_REQUEST))
+    other["inputs"][0]["shape"] = [256, 256]
+    other["outputs"][0]["shape"] = [256, 512]
+    assert CompileRequest.from_json(other).shape_hash != r.shape_hash
+
+
+def test_kvspace_backed_cache_records_versions():
+    from deepx_op_gpukernelcompiler_b200.kvspace_local import KVSpace
+    from deepx_op_gpukernelcompiler_b200.plan import record_key
+    _build.build()
+    kv = KVSpace()
+    first = PlanCache(kv)
+    first.get(DOC_REQUEST)
+    small = json.loads(json.dumps(DOC_REQUEST))
+    small["inputs"][0]["shape"] = [16, 256]
+    small["outputs"][0]["shape"] = [16, 512]
+    first.get(small)
+    assert first.misses == 2 and first.kv_hits == 0
+    recs = first.records("__fusion_0")
+    assert len(recs) == 2
+    req = CompileRequest.from_json(DOC_REQUEST)
+    rec = recs[req.shape_hash]
+    assert record_key(req) == f"/func/__fusion_0_b200/{req.shape_hash}"
+    assert rec["entry"] == "dx_plan_call" and rec["library"] == "libdeepx_fused.so"
+    assert rec["kernel"] == "umma" and recs[CompileRequest.from_json(small).shape_hash]["kernel"] == "decode"
+    assert CompileRequest.from_json(rec["request"]) == req
+    # A second process-level cache over the same store finds the versions.
+    second = PlanCache(kv)
+    second.get(json.dumps(DOC_REQUEST))
+    assert second.kv_hits == 1 and second.misses == 0
+
+
+def test_kvspace_record_collision_is_rejected():
+    from deepx_op_gpukernelcompiler_b200.kvspace_local import KVSpace
+    from deepx_op_gpukernelcompiler_b200.plan import record_key
+    _build.build()
+    kv = KVSpace()
+    req = CompileRequest.from_json(DOC_REQUEST)
+    bogus = json.loads(json.dumps(DOC_REQUEST))
+    bogus["inputs"][0]["shape"] = [64, 256]
+    bogus["outputs"][0]["shape"] = [64, 512]
+    kv.set(record_key(req), json.dumps({"request": bogus}))
+    with pytest.raises(CompileError, match="collision"):
+        PlanCache(kv).get(DOC_REQUEST)
