@@ -452,6 +452,11 @@ int launch_decode(const Problem& pr, int dev, int sms, const DecodePlan& d) {
   p.partials = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + d.ticket_bytes);
   p.act = pr.act;
   p.alpha = pr.alpha;
+  {
+    unsigned long long* tr = g_trace.load();
+    const size_t need = static_cast<size_t>(d.grid) * dx::kTraceSlots * 8;
+    p.trace = (tr != nullptr && g_trace_bytes.load() >= need) ? tr : nullptr;
+  }
   (void)sms;
   set_plan("decode mn=%d stages=%d grid=%d n_tiles=%d kbt=%d max_seg=%d workspace=%zu", MN,
            S::STAGES, d.grid, d.n_tiles, d.kbt, d.max_seg, d.bytes);

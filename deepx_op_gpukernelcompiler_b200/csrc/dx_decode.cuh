@@ -42,7 +42,17 @@ struct DecodeParams {
   int* tickets;         // [n_tiles][4] (per warp quarter), zero between calls
   int act;
   float alpha;          // Y = act(alpha * acc + bias) + R
+  // Optional timeline (dx_set_trace_buffer), kTraceSlots stamps per CTA:
+  // [0] after set-up, [1] first and [2] last TMA issue, [3] last MMA issue,
+  // [4 + i] epilogue of work item i finished (i < 9), [13] the SM's id,
+  // [14] epilogue warps done, [15] exit.
+  unsigned long long* trace;
 };
+
+__device__ __forceinline__ void decode_trace(const DecodeParams& p, int slot) {
+  if (p.trace != nullptr)
+    p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + slot] = global_timer_ns();
+}
 
 template <int MN>
 struct DecodeShape {
@@ -131,6 +141,14 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_word;
+  if (threadIdx.x == 0) {
+    decode_trace(p, 0);
+    if (p.trace != nullptr) {
+      uint32_t smid;
+      asm volatile("mov.u32 %0, %%smid;" : "=r"(smid));
+      p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + 13] = smid;
+    }
+  }
 
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
@@ -154,6 +172,7 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
             tma_load_2d(&tmW, sW + s * S::W_BYTES + j * S::W_BOX_BYTES, fb, t * S::NT + 64 * j,
                         kb * S::BK);
           tma_load_2d(&tmX, sX + s * S::X_BYTES, fb, kb * S::BK, 0);
+          if (issued == 0) decode_trace(p, 1);
           ++issued;
           if (++s == S::STAGES) {
             s = 0;
@@ -162,6 +181,7 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
         }
         u += kb1 - kb0;
       }
+      decode_trace(p, 2);
       const uint32_t n_drain = issued < (uint32_t)S::STAGES ? issued : (uint32_t)S::STAGES;
       for (uint32_t i = issued - n_drain; i < issued; ++i)
         mbar_wait_drain(bar(S::BAR_FULL + (int)(i % S::STAGES)), (i / S::STAGES) & 1u);
@@ -211,6 +231,7 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
         }
         if (ok) umma_commit(bar(S::BAR_TFULL + b));
       }
+      decode_trace(p, 3);
       umma_commit(bar(S::BAR_DRAIN));
       mbar_wait_drain(bar(S::BAR_DRAIN), 0);
     }
@@ -231,6 +252,13 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
       u += kb1 - kb0;
       const int b = local & 1;
       const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
+      // The item's bias, loaded while its accumulator is still being built.
+      float bv[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int n = t * S::NT + h * 128 + n_local;
+        bv[h] = (bias != nullptr && n < p.N) ? Tr::to_float(bias[n]) : 0.0f;
+      }
       if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
       tc_fence_after();
       float acc[2][MN];
@@ -279,27 +307,46 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
         int ticket = 0;
         if (lane == 0) ticket = atomicAdd(p.tickets + t * 4 + q, 1);
         ticket = __shfl_sync(0xffffffffu, ticket, 0);
-        if (ticket != nseg - 1) continue;
+        if (ticket != nseg - 1) {
+          if (q == 0 && lane == 0 && local < 9) decode_trace(p, 4 + local);
+          continue;
+        }
         __threadfence();
         // Fixed summation order over segments: bitwise identical results
-        // whichever CTA finishes last.  All loads of a segment are issued
-        // before they are added.
+        // whichever CTA finishes last.  The loads of SB segments (128 values
+        // per thread) are all issued before any of them is added, so a tile
+        // split over many CTAs costs few memory round trips.
+        // (With MN = 64 one half-tile of one segment, 64 values, at a time.)
+        constexpr int SB = MN <= 32 ? 64 / MN : 1;
+        constexpr int NH = MN <= 32 ? 2 : 1;
 #pragma unroll
         for (int h = 0; h < 2; ++h)
 #pragma unroll
           for (int m = 0; m < MN; ++m) acc[h][m] = 0.0f;
-        for (int sg = 0; sg < nseg; ++sg) {
-          const float* src = part_t + static_cast<size_t>(sg) * MN * S::NT;
-          float f[2][MN];
+        for (int sg0 = 0; sg0 < nseg; sg0 += SB) {
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
+          for (int h0 = 0; h0 < 2; h0 += NH) {
+            float f[SB][NH][MN];
 #pragma unroll
-            for (int m = 0; m < MN; ++m)
-              f[h][m] = m < M ? __ldcg(src + m * S::NT + h * 128 + n_local) : 0.0f;
+            for (int sb = 0; sb < SB; ++sb) {
+              const float* src = part_t + static_cast<size_t>(sg0 + sb) * MN * S::NT;
 #pragma unroll
-          for (int h = 0; h < 2; ++h)
+              for (int hh = 0; hh < NH; ++hh)
 #pragma unroll
-            for (int m = 0; m < MN; ++m) acc[h][m] += f[h][m];
+                for (int m = 0; m < MN; ++m)
+                  f[sb][hh][m] = (sg0 + sb < nseg && m < M)
+                                     ? __ldcg(src + m * S::NT + (h0 + hh) * 128 + n_local)
+                                     : 0.0f;
+            }
+#pragma unroll
+            for (int sb = 0; sb < SB; ++sb)
+              if (sg0 + sb < nseg) {
+#pragma unroll
+                for (int hh = 0; hh < NH; ++hh)
+#pragma unroll
+                  for (int m = 0; m < MN; ++m) acc[h0 + hh][m] += f[sb][hh][m];
+              }
+          }
         }
         if (lane == 0) p.tickets[t * 4 + q] = 0;
       }
@@ -307,18 +354,19 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
       for (int h = 0; h < 2; ++h) {
         const int n = t * S::NT + h * 128 + n_local;
         if (n < p.N) {
-          const float bv = bias != nullptr ? Tr::to_float(bias[n]) : 0.0f;
 #pragma unroll
           for (int m = 0; m < MN; ++m) {
             if (m < M) {
-              float y = act_apply(fmaf(p.alpha, acc[h][m], bv), p.act);
+              float y = act_apply(fmaf(p.alpha, acc[h][m], bv[h]), p.act);
               if (res != nullptr) y += Tr::to_float(res[m * p.ldr + n]);
               Y[m * p.ldy + n] = Tr::from_float(y);
             }
           }
         }
       }
+      if (q == 0 && lane == 0 && local < 9) decode_trace(p, 4 + local);
     }
+    if (q == 0 && lane == 0) decode_trace(p, 14);
   }
 
   tc_fence_before();
@@ -327,6 +375,7 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem_base, S::TMEM_COLS);
   }
+  if (threadIdx.x == 0) decode_trace(p, 15);
 }
 
 }  // namespace dx

@@ -63,8 +63,6 @@ struct UmmaParams {
   unsigned long long* trace;
 };
 
-constexpr int kTraceSlots = 16;
-
 __device__ __forceinline__ void trace_mark(const UmmaParams& p, int slot) {
   if (p.trace != nullptr && slot < kTraceSlots)
     p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + slot] = global_timer_ns();

@@ -178,10 +178,13 @@ const char* dx_last_error_string(void);
  * thread: variant, tile shape, pipeline depth, grid ("" if none). */
 const char* dx_last_launch_plan(void);
 
-/* Timeline tracing of the tensor-core GEMM kernels (profiling aid).  With a
+/* Timeline tracing of the tensor-core kernels (profiling aid).  With a
  * device buffer set, every later launch records %globaltimer stamps (ns) per
- * CTA: 16 uint64 slots per CTA in blockIdx order — slot 0 after set-up,
- * slot 1+i when work item i's epilogue finished (i < 14), slot 15 at exit.
+ * CTA: 16 uint64 slots per CTA in blockIdx order.  GEMM kernels: slot 0 after
+ * set-up, slot 1+i when work item i's epilogue finished (i < 14), slot 15 at
+ * exit.  Decode kernel: slot 0 after set-up, 1 / 2 first / last TMA issue,
+ * 3 last MMA issue, 4+i work item i finished (i < 9), 13 the SM id (not a
+ * time), 14 epilogue done, 15 exit.
  * The buffer must hold 16 * 8 bytes per CTA of the grid (148 SMs: 18,944 B);
  * launches whose grid does not fit are not traced.  NULL turns tracing off.
  * Process-wide setting; the caller owns the buffer. */
