@@ -66,6 +66,11 @@ SIGNATURES = {
                                            ctypes.POINTER(ctypes.c_void_p), _i64, ctypes.c_int,
                                            _vp]),
     "dx_fused_linear_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, ctypes.c_int, ctypes.c_int]),
+    "dx_fused_gated_linear": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
+                                             _i64, _i64, _i64, ctypes.c_int, ctypes.c_int,
+                                             ctypes.c_int, _vp, ctypes.c_size_t, _vp]),
+    "dx_fused_gated_linear_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, ctypes.c_int,
+                                                               ctypes.c_int]),
     "dx_select_kernel": (ctypes.c_int, [_i64, _i64, _i64, ctypes.c_int]),
     "dx_last_error_string": (ctypes.c_char_p, []),
     "dx_last_launch_plan": (ctypes.c_char_p, []),

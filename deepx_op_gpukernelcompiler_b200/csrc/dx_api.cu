@@ -153,6 +153,11 @@ struct Problem {
   size_t ws_bytes;
   cudaStream_t stream;
   float alpha = 1.0f;  // Y = act(alpha * X W + bias) + R
+  // Gated form: Y = act(X W + bias) * (X W2 + bias2); no residual, alpha 1.
+  bool gated = false;
+  const void* W2 = nullptr;
+  const void* bias2 = nullptr;
+  int64_t ldw2 = 0;
 };
 
 // ----------------------------------------------------------- decode plan
@@ -162,6 +167,7 @@ constexpr int kDecodeTileN = 256;  // W columns per decode work unit
 // partial sums of one problem never overlap the tickets of another problem
 // that reuses the same workspace later; the kernel leaves the slab zeroed.
 constexpr size_t kTicketSlabBytes = size_t(64) << 10;
+// (one 32-bit counter word per tile and warp quarter)
 constexpr int64_t kDecodeMaxTiles = static_cast<int64_t>(kTicketSlabBytes / (4 * sizeof(int)));
 
 int decode_mn(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : 64); }
@@ -174,14 +180,24 @@ long long decode_cta_of_host(long long u, long long U, int G) {
 
 struct DecodePlan {
   int n_tiles = 0, kbt = 0, grid = 0, max_seg = 0, mn = 16;
+  int nh = 2;  // 128-column UMMA halves per work unit
   long long units = 0;
   size_t ticket_bytes = 0, bytes = 0;
 };
 
-DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sms) {
+// Halves per work unit: 2; the gated form with M <= 16 uses 4 (256 columns
+// of each weight, so both weights are read in 512-byte row segments).
+int decode_halves(int64_t M, bool gated) { return gated && decode_mn(M) == 16 ? 4 : 2; }
+
+// Output columns per work unit: 256 (plain), 64 x halves (gated).
+int decode_tile_n(int64_t M, bool gated) { return gated ? 64 * decode_halves(M, true) : kDecodeTileN; }
+
+DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sms, bool gated = false) {
   DecodePlan d;
   d.mn = decode_mn(M);
-  d.n_tiles = static_cast<int>((N + kDecodeTileN - 1) / kDecodeTileN);
+  d.nh = decode_halves(M, gated);
+  const int tile_n = decode_tile_n(M, gated);
+  d.n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
   d.kbt = static_cast<int>((K + 63) / 64);
   d.units = static_cast<long long>(d.n_tiles) * d.kbt;
   const long long want = sms;  // one CTA per SM
@@ -196,7 +212,7 @@ DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sms) {
   d.max_seg = ms;
   d.ticket_bytes = kTicketSlabBytes;
   d.bytes = d.ticket_bytes +
-            static_cast<size_t>(d.n_tiles) * d.max_seg * d.mn * kDecodeTileN * sizeof(float);
+            static_cast<size_t>(d.n_tiles) * d.max_seg * d.mn * (128 * d.nh) * sizeof(float);
   return d;
 }
 
@@ -214,8 +230,8 @@ int pick_group_m(int m_tiles, int64_t rows_per_tile, int64_t K) {
   return static_cast<int>((m_tiles + groups - 1) / groups);
 }
 
-int make_umma_maps(const Problem& pr, CUtensorMap* tA, CUtensorMap* tB, CUtensorMap* tY,
-                   CUtensorMap* tR) {
+int make_umma_maps(const Problem& pr, CUtensorMap* tA, CUtensorMap* tB, CUtensorMap* tB2,
+                   CUtensorMap* tY, CUtensorMap* tR) {
   const CUtensorMapDataType dt = tma_dtype(pr.dtype);
   int rc;
   if ((rc = make_tmap_2d(tA, pr.X, dt, pr.K, pr.M, pr.ldx, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -224,6 +240,13 @@ int make_umma_maps(const Problem& pr, CUtensorMap* tA, CUtensorMap* tB, CUtensor
   if ((rc = make_tmap_2d(tB, pr.W, dt, pr.N, pr.K, pr.ldw, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B,
                          "W")))
     return rc;
+  if (pr.gated) {
+    if ((rc = make_tmap_2d(tB2, pr.W2, dt, pr.N, pr.K, pr.ldw2, 64, 64,
+                           CU_TENSOR_MAP_SWIZZLE_128B, "W2")))
+      return rc;
+  } else {
+    *tB2 = *tB;  // never read
+  }
   if ((rc = make_tmap_2d(tY, pr.Y, dt, pr.N, pr.M, pr.ldy, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B,
                          "Y")))
     return rc;
@@ -243,6 +266,7 @@ int make_umma_maps(const Problem& pr, CUtensorMap* tA, CUtensorMap* tB, CUtensor
 // the last partial wave split `splits` ways along K when a workspace allows.
 struct UmmaPlan {
   bool pair = false;
+  bool gated = false;  // output tiles bn / 2 wide, no split tail
   int bn = 256;
   int rows = 128;  // tile rows: 256 for pairs
   int workers = 0;
@@ -259,21 +283,25 @@ double umma_efficiency(bool pair, int bn) {
 }
 
 UmmaPlan plan_umma(int64_t M, int64_t N, int64_t K, int sms, int pair_slots, bool allow_split,
-                   bool single_cta_only) {
+                   bool single_cta_only, bool gated = false) {
   UmmaPlan best;
   double best_cost = 1e300;
   const int kb = static_cast<int>((K + 63) / 64);
+  if (gated) allow_split = false;
   for (int use_pair = 0; use_pair < 2; ++use_pair) {
     if (use_pair && (single_cta_only || M < 256 || pair_slots <= 0)) continue;
     for (int bn : {256, 128}) {
-      if (bn == 256 && N <= 128) continue;
+      // The gated kernels exist for BN = 256 (128 gate + 128 up columns).
+      if (gated ? bn != 256 : (bn == 256 && N <= 128)) continue;
       UmmaPlan pl;
       pl.pair = use_pair != 0;
+      pl.gated = gated;
       pl.bn = bn;
       pl.rows = pl.pair ? 256 : 128;
       pl.workers = pl.pair ? pair_slots : sms;
       pl.k_blocks = kb;
-      const int64_t tiles = ((M + pl.rows - 1) / pl.rows) * ((N + bn - 1) / bn);
+      const int64_t tile_n = gated ? bn / 2 : bn;
+      const int64_t tiles = ((M + pl.rows - 1) / pl.rows) * ((N + tile_n - 1) / tile_n);
       pl.num_tiles = static_cast<int>(tiles);
       const int64_t full = tiles / pl.workers, rem = tiles % pl.workers;
       int splits = 1;
@@ -306,11 +334,13 @@ UmmaParams umma_params(const Problem& pr, const UmmaPlan& pl) {
   p.N = static_cast<int>(pr.N);
   p.K = static_cast<int>(pr.K);
   p.m_tiles = static_cast<int>((pr.M + pl.rows - 1) / pl.rows);
-  p.n_tiles = static_cast<int>((pr.N + pl.bn - 1) / pl.bn);
+  const int tile_n = pl.gated ? pl.bn / 2 : pl.bn;
+  p.n_tiles = static_cast<int>((pr.N + tile_n - 1) / tile_n);
   p.k_blocks = pl.k_blocks;
   p.num_tiles = p.m_tiles * p.n_tiles;
   p.group_m = pick_group_m(p.m_tiles, pl.rows, pr.K);
   p.bias = pr.bias;
+  p.bias2 = pr.bias2;
   p.act = pr.act;
   p.has_residual = pr.R != nullptr ? 1 : 0;
   p.alpha = pr.alpha;
@@ -336,21 +366,21 @@ int umma_grid_workers(const UmmaPlan& pl) {
   return static_cast<int>(std::min<int64_t>(pl.workers, items));
 }
 
-template <int BN, typename T>
+template <int BN, typename T, bool G = false>
 int launch_umma(const Problem& pr, int dev, const UmmaPlan& pl) {
   using S = UmmaShape<BN>;
-  auto kern = dx::umma_fused_linear_kernel<BN, T>;
+  auto kern = dx::umma_fused_linear_kernel<BN, T, G>;
   int rc = ensure_smem_attr(dev, reinterpret_cast<const void*>(kern), S::SMEM_BYTES, false);
   if (rc) return rc;
-  CUtensorMap tA, tB, tY, tR;
-  if ((rc = make_umma_maps(pr, &tA, &tB, &tY, &tR))) return rc;
+  CUtensorMap tA, tB, tB2, tY, tR;
+  if ((rc = make_umma_maps(pr, &tA, &tB, &tB2, &tY, &tR))) return rc;
   const UmmaParams p = umma_params(pr, pl);
   const int grid = umma_grid_workers(pl);
-  set_plan("umma_1cta tile=128x%d stages=%d grid=%d tiles=%d dp_tiles=%d splits=%d group_m=%d "
+  set_plan("umma_1cta%s tile=128x%d stages=%d grid=%d tiles=%d dp_tiles=%d splits=%d group_m=%d "
            "smem=%d workspace=%zu",
-           BN, S::STAGES, grid, p.num_tiles, p.dp_tiles, p.splits, p.group_m, S::SMEM_BYTES,
-           pl.bytes);
-  kern<<<grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tA, tB, tY, tR, p);
+           G ? "_gated" : "", G ? BN / 2 : BN, S::STAGES, grid, p.num_tiles, p.dp_tiles, p.splits,
+           p.group_m, S::SMEM_BYTES, pl.bytes);
+  kern<<<grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tA, tB, tB2, tY, tR, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch umma_fused_linear_kernel");
   return DX_OK;
@@ -398,39 +428,46 @@ int pair_slots(int dev, int sms) {
   return n;
 }
 
-template <int BN, typename T>
+template <int BN, typename T, bool G = false>
 int launch_umma2(const Problem& pr, int dev, const UmmaPlan& pl) {
   using S = Umma2Shape<BN>;
-  auto kern = dx::umma2_fused_linear_kernel<BN, T>;
+  auto kern = dx::umma2_fused_linear_kernel<BN, T, G>;
   int rc = ensure_smem_attr(dev, reinterpret_cast<const void*>(kern), S::SMEM_BYTES, false);
   if (rc) return rc;
-  CUtensorMap tA, tB, tY, tR;
-  if ((rc = make_umma_maps(pr, &tA, &tB, &tY, &tR))) return rc;
+  CUtensorMap tA, tB, tB2, tY, tR;
+  if ((rc = make_umma_maps(pr, &tA, &tB, &tB2, &tY, &tR))) return rc;
   const UmmaParams p = umma_params(pr, pl);
   const int grid = 2 * umma_grid_workers(pl);
-  set_plan("umma_pair tile=256x%d stages=%d grid=%d pair_slots=%d tiles=%d dp_tiles=%d splits=%d "
-           "group_m=%d smem=%d workspace=%zu",
-           BN, S::STAGES, grid, pl.workers, p.num_tiles, p.dp_tiles, p.splits, p.group_m,
-           S::SMEM_BYTES, pl.bytes);
+  set_plan("umma_pair%s tile=256x%d stages=%d grid=%d pair_slots=%d tiles=%d dp_tiles=%d "
+           "splits=%d group_m=%d smem=%d workspace=%zu",
+           G ? "_gated" : "", G ? BN / 2 : BN, S::STAGES, grid, pl.workers, p.num_tiles,
+           p.dp_tiles, p.splits, p.group_m, S::SMEM_BYTES, pl.bytes);
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pair_launch_config(grid, S::THREADS, S::SMEM_BYTES, pr.stream, attr);
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tY, tR, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tB2, tY, tR, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch umma2_fused_linear_kernel");
   return DX_OK;
 }
 
-template <int MN, typename T>
+template <int MN, typename T, int NH = 2>
 int launch_decode(const Problem& pr, int dev, int sms, const DecodePlan& d) {
-  using S = DecodeShape<MN>;
-  auto kern = dx::decode_fused_linear_kernel<MN, T>;
+  using S = DecodeShape<MN, NH>;
+  auto kern = dx::decode_fused_linear_kernel<MN, T, NH>;
   int rc = ensure_smem_attr(dev, reinterpret_cast<const void*>(kern), S::SMEM_BYTES, true);
   if (rc) return rc;
   const CUtensorMapDataType dt = tma_dtype(pr.dtype);
-  CUtensorMap tW, tX;
+  CUtensorMap tW, tW2, tX;
   if ((rc = make_tmap_2d(&tW, pr.W, dt, pr.N, pr.K, pr.ldw, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B,
                          "W")))
     return rc;
+  if (pr.gated) {
+    if ((rc = make_tmap_2d(&tW2, pr.W2, dt, pr.N, pr.K, pr.ldw2, 64, 64,
+                           CU_TENSOR_MAP_SWIZZLE_128B, "W2")))
+      return rc;
+  } else {
+    tW2 = tW;  // never read
+  }
   if ((rc = make_tmap_2d(&tX, pr.X, dt, pr.K, pr.M, pr.ldx, 64, MN, CU_TENSOR_MAP_SWIZZLE_128B,
                          "X")))
     return rc;
@@ -452,15 +489,19 @@ int launch_decode(const Problem& pr, int dev, int sms, const DecodePlan& d) {
   p.partials = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + d.ticket_bytes);
   p.act = pr.act;
   p.alpha = pr.alpha;
+  p.gated = pr.gated ? 1 : 0;
+  p.bias2 = pr.bias2;
   {
     unsigned long long* tr = g_trace.load();
     const size_t need = static_cast<size_t>(d.grid) * dx::kTraceSlots * 8;
     p.trace = (tr != nullptr && g_trace_bytes.load() >= need) ? tr : nullptr;
   }
   (void)sms;
-  set_plan("decode mn=%d stages=%d grid=%d n_tiles=%d kbt=%d max_seg=%d workspace=%zu", MN,
-           S::STAGES, d.grid, d.n_tiles, d.kbt, d.max_seg, d.bytes);
-  kern<<<d.grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tW, tX, p);
+  set_plan("decode%s mn=%d halves=%d stages=%d grid=%d n_tiles=%d kbt=%d max_seg=%d "
+           "workspace=%zu",
+           pr.gated ? "_gated" : "", MN, NH, S::STAGES, d.grid, d.n_tiles, d.kbt, d.max_seg,
+           d.bytes);
+  kern<<<d.grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tW, tW2, tX, p);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch decode_fused_linear_kernel");
   return DX_OK;
@@ -493,6 +534,32 @@ int launch_simt(const Problem& pr, int sms) {
   return DX_OK;
 }
 
+template <typename T>
+int launch_simt_gated(const Problem& pr, int sms) {
+  const T* X = static_cast<const T*>(pr.X);
+  const T* Wg = static_cast<const T*>(pr.W);
+  const T* Wu = static_cast<const T*>(pr.W2);
+  const T* bg = static_cast<const T*>(pr.bias);
+  const T* bu = static_cast<const T*>(pr.bias2);
+  T* Y = static_cast<T*>(pr.Y);
+  const int M = static_cast<int>(pr.M), N = static_cast<int>(pr.N), K = static_cast<int>(pr.K);
+  const bool big = ((pr.M + 63) / 64) * ((pr.N + 63) / 64) >= 2LL * sms;
+  const int tile = big ? 64 : 32;
+  if ((pr.M + tile - 1) / tile > 65535) return fail(DX_ERR_UNSUPPORTED, "M too large for the SIMT kernel");
+  dim3 grid(static_cast<unsigned>((pr.N + tile - 1) / tile),
+            static_cast<unsigned>((pr.M + tile - 1) / tile));
+  set_plan("simt_gated tile=%d grid=%ux%u", tile, grid.x, grid.y);
+  if (big)
+    dx::simt_gated_linear_kernel<T, 64, 64><<<grid, 256, 0, pr.stream>>>(
+        X, Wg, Wu, bg, bu, Y, M, N, K, pr.ldx, pr.ldw, pr.ldw2, pr.ldy, pr.act);
+  else
+    dx::simt_gated_linear_kernel<T, 32, 32><<<grid, 256, 0, pr.stream>>>(
+        X, Wg, Wu, bg, bu, Y, M, N, K, pr.ldx, pr.ldw, pr.ldw2, pr.ldy, pr.act);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch simt_gated_linear_kernel");
+  return DX_OK;
+}
+
 // ---------------------------------------------------------- validation
 int validate(const Problem& p, int kernel) {
   if (p.dtype < DX_DTYPE_F32 || p.dtype > DX_DTYPE_BF16)
@@ -519,19 +586,27 @@ int validate(const Problem& p, int kernel) {
     return fail(DX_ERR_INVALID_ARGUMENT, "ldy=%lld < N=%lld", (long long)p.ldy, (long long)p.N);
   if (p.R != nullptr && p.ldr < p.N)
     return fail(DX_ERR_INVALID_ARGUMENT, "ldr=%lld < N=%lld", (long long)p.ldr, (long long)p.N);
+  if (p.gated) {
+    if (p.K > 0 && p.W2 == nullptr) return fail(DX_ERR_INVALID_ARGUMENT, "Wu is NULL");
+    if (p.ldw2 < p.N)
+      return fail(DX_ERR_INVALID_ARGUMENT, "ldwu=%lld < N=%lld", (long long)p.ldw2, (long long)p.N);
+  }
   return DX_OK;
 }
 
 bool umma_eligible(const Problem& p) {
   if (p.dtype == DX_DTYPE_F32 || p.K == 0) return false;
   if (!tma_ok(p.X, p.ldx) || !tma_ok(p.W, p.ldw) || !tma_ok(p.Y, p.ldy)) return false;
+  if (p.gated && !tma_ok(p.W2, p.ldw2)) return false;
   if (p.R != nullptr && !tma_ok(p.R, p.ldr)) return false;
   return true;
 }
 
 bool decode_eligible(const Problem& p) {
   if (p.dtype == DX_DTYPE_F32 || p.K == 0 || p.M > kDecodeMaxM) return false;
-  if ((p.N + kDecodeTileN - 1) / kDecodeTileN > kDecodeMaxTiles) return false;
+  const int tn = decode_tile_n(p.M, p.gated);
+  if ((p.N + tn - 1) / tn > kDecodeMaxTiles) return false;
+  if (p.gated && !tma_ok(p.W2, p.ldw2)) return false;
   return tma_ok(p.X, p.ldx) && tma_ok(p.W, p.ldw);
 }
 
@@ -539,7 +614,7 @@ int select_variant(const Problem& p, int sms, bool ws_known) {
   if (p.dtype == DX_DTYPE_F32 || p.K == 0) return DX_KERNEL_SIMT;
   if (decode_eligible(p)) {
     if (!ws_known) return DX_KERNEL_DECODE;
-    const DecodePlan d = decode_plan(p.M, p.N, p.K, sms);
+    const DecodePlan d = decode_plan(p.M, p.N, p.K, sms, p.gated);
     if (p.ws != nullptr && p.ws_bytes >= d.bytes && aligned16(p.ws)) return DX_KERNEL_DECODE;
   }
   if (umma_eligible(p)) return DX_KERNEL_UMMA;
@@ -550,9 +625,9 @@ int select_variant(const Problem& p, int sms, bool ws_known) {
 // holds it, else whole tiles only.
 UmmaPlan umma_plan_for(const Problem& p, int dev, int sms, bool single_cta_only) {
   const int slots = (p.M >= 256 && !single_cta_only) ? pair_slots<256, __nv_bfloat16>(dev, sms) : 0;
-  UmmaPlan pl = plan_umma(p.M, p.N, p.K, sms, slots, true, single_cta_only);
+  UmmaPlan pl = plan_umma(p.M, p.N, p.K, sms, slots, true, single_cta_only, p.gated);
   if (pl.bytes > 0 && (p.ws == nullptr || p.ws_bytes < pl.bytes || !aligned16(p.ws)))
-    pl = plan_umma(p.M, p.N, p.K, sms, slots, false, single_cta_only);
+    pl = plan_umma(p.M, p.N, p.K, sms, slots, false, single_cta_only, p.gated);
   return pl;
 }
 
@@ -562,18 +637,21 @@ int dispatch_typed(const Problem& p, int variant, int dev, int sms) {
     case DX_KERNEL_UMMA:
     case DX_KERNEL_UMMA_1CTA: {
       const UmmaPlan pl = umma_plan_for(p, dev, sms, variant == DX_KERNEL_UMMA_1CTA);
+      if (p.gated)
+        return pl.pair ? launch_umma2<256, T, true>(p, dev, pl) : launch_umma<256, T, true>(p, dev, pl);
       if (pl.pair)
         return pl.bn == 256 ? launch_umma2<256, T>(p, dev, pl) : launch_umma2<128, T>(p, dev, pl);
       return pl.bn == 256 ? launch_umma<256, T>(p, dev, pl) : launch_umma<128, T>(p, dev, pl);
     }
     case DX_KERNEL_DECODE: {
-      const DecodePlan d = decode_plan(p.M, p.N, p.K, sms);
-      if (d.mn == 16) return launch_decode<16, T>(p, dev, sms, d);
+      const DecodePlan d = decode_plan(p.M, p.N, p.K, sms, p.gated);
+      if (d.mn == 16)
+        return d.nh == 4 ? launch_decode<16, T, 4>(p, dev, sms, d) : launch_decode<16, T>(p, dev, sms, d);
       if (d.mn == 32) return launch_decode<32, T>(p, dev, sms, d);
       return launch_decode<64, T>(p, dev, sms, d);
     }
     default:
-      return launch_simt<T>(p, sms);
+      return p.gated ? launch_simt_gated<T>(p, sms) : launch_simt<T>(p, sms);
   }
 }
 
@@ -603,7 +681,7 @@ int run(const Problem& p, int kernel) {
                   "decode kernel needs fp16/bf16, 0 < K, M <= %d, N <= %lld, and "
                   "16-byte-aligned X/W with row pitches that are multiples of 16 bytes",
                   kDecodeMaxM, (long long)(kDecodeMaxTiles * kDecodeTileN));
-    const DecodePlan d = decode_plan(p.M, p.N, p.K, sms);
+    const DecodePlan d = decode_plan(p.M, p.N, p.K, sms, p.gated);
     if (p.ws == nullptr || p.ws_bytes < d.bytes || !aligned16(p.ws))
       return fail(DX_ERR_WORKSPACE, "decode kernel needs a 16-byte-aligned workspace of %zu bytes",
                   d.bytes);
@@ -612,7 +690,7 @@ int run(const Problem& p, int kernel) {
     case DX_DTYPE_F32:
       if (variant != DX_KERNEL_SIMT)
         return fail(DX_ERR_UNSUPPORTED, "fp32 runs only on the exact-fp32 SIMT kernel");
-      return launch_simt<float>(p, sms);
+      return p.gated ? launch_simt_gated<float>(p, sms) : launch_simt<float>(p, sms);
     case DX_DTYPE_F16:
       return dispatch_typed<__half>(p, variant, dev, sms);
     default:
@@ -657,6 +735,32 @@ size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K, int dtype
     return plan_umma(M, N, K, sms, slots, true, single).bytes;
   }
   return 0;
+}
+
+int dx_fused_gated_linear(const void* X, const void* Wg, const void* Wu, const void* bias_g,
+                          const void* bias_u, void* Y, int64_t M, int64_t N, int64_t K,
+                          int64_t ldx, int64_t ldwg, int64_t ldwu, int64_t ldy, int dtype, int act,
+                          int kernel, void* workspace, size_t workspace_bytes, void* stream) {
+  Problem p{X, Wg, bias_g, nullptr, Y, M, N, K, ldx, ldwg, 0, ldy, dtype, act, workspace,
+            workspace_bytes, static_cast<cudaStream_t>(stream)};
+  p.gated = true;
+  p.W2 = Wu;
+  p.bias2 = bias_u;
+  p.ldw2 = ldwu;
+  return run(p, kernel);
+}
+
+size_t dx_fused_gated_linear_workspace_size(int64_t M, int64_t N, int64_t K, int dtype,
+                                            int kernel) {
+  t_last_error.clear();
+  if (M <= 0 || N <= 0 || K <= 0 || dtype == DX_DTYPE_F32 || kernel == DX_KERNEL_SIMT) return 0;
+  int dev = 0, sms = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || device_sms(dev, &sms) != DX_OK) return 0;
+  const int tn = decode_tile_n(M, true);
+  const bool fits = M <= kDecodeMaxM && (N + tn - 1) / tn <= kDecodeMaxTiles;
+  if (kernel == DX_KERNEL_AUTO) kernel = fits ? DX_KERNEL_DECODE : DX_KERNEL_UMMA;
+  if (kernel == DX_KERNEL_DECODE && fits) return decode_plan(M, N, K, sms, true).bytes;
+  return 0;  // the gated tensor-core kernels take no split tail
 }
 
 int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype) {

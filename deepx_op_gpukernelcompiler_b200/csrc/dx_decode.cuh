@@ -16,9 +16,15 @@
 //     same number of bytes regardless of N/K; a CTA's range crosses at most
 //     a few n-tiles.
 //   * partial sums of a tile that several CTAs share go to a workspace as
-//     fp32; the last CTA to finish a tile (atomic ticket) sums the partials
-//     in fixed segment order — deterministic, no float atomics — applies
-//     bias, activation and residual, stores Y, and resets the ticket to 0.
+//     fp32; the last CTA to arrive at a tile (atomic counter) sums the
+//     others' partials and its own registers in fixed segment order —
+//     deterministic, no float atomics — applies bias, activation and
+//     residual, stores Y, and resets the counter to 0.
+//   * gated form (p.gated): Y = act(X Wg + bg) * (X Wu + bu).  A work unit
+//     covers NH/2 x 128 output columns: its first NH/2 UMMA halves read Wg's
+//     columns, the others Wu's same columns; the epilogue combines them.
+//     With NH = 4 (M <= 16) each weight's row segment read is 512 B, as in
+//     the plain form; NH = 2 (256 B segments) serves M up to 64.
 // Bounded waits and exit draining as in dx_umma_gemm.cuh.
 #pragma once
 
@@ -29,7 +35,7 @@ namespace dx {
 
 struct DecodeParams {
   int M, N, K;
-  int n_tiles;          // ceil(N / 256)
+  int n_tiles;          // ceil(N / 256); gated: ceil(N / 128)
   int kbt;              // k-blocks (64 deep) per tile
   long long units;      // n_tiles * kbt
   int grid;             // CTAs
@@ -39,13 +45,19 @@ struct DecodeParams {
   const void* residual; // [M, N] (ldr) or nullptr
   void* Y;
   float* partials;      // [n_tiles][max_seg][MN][256] fp32
-  int* tickets;         // [n_tiles][4] (per warp quarter), zero between calls
+  int* tickets;         // [n_tiles][4] (per warp quarter): arrivals | written << 16;
+                        // zero between calls
   int act;
   float alpha;          // Y = act(alpha * acc + bias) + R
+  int gated;            // Y = act(acc_g + bias) * (acc_u + bias2)
+  const void* bias2;    // gated: up-projection bias (N) or nullptr
   // Optional timeline (dx_set_trace_buffer), kTraceSlots stamps per CTA:
-  // [0] after set-up, [1] first and [2] last TMA issue, [3] last MMA issue,
-  // [4 + i] epilogue of work item i finished (i < 9), [13] the SM's id,
-  // [14] epilogue warps done, [15] exit.
+  // [0] after set-up, [1] first and [2] last TMA issue, [3] last MMA issue;
+  // for the CTA's last work item (warp quarter 0): [4] accumulator ready,
+  // [5] accumulator read, [6] arrival counted, [7] own partial published or
+  // the others' found written, [8] fix-up sums done, [9] item finished;
+  // [10 + i] work item i finished (i < 2), [12] kernel entry, [13] the SM's
+  // id, [14] epilogue warps done, [15] exit.
   unsigned long long* trace;
 };
 
@@ -54,19 +66,20 @@ __device__ __forceinline__ void decode_trace(const DecodeParams& p, int slot) {
     p.trace[static_cast<size_t>(blockIdx.x) * kTraceSlots + slot] = global_timer_ns();
 }
 
-template <int MN>
+// NH: 128-column UMMA halves per work unit (2; 4 for the wide gated form).
+template <int MN, int NH = 2>
 struct DecodeShape {
-  static constexpr int NT = 256;                   // W columns per work unit
+  static constexpr int NT = 128 * NH;              // W columns staged per work unit
   static constexpr int BK = 64;
   static constexpr int W_BOX_BYTES = 64 * BK * 2;  // [64 k x 64 n]
-  static constexpr int W_BYTES = 4 * W_BOX_BYTES;  // 256 n per stage
   static constexpr int HALF_BYTES = 2 * W_BOX_BYTES;
+  static constexpr int W_BYTES = NH * HALF_BYTES;  // NT n per stage
   static constexpr int X_BYTES = MN * BK * 2;      // MN rows x 128 B
   static constexpr int STAGE_BYTES = W_BYTES + X_BYTES;
-  static constexpr int STAGES = MN <= 32 ? 6 : 5;
-  // two buffers x two halves x MN fp32 columns, as a power of two >= 32
-  static constexpr int ACC_COLS = 2 * MN;
-  static constexpr int TMEM_COLS = 4 * MN < 32 ? 32 : 4 * MN;
+  static constexpr int STAGES = NH == 4 ? 3 : (MN <= 32 ? 6 : 5);
+  // two buffers x NH halves x MN fp32 columns, as a power of two >= 32
+  static constexpr int ACC_COLS = NH * MN;
+  static constexpr int TMEM_COLS = 2 * ACC_COLS < 32 ? 32 : 2 * ACC_COLS;
   static constexpr int THREADS = 192;
   static constexpr int OFF_W = 0;
   static constexpr int OFF_X = OFF_W + STAGES * W_BYTES;
@@ -80,6 +93,7 @@ struct DecodeShape {
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // tmem base, abort flag
   static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 16;
   static_assert(MN == 16 || MN == 32 || MN == 64, "decode batch tile");
+  static_assert(NH == 2 || (NH == 4 && MN == 16), "halves per unit");
   static_assert(X_BYTES % 1024 == 0, "X stage alignment");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
 };
@@ -91,11 +105,33 @@ __device__ __forceinline__ int decode_cta_of(long long u, long long U, int G) {
   return g;
 }
 
-template <int MN, typename T>
-__global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
+// Bounded wait until the high half (partials written) of *ctr reaches
+// `target`.  Returns false when the CTA's abort flag is raised or the wait
+// exceeded kWaitLimitNs (then it raises both flags itself).
+__device__ __forceinline__ bool decode_wait_written(const int* ctr, int target,
+                                                    volatile int* abort_flag) {
+  const uint64_t t0 = global_timer_ns();
+  uint32_t spins = 0;
+  while ((*reinterpret_cast<const volatile int*>(ctr) >> 16) < target) {
+    __nanosleep(32);
+    if ((++spins & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (global_timer_ns() - t0 > kWaitLimitNs) {
+        *abort_flag = 1;
+        atomicOr(&g_device_status, 1);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+template <int MN, typename T, int NH = 2>
+__global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
     decode_fused_linear_kernel(const __grid_constant__ CUtensorMap tmW,
+                               const __grid_constant__ CUtensorMap tmW2,
                                const __grid_constant__ CUtensorMap tmX, const DecodeParams p) {
-  using S = DecodeShape<MN>;
+  using S = DecodeShape<MN, NH>;
   using Tr = ElemTraits<T>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw_u32 = smem_u32(smem_raw);
@@ -109,6 +145,7 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
   volatile int* const abort_flag = reinterpret_cast<volatile int*>(base_ptr + S::OFF_MISC + 4);
   auto bar = [bars](int i) { return bars + 8u * static_cast<uint32_t>(i); };
 
+  if (threadIdx.x == 0) decode_trace(p, 12);
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int g = blockIdx.x;
@@ -131,6 +168,7 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmW);
+    if (p.gated) tma_prefetch_desc(&tmW2);
     tma_prefetch_desc(&tmX);
   }
   if (warp == 1) {
@@ -153,6 +191,9 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
   if (warp == 0) {
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
+      // W is read exactly once: evict-first, so it does not push the split-K
+      // partials (read back by the tile's last CTA) out of L2.
+      const uint64_t pol_w = make_l2_policy_evict_first();
       int s = 0;
       uint32_t ph = 0, issued = 0;
       bool ok = true;
@@ -168,9 +209,16 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
           const uint32_t fb = bar(S::BAR_FULL + s);
           mbar_arrive_expect_tx(fb, S::STAGE_BYTES);
 #pragma unroll
-          for (int j = 0; j < 4; ++j)
-            tma_load_2d(&tmW, sW + s * S::W_BYTES + j * S::W_BOX_BYTES, fb, t * S::NT + 64 * j,
-                        kb * S::BK);
+          for (int j = 0; j < 2 * NH; ++j) {
+            // Gated: halves 0 .. NH/2-1 from Wg, the rest from Wu, at the
+            // unit's NH/2 x 128 output columns.
+            const int h = j >> 1;
+            const CUtensorMap* const mw = (p.gated && h >= NH / 2) ? &tmW2 : &tmW;
+            const int col = p.gated ? t * (S::NT / 2) + (h % (NH / 2)) * 128 + 64 * (j & 1)
+                                    : t * S::NT + 64 * j;
+            tma_load_2d_hint(mw, sW + s * S::W_BYTES + j * S::W_BOX_BYTES, fb, col, kb * S::BK,
+                             pol_w);
+          }
           tma_load_2d(&tmX, sX + s * S::X_BYTES, fb, kb * S::BK, 0);
           if (issued == 0) decode_trace(p, 1);
           ++issued;
@@ -213,7 +261,7 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
           // X tile: K-major rows of 128 B, 8-row groups 1024 B apart.
           const uint64_t bd = smem_desc_sw128(sX + s * S::X_BYTES, 16, 1024);
 #pragma unroll
-          for (int h = 0; h < 2; ++h) {
+          for (int h = 0; h < NH; ++h) {
             // W^T half: MN-major (n contiguous), two 64-wide n groups one box
             // apart, 8-row k groups 1024 B apart; +2048 B per K=16 step.
             const uint64_t ad =
@@ -241,6 +289,7 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
     const int q = warp & 3;
     const int n_local = q * 32 + lane;
     const T* const bias = static_cast<const T*>(p.bias);
+    const T* const bias2 = static_cast<const T*>(p.bias2);
     const T* const res = static_cast<const T*>(p.residual);
     T* const Y = static_cast<T*>(p.Y);
     const int M = p.M;
@@ -252,18 +301,31 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
       u += kb1 - kb0;
       const int b = local & 1;
       const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
-      // The item's bias, loaded while its accumulator is still being built.
-      float bv[2];
+      // The item's bias, loaded while its accumulator is still being built
+      // (gated: bv[hp] gate and bv[hp + NH/2] up bias of output column
+      // t * NT/2 + hp * 128 + n_local).
+      float bv[NH];
+      if (p.gated) {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int n = t * S::NT + h * 128 + n_local;
-        bv[h] = (bias != nullptr && n < p.N) ? Tr::to_float(bias[n]) : 0.0f;
+        for (int hp = 0; hp < NH / 2; ++hp) {
+          const int n = t * (S::NT / 2) + hp * 128 + n_local;
+          bv[hp] = (bias != nullptr && n < p.N) ? Tr::to_float(bias[n]) : 0.0f;
+          bv[hp + NH / 2] = (bias2 != nullptr && n < p.N) ? Tr::to_float(bias2[n]) : 0.0f;
+        }
+      } else {
+#pragma unroll
+        for (int h = 0; h < NH; ++h) {
+          const int n = t * S::NT + h * 128 + n_local;
+          bv[h] = (bias != nullptr && n < p.N) ? Tr::to_float(bias[n]) : 0.0f;
+        }
       }
       if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
       tc_fence_after();
-      float acc[2][MN];
+      const bool tr = q == 0 && lane == 0;
+      if (tr) decode_trace(p, 4);
+      float acc[NH][MN];
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
+      for (int h = 0; h < NH; ++h) {
         const uint32_t taddr = tmem_base + static_cast<uint32_t>(b * S::ACC_COLS + h * MN) +
                                (static_cast<uint32_t>(q * 32) << 16);
         if constexpr (MN == 16) {
@@ -286,85 +348,171 @@ __global__ void __launch_bounds__(DecodeShape<MN>::THREADS, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(bar(S::BAR_TEMPTY + b));
+      if (tr) decode_trace(p, 5);
 
       if (!(kb0 == 0 && kb1 == p.kbt)) {
-        // Tile shared with other CTAs: publish this segment's partial sums
-        // ([MN][256] fp32, lanes contiguous in n).
+        // Tile shared with other CTAs.  One counter word per (tile, warp
+        // quarter): arrivals in the low 16 bits, partials written in the high
+        // 16 bits.  Each CTA arrives first; the last to arrive keeps its sums
+        // in registers, every other one publishes its partial ([MN][256] fp32,
+        // lanes contiguous in n) and then counts it written.  Each warp
+        // finishes its own 2 x 32 columns, so no cross-warp barrier can be
+        // left waiting on an exit.
         const int first = decode_cta_of(static_cast<long long>(t) * p.kbt, U, p.grid);
         const int last = decode_cta_of(static_cast<long long>(t + 1) * p.kbt - 1, U, p.grid);
         const int nseg = last - first + 1;
+        const int own = g - first;
         float* const part_t = p.partials + static_cast<size_t>(t) * p.max_seg * MN * S::NT;
-        float* const mine = part_t + static_cast<size_t>(g - first) * MN * S::NT;
+        int* const ctr = p.tickets + t * 4 + q;
+        int old = 0;
+        if (lane == 0) old = atomicAdd(ctr, 1);
+        old = __shfl_sync(0xffffffffu, old, 0);
+        if (tr) decode_trace(p, 6);
+        if ((old & 0xffff) != nseg - 1) {
+          float* const mine = part_t + static_cast<size_t>(own) * MN * S::NT;
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+          for (int h = 0; h < NH; ++h)
 #pragma unroll
-          for (int m = 0; m < MN; ++m)
-            if (m < M) mine[m * S::NT + h * 128 + n_local] = acc[h][m];
-        __threadfence();
-        __syncwarp();
-        // One ticket per (tile, warp quarter): each warp finishes its own 2 x 32
-        // columns, so no cross-warp barrier can be left waiting on an exit.
-        int ticket = 0;
-        if (lane == 0) ticket = atomicAdd(p.tickets + t * 4 + q, 1);
-        ticket = __shfl_sync(0xffffffffu, ticket, 0);
-        if (ticket != nseg - 1) {
-          if (q == 0 && lane == 0 && local < 9) decode_trace(p, 4 + local);
+            for (int m = 0; m < MN; ++m)
+              if (m < M) mine[m * S::NT + h * 128 + n_local] = acc[h][m];
+          __threadfence();
+          __syncwarp();
+          if (lane == 0) atomicAdd(ctr, 1 << 16);
+          if (tr) {
+            decode_trace(p, 7);
+            decode_trace(p, 9);
+            if (local < 2) decode_trace(p, 10 + local);
+          }
           continue;
         }
+        // Last to arrive: the other nseg - 1 CTAs have arrived; wait (bounded)
+        // until their partials are written — usually long done.
+        int ok = 1;
+        if (lane == 0 && (old >> 16) != nseg - 1)
+          ok = decode_wait_written(ctr, nseg - 1, abort_flag) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        if (!ok) break;
         __threadfence();
-        // Fixed summation order over segments: bitwise identical results
-        // whichever CTA finishes last.  The loads of SB segments (128 values
-        // per thread) are all issued before any of them is added, so a tile
-        // split over many CTAs costs few memory round trips.
-        // (With MN = 64 one half-tile of one segment, 64 values, at a time.)
-        constexpr int SB = MN <= 32 ? 64 / MN : 1;
-        constexpr int NH = MN <= 32 ? 2 : 1;
+        if (tr) decode_trace(p, 7);
+        // Fixed summation order over segments (0 + s_0 + s_1 + ...): bitwise
+        // identical results whichever CTA finishes last.
+        if constexpr (MN == 64) {
+          // Registers cannot hold a second [NH][64] array: this CTA's segment
+          // goes through memory like the others, one half-tile at a time.
+          float* const mine = part_t + static_cast<size_t>(own) * MN * S::NT;
 #pragma unroll
-        for (int h = 0; h < 2; ++h)
+          for (int h = 0; h < NH; ++h)
 #pragma unroll
-          for (int m = 0; m < MN; ++m) acc[h][m] = 0.0f;
-        for (int sg0 = 0; sg0 < nseg; sg0 += SB) {
-#pragma unroll
-          for (int h0 = 0; h0 < 2; h0 += NH) {
-            float f[SB][NH][MN];
-#pragma unroll
-            for (int sb = 0; sb < SB; ++sb) {
-              const float* src = part_t + static_cast<size_t>(sg0 + sb) * MN * S::NT;
-#pragma unroll
-              for (int hh = 0; hh < NH; ++hh)
-#pragma unroll
-                for (int m = 0; m < MN; ++m)
-                  f[sb][hh][m] = (sg0 + sb < nseg && m < M)
-                                     ? __ldcg(src + m * S::NT + (h0 + hh) * 128 + n_local)
-                                     : 0.0f;
+            for (int m = 0; m < MN; ++m) {
+              if (m < M) mine[m * S::NT + h * 128 + n_local] = acc[h][m];
+              acc[h][m] = 0.0f;
             }
+          for (int sg = 0; sg < nseg; ++sg) {
+            const float* src = part_t + static_cast<size_t>(sg) * MN * S::NT;
 #pragma unroll
-            for (int sb = 0; sb < SB; ++sb)
-              if (sg0 + sb < nseg) {
+            for (int h = 0; h < NH; ++h) {
+              float fv[MN];
 #pragma unroll
-                for (int hh = 0; hh < NH; ++hh)
+              for (int m = 0; m < MN; ++m)
+                fv[m] = m < M ? __ldcg(src + m * S::NT + h * 128 + n_local) : 0.0f;
 #pragma unroll
-                  for (int m = 0; m < MN; ++m) acc[h0 + hh][m] += f[sb][hh][m];
+              for (int m = 0; m < MN; ++m) acc[h][m] += fv[m];
+            }
+          }
+        } else {
+          // This CTA's segment comes from registers.  The loads of SB other
+          // segments are issued before any of them is added, so a tile split
+          // over many CTAs costs few memory round trips.  Each pass loads LH
+          // halves of SB segments.
+          constexpr int LH = NH < 64 / MN ? NH : 64 / MN;
+          constexpr int SB = 96 / (LH * MN) > 1 ? 96 / (LH * MN) : 1;
+          const int n_other = nseg - 1;
+          float sum[NH][MN];
+#pragma unroll
+          for (int h = 0; h < NH; ++h)
+#pragma unroll
+            for (int m = 0; m < MN; ++m) sum[h][m] = 0.0f;
+          for (int o0 = 0; o0 < n_other; o0 += SB) {
+#pragma unroll
+            for (int h0 = 0; h0 < NH; h0 += LH) {
+              float f[SB][LH][MN];
+#pragma unroll
+              for (int sb = 0; sb < SB; ++sb) {
+                const int o = o0 + sb;
+                const int sg = o < own ? o : o + 1;
+                const float* src = part_t + static_cast<size_t>(sg) * MN * S::NT;
+#pragma unroll
+                for (int hh = 0; hh < LH; ++hh)
+#pragma unroll
+                  for (int m = 0; m < MN; ++m)
+                    f[sb][hh][m] = (o < n_other && m < M)
+                                       ? __ldcg(src + m * S::NT + (h0 + hh) * 128 + n_local)
+                                       : 0.0f;
               }
+#pragma unroll
+              for (int sb = 0; sb < SB; ++sb) {
+                const int o = o0 + sb;
+                if (o < n_other) {
+                  if (o == own) {  // segment `own` precedes this one (segment own + 1)
+#pragma unroll
+                    for (int hh = 0; hh < LH; ++hh)
+#pragma unroll
+                      for (int m = 0; m < MN; ++m) sum[h0 + hh][m] += acc[h0 + hh][m];
+                  }
+#pragma unroll
+                  for (int hh = 0; hh < LH; ++hh)
+#pragma unroll
+                    for (int m = 0; m < MN; ++m) sum[h0 + hh][m] += f[sb][hh][m];
+                }
+              }
+            }
+          }
+          if (own == n_other) {  // this CTA's segment is the tile's last
+#pragma unroll
+            for (int h = 0; h < NH; ++h)
+#pragma unroll
+              for (int m = 0; m < MN; ++m) sum[h][m] += acc[h][m];
+          }
+#pragma unroll
+          for (int h = 0; h < NH; ++h)
+#pragma unroll
+            for (int m = 0; m < MN; ++m) acc[h][m] = sum[h][m];
+        }
+        if (lane == 0) *ctr = 0;  // every CTA of the tile has arrived and written
+        if (tr) decode_trace(p, 8);
+      }
+      if (p.gated) {
+#pragma unroll
+        for (int hp = 0; hp < NH / 2; ++hp) {
+          const int n = t * (S::NT / 2) + hp * 128 + n_local;
+          if (n < p.N) {
+#pragma unroll
+            for (int m = 0; m < MN; ++m)
+              if (m < M)
+                Y[m * p.ldy + n] = Tr::from_float(act_apply(acc[hp][m] + bv[hp], p.act) *
+                                                  (acc[hp + NH / 2][m] + bv[hp + NH / 2]));
           }
         }
-        if (lane == 0) p.tickets[t * 4 + q] = 0;
-      }
+      } else {
 #pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int n = t * S::NT + h * 128 + n_local;
-        if (n < p.N) {
+        for (int h = 0; h < NH; ++h) {
+          const int n = t * S::NT + h * 128 + n_local;
+          if (n < p.N) {
 #pragma unroll
-          for (int m = 0; m < MN; ++m) {
-            if (m < M) {
-              float y = act_apply(fmaf(p.alpha, acc[h][m], bv[h]), p.act);
-              if (res != nullptr) y += Tr::to_float(res[m * p.ldr + n]);
-              Y[m * p.ldy + n] = Tr::from_float(y);
+            for (int m = 0; m < MN; ++m) {
+              if (m < M) {
+                float y = act_apply(fmaf(p.alpha, acc[h][m], bv[h]), p.act);
+                if (res != nullptr) y += Tr::to_float(res[m * p.ldr + n]);
+                Y[m * p.ldy + n] = Tr::from_float(y);
+              }
             }
           }
         }
       }
-      if (q == 0 && lane == 0 && local < 9) decode_trace(p, 4 + local);
+      if (q == 0 && lane == 0) {
+        decode_trace(p, 9);
+        if (local < 2) decode_trace(p, 10 + local);
+      }
     }
     if (q == 0 && lane == 0) decode_trace(p, 14);
   }

@@ -7,7 +7,8 @@
 //     (rows not a multiple of 16 bytes), and K == 0.
 // Each thread accumulates its outputs over k = 0..K-1 in order, so results
 // are deterministic.  Tiles are BM x BN with 256 threads in a 16 x 16 grid;
-// thread (ty, tx) owns rows ty + 16 i and columns tx + 16 j.
+// thread (ty, tx) owns rows ty + 16 i and columns tx + 16 j.  A gated form
+// (two weight matrices, Y = act(X Wg + bg) * (X Wu + bu)) shares the tiling.
 #pragma once
 
 #include <type_traits>
@@ -79,6 +80,83 @@ __global__ void __launch_bounds__(256)
       v = act_apply<!std::is_same<T, float>::value>(v, act);
       if (R != nullptr) v += Tr::to_float(R[m * ldr + n]);
       Y[m * ldy + n] = Tr::from_float(v);
+    }
+  }
+}
+
+// Gated form: Y = act(X Wg + bg) * (X Wu + bu), same tiling, two accumulator
+// sets (gate and up) fed by one X tile.
+template <typename T, int BM, int BN>
+__global__ void __launch_bounds__(256)
+    simt_gated_linear_kernel(const T* __restrict__ X, const T* __restrict__ Wg,
+                             const T* __restrict__ Wu, const T* __restrict__ bg,
+                             const T* __restrict__ bu, T* __restrict__ Y, int M, int N, int K,
+                             long long ldx, long long ldwg, long long ldwu, long long ldy, int act) {
+  using Tr = ElemTraits<T>;
+  constexpr int BK = 16;
+  constexpr int TM = BM / 16;
+  constexpr int TN = BN / 16;
+  __shared__ float As[BK][BM + 1];
+  __shared__ float Gs[BK][BN];
+  __shared__ float Us[BK][BN];
+  const int tx = threadIdx.x & 15;
+  const int ty = threadIdx.x >> 4;
+  const int m0 = blockIdx.y * BM;
+  const int n0 = blockIdx.x * BN;
+
+  float ag[TM][TN], au[TM][TN];
+#pragma unroll
+  for (int i = 0; i < TM; ++i)
+#pragma unroll
+    for (int j = 0; j < TN; ++j) ag[i][j] = au[i][j] = 0.0f;
+
+  for (int k0 = 0; k0 < K; k0 += BK) {
+    for (int idx = threadIdx.x; idx < BM * BK; idx += 256) {
+      const int mm = idx / BK, kk = idx % BK;
+      const int m = m0 + mm, k = k0 + kk;
+      As[kk][mm] = (m < M && k < K) ? Tr::to_float(X[m * ldx + k]) : 0.0f;
+    }
+    for (int idx = threadIdx.x; idx < BK * BN; idx += 256) {
+      const int kk = idx / BN, nn = idx % BN;
+      const int k = k0 + kk, n = n0 + nn;
+      const bool in = k < K && n < N;
+      Gs[kk][nn] = in ? Tr::to_float(Wg[k * ldwg + n]) : 0.0f;
+      Us[kk][nn] = in ? Tr::to_float(Wu[k * ldwu + n]) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      float a[TM], g[TN], u[TN];
+#pragma unroll
+      for (int i = 0; i < TM; ++i) a[i] = As[kk][ty + 16 * i];
+#pragma unroll
+      for (int j = 0; j < TN; ++j) {
+        g[j] = Gs[kk][tx + 16 * j];
+        u[j] = Us[kk][tx + 16 * j];
+      }
+#pragma unroll
+      for (int i = 0; i < TM; ++i)
+#pragma unroll
+        for (int j = 0; j < TN; ++j) {
+          ag[i][j] = fmaf(a[i], g[j], ag[i][j]);
+          au[i][j] = fmaf(a[i], u[j], au[i][j]);
+        }
+    }
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int i = 0; i < TM; ++i) {
+    const int m = m0 + ty + 16 * i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < TN; ++j) {
+      const int n = n0 + tx + 16 * j;
+      if (n >= N) continue;
+      float gv = ag[i][j], uv = au[i][j];
+      if (bg != nullptr) gv += Tr::to_float(bg[n]);
+      if (bu != nullptr) uv += Tr::to_float(bu[n]);
+      Y[m * ldy + n] = Tr::from_float(act_apply<!std::is_same<T, float>::value>(gv, act) * uv);
     }
   }
 }

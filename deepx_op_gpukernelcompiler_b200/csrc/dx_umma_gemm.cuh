@@ -27,6 +27,12 @@
 //            the staging buffer), converts, and TMA-stores.  The output tile
 //            crosses HBM exactly once; the next tile's main loop runs in the
 //            other accumulator meanwhile.
+// Gated form (kGated): Y = act(X Wg + bg) * (X Wu + bu), the first half of a
+// gated FFN.  A BN-wide accumulator holds BN/2 gate columns followed by the
+// matching BN/2 up columns: the producer fills the B operand's first half
+// from Wg and its second half from Wu (for pairs: the leader stages Wg, the
+// peer Wu), one MMA covers both, and the epilogue combines column c with
+// column c + BN/2 into one output column.  Output tiles are BN/2 wide.
 // Tiles are visited M-fastest inside groups of `group_m` m-tiles, so a band
 // of X stays in L2 while all of W streams past it; Y and R are streamed with
 // an evict-first L2 policy.
@@ -44,6 +50,7 @@ struct UmmaParams {
   int m_tiles, n_tiles, k_blocks, num_tiles;  // tiles of (rows per tile) x BN
   int group_m;                                // m-tiles per raster group
   const void* bias;                           // N elements, or nullptr
+  const void* bias2;                          // gated: up-projection bias, or nullptr
   int act;
   int has_residual;
   float alpha;                                // Y = act(alpha * acc + bias) + R
@@ -286,6 +293,90 @@ __device__ __forceinline__ bool epilogue_tile(const EpilogueCtx<T>& c, uint32_t 
   return true;
 }
 
+// Gated form of epilogue_tile: the accumulator holds BN/2 gate columns then
+// BN/2 up columns; output column n0 + j = act(gate_j + bg) * (up_j + bu).
+// `c` must have no bias, no activation, alpha 1 and no residual (they are
+// applied here); the biases arrive spread over the warp as in epi_load_bias.
+template <int BN, typename T, typename Release>
+__device__ __forceinline__ bool epilogue_tile_gated(const EpilogueCtx<T>& c, uint32_t tmem_acc,
+                                                    int q, int lane, int row0, int n0, int act,
+                                                    bool has_bg, bool has_bu, uint4 bg_reg,
+                                                    uint4 bu_reg, uint32_t& it,
+                                                    volatile int* abort_flag, Release release) {
+  using Tr = ElemTraits<T>;
+  constexpr int BNO = BN / 2;
+  const int row_base = row0 + q * 32;
+  const bool rows_live = row_base < c.M;
+  const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(q * 32) << 16);
+  int n_chunks = 0;
+  if (rows_live) {
+    const int cols = min(BNO, c.N - n0);
+    n_chunks = cols > 0 ? (cols + 31) / 32 : 0;
+  }
+  if (n_chunks == 0) {
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) release();
+    return true;
+  }
+  // Both halves of chunk ch + 1 are loading while chunk ch is finished.
+  uint32_t rg[32], ru[32];
+  tmem_ld_32x32b_x32(lane_addr, rg);
+  tmem_ld_32x32b_x32(lane_addr + static_cast<uint32_t>(BNO), ru);
+#pragma unroll 1
+  for (int ch = 0; ch < n_chunks; ++ch) {
+    const int n_c = n0 + 32 * ch;
+    epi_chunk_begin(c, n_c, row_base, lane, it);
+    tmem_wait_ld();
+    float g[32], u[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      g[j] = __uint_as_float(rg[j]);
+      u[j] = __uint_as_float(ru[j]);
+    }
+    if (ch + 1 < n_chunks) {
+      tmem_ld_32x32b_x32(lane_addr + static_cast<uint32_t>(32 * (ch + 1)), rg);
+      tmem_ld_32x32b_x32(lane_addr + static_cast<uint32_t>(BNO + 32 * (ch + 1)), ru);
+    } else {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) release();
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int src = 4 * ch + j;  // lane holding columns n_c + 8j .. n_c + 8j + 8
+      const uint32_t gv[4] = {__shfl_sync(0xffffffffu, bg_reg.x, src),
+                              __shfl_sync(0xffffffffu, bg_reg.y, src),
+                              __shfl_sync(0xffffffffu, bg_reg.z, src),
+                              __shfl_sync(0xffffffffu, bg_reg.w, src)};
+      const uint32_t uv[4] = {__shfl_sync(0xffffffffu, bu_reg.x, src),
+                              __shfl_sync(0xffffffffu, bu_reg.y, src),
+                              __shfl_sync(0xffffffffu, bu_reg.z, src),
+                              __shfl_sync(0xffffffffu, bu_reg.w, src)};
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const float2 fg = Tr::unpack2(gv[h]);
+        const float2 fu = Tr::unpack2(uv[h]);
+        if (has_bg) {
+          g[8 * j + 2 * h] += fg.x;
+          g[8 * j + 2 * h + 1] += fg.y;
+        }
+        if (has_bu) {
+          u[8 * j + 2 * h] += fu.x;
+          u[8 * j + 2 * h + 1] += fu.y;
+        }
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) g[j] = act_apply(g[j], act) * u[j];
+    if (!epi_chunk_end(c, g, n_c, row_base, lane, it, abort_flag, make_uint4(0u, 0u, 0u, 0u), ch)) {
+      if (ch + 1 < n_chunks) tmem_wait_ld();
+      return false;
+    }
+  }
+  return true;
+}
+
 // Bounded wait until *ctr reaches `target` (other CTAs of this launch add to
 // it; all CTAs of the launch are resident).  Returns false on timeout.
 __device__ __forceinline__ bool wait_counter(const int* ctr, int target, volatile int* abort_flag) {
@@ -443,10 +534,11 @@ struct UmmaShape {
   static_assert(BN % 64 == 0 && BN >= 64 && BN <= 256, "UMMA N");
 };
 
-template <int BN, typename T>
+template <int BN, typename T, bool kGated = false>
 __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
     umma_fused_linear_kernel(const __grid_constant__ CUtensorMap tmA,
                              const __grid_constant__ CUtensorMap tmB,
+                             const __grid_constant__ CUtensorMap tmB2,
                              const __grid_constant__ CUtensorMap tmY,
                              const __grid_constant__ CUtensorMap tmR, const UmmaParams p) {
   using S = UmmaShape<BN>;
@@ -483,6 +575,7 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (kGated) tma_prefetch_desc(&tmB2);
     tma_prefetch_desc(&tmY);
     if (p.has_residual) tma_prefetch_desc(&tmR);
   }
@@ -508,7 +601,7 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
         if (!umma_item(p, blockIdx.x, i, w)) break;
         int mb, nb;
         umma_tile_coords(p, w.tile, mb, nb);
-        const int m0 = mb * S::BM, n0 = nb * BN;
+        const int m0 = mb * S::BM, n0 = nb * (kGated ? BN / 2 : BN);
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(bar(S::BAR_EMPTY + s), ph ^ 1u, abort_flag)) {
             ok = false;
@@ -518,9 +611,17 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
           mbar_arrive_expect_tx(fb, S::STAGE_BYTES);
           tma_load_2d_hint(&tmA, sA + s * S::A_BYTES, fb, kb * S::BK, m0, pol);
 #pragma unroll
-          for (int j = 0; j < BN / 64; ++j)
-            tma_load_2d_hint(&tmB, sB + s * S::B_BYTES + j * S::B_BOX_BYTES, fb, n0 + 64 * j,
-                             kb * S::BK, pol);
+          for (int j = 0; j < BN / 64; ++j) {
+            if constexpr (kGated) {
+              // First half of the boxes from Wg, second half from Wu.
+              constexpr int HB = BN / 128;
+              tma_load_2d_hint(j < HB ? &tmB : &tmB2, sB + s * S::B_BYTES + j * S::B_BOX_BYTES, fb,
+                               n0 + 64 * (j % HB), kb * S::BK, pol);
+            } else {
+              tma_load_2d_hint(&tmB, sB + s * S::B_BYTES + j * S::B_BOX_BYTES, fb, n0 + 64 * j,
+                               kb * S::BK, pol);
+            }
+          }
           ++issued;
           if (++s == S::STAGES) {
             s = 0;
@@ -596,6 +697,16 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
     c.ebuf_ptr0 = base_ptr + S::OFF_EPI + e * 2 * kEpiBufBytes;
     c.rbar0 = bar(S::BAR_RES + e * 2);
     c.pol_stream = make_l2_policy_evict_first();
+    // Gated: biases are added before the activation in epilogue_tile_gated;
+    // cg / cu only load them.
+    EpilogueCtx<T> cg = c, cu = c;
+    if (kGated) {
+      cu.bias = static_cast<const T*>(p.bias2);
+      cu.bias_vec_ok = cu.bias != nullptr && (reinterpret_cast<uintptr_t>(cu.bias) & 15u) == 0;
+      c.bias = nullptr;
+      c.act = kActNone;
+      c.alpha = 1.0f;
+    }
     uint32_t it = 0;
     int local = 0;
     for (int i = 0;; ++i, ++local) {
@@ -605,14 +716,20 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
       const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
       int mb, nb;
       umma_tile_coords(p, w.tile, mb, nb);
-      const uint4 bias_reg = epi_load_bias(c, nb * BN, BN, lane);
+      const int n0o = nb * (kGated ? BN / 2 : BN);
+      const uint4 bias_reg = epi_load_bias(kGated ? cg : c, n0o, kGated ? BN / 2 : BN, lane);
+      const uint4 bias_up = kGated ? epi_load_bias(cu, n0o, BN / 2, lane) : make_uint4(0u, 0u, 0u, 0u);
       if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
       tc_fence_after();
       const uint32_t tempty = bar(S::BAR_TEMPTY + b);
       const uint32_t acc = tmem_base + static_cast<uint32_t>(b * BN);
       auto release = [tempty] { mbar_arrive(tempty); };
       bool done;
-      if (w.split < 0) {
+      if constexpr (kGated) {
+        done = epilogue_tile_gated<BN, T>(c, acc, q, lane, mb * S::BM, n0o, p.act, cg.bias != nullptr,
+                                          cu.bias != nullptr, bias_reg, bias_up, it, abort_flag,
+                                          release);
+      } else if (w.split < 0) {
         done = epilogue_tile<BN, T>(c, acc, q, lane, mb * S::BM, nb * BN, bias_reg, it, abort_flag,
                                     release);
       } else {
@@ -674,10 +791,11 @@ struct Umma2Shape {
   static_assert(BN == 128 || BN == 256, "pair tile N");
 };
 
-template <int BN, typename T>
+template <int BN, typename T, bool kGated = false>
 __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
     umma2_fused_linear_kernel(const __grid_constant__ CUtensorMap tmA,
                               const __grid_constant__ CUtensorMap tmB,
+                              const __grid_constant__ CUtensorMap tmB2,
                               const __grid_constant__ CUtensorMap tmY,
                               const __grid_constant__ CUtensorMap tmR, const UmmaParams p) {
   using S = Umma2Shape<BN>;
@@ -717,6 +835,7 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tmA);
     tma_prefetch_desc(&tmB);
+    if (kGated) tma_prefetch_desc(&tmB2);
     tma_prefetch_desc(&tmY);
     if (p.has_residual) tma_prefetch_desc(&tmR);
   }
@@ -745,7 +864,9 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
         int mb, nb;
         umma_tile_coords(p, w.tile, mb, nb);
         const int m0 = mb * 2 * S::BM + static_cast<int>(rank) * S::BM;
-        const int n0 = nb * BN + static_cast<int>(rank) * S::BN_CTA;
+        // Gated: the leader stages Wg's and the peer Wu's BN/2 columns.
+        const int n0 = kGated ? nb * S::BN_CTA : nb * BN + static_cast<int>(rank) * S::BN_CTA;
+        const CUtensorMap* const mapB = (kGated && rank != 0) ? &tmB2 : &tmB;
         for (int kb = w.kb0; kb < w.kb1; ++kb) {
           if (!mbar_wait(bar(S::BAR_EMPTY + s), ph ^ 1u, abort_flag)) {
             ok = false;
@@ -757,7 +878,7 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
           tma_load_2d_pair(&tmA, sA + s * S::A_BYTES, fb, kb * S::BK, m0, pol);
 #pragma unroll
           for (int j = 0; j < S::BN_CTA / 64; ++j)
-            tma_load_2d_pair(&tmB, sB + s * S::B_BYTES + j * S::B_BOX_BYTES, fb, n0 + 64 * j,
+            tma_load_2d_pair(mapB, sB + s * S::B_BYTES + j * S::B_BOX_BYTES, fb, n0 + 64 * j,
                              kb * S::BK, pol);
           ++issued;
           if (++s == S::STAGES) {
@@ -836,6 +957,16 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
     c.ebuf_ptr0 = base_ptr + S::OFF_EPI + e * 2 * kEpiBufBytes;
     c.rbar0 = bar(S::BAR_RES + e * 2);
     c.pol_stream = make_l2_policy_evict_first();
+    // Gated: biases are added before the activation in epilogue_tile_gated;
+    // cg / cu only load them.
+    EpilogueCtx<T> cg = c, cu = c;
+    if (kGated) {
+      cu.bias = static_cast<const T*>(p.bias2);
+      cu.bias_vec_ok = cu.bias != nullptr && (reinterpret_cast<uintptr_t>(cu.bias) & 15u) == 0;
+      c.bias = nullptr;
+      c.act = kActNone;
+      c.alpha = 1.0f;
+    }
     uint32_t it = 0;
     int local = 0;
     for (int i = 0;; ++i, ++local) {
@@ -845,7 +976,9 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
       const uint32_t use_ph = (static_cast<uint32_t>(local) >> 1) & 1u;
       int mb, nb;
       umma_tile_coords(p, w.tile, mb, nb);
-      const uint4 bias_reg = epi_load_bias(c, nb * BN, BN, lane);
+      const int n0o = nb * (kGated ? BN / 2 : BN);
+      const uint4 bias_reg = epi_load_bias(kGated ? cg : c, n0o, kGated ? BN / 2 : BN, lane);
+      const uint4 bias_up = kGated ? epi_load_bias(cu, n0o, BN / 2, lane) : make_uint4(0u, 0u, 0u, 0u);
       if (!mbar_wait(bar(S::BAR_TFULL + b), use_ph, abort_flag)) break;
       tc_fence_after();
       const uint32_t tempty_leader = mapa_shared(bar(S::BAR_TEMPTY + b), 0);
@@ -853,7 +986,11 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
       const int row0 = mb * 2 * S::BM + static_cast<int>(rank) * S::BM;
       auto release = [tempty_leader] { mbar_arrive_cluster(tempty_leader); };
       bool done;
-      if (w.split < 0) {
+      if constexpr (kGated) {
+        done = epilogue_tile_gated<BN, T>(c, acc, q, lane, row0, n0o, p.act, cg.bias != nullptr,
+                                          cu.bias != nullptr, bias_reg, bias_up, it, abort_flag,
+                                          release);
+      } else if (w.split < 0) {
         done = epilogue_tile<BN, T>(c, acc, q, lane, row0, nb * BN, bias_reg, it, abort_flag,
                                     release);
       } else {

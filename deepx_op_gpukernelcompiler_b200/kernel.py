@@ -13,7 +13,12 @@ multi-backend dispatch and no CPU path.  Besides the compilable patterns it
 runs the two single-GEMM patterns the reference lists as needs_template
 (fusion.py:24-25): ``attention_output`` (template ``gemm``: a @ b) and
 ``attention_score`` (template ``gemm_elem``: (a @ b) * scale, with
-scale = 1/sqrt(K)), through compiled plans (plan.py).  Extra keyword arguments over the
+scale = 1/sqrt(K)), through compiled plans (plan.py), and two of the
+``multi_kernel`` FFN chains as chains of fused launches: ``ffn_two_layer``
+(relu(a @ W1 + b1) @ W2 + b2, fusion.py:42-43) and ``ffn_gated``
+((silu(a @ Wg + bg) * (a @ Wu + bu)) @ Wo + bo, fusion.py:44-46, the gate and
+up GEMMs in one dual-GEMM launch).  Their weights are scaled by
+1/sqrt(fan-in) so the chain's output stays O(1).  Extra keyword arguments over the
 reference: ``dtype`` (default fp16 as in the reference), ``seed`` (default
 unseeded, as in the reference), ``n_iter`` and ``warmup``.  ``block`` is
 accepted for signature compatibility; the engine chooses its own tiles.
@@ -25,7 +30,7 @@ import torch
 from .fusion import ACTIVATION_PT, classify
 from .kernel_b200 import make_linear_kernel
 from .kvfunc import read_func
-from .mlp import mlp_residual
+from .mlp import gated_ffn, mlp_residual, two_layer_ffn
 from .plan import CompileRequest, Plan
 
 DEFAULT_SHAPE = {"M": 512, "N": 512, "K": 256}
@@ -37,6 +42,9 @@ ENGINES = {
 
 # needs_template rows (fusion.py:24-25) whose template the engine implements.
 ENGINE_TEMPLATES = {"gemm", "gemm_elem"}
+
+# multi_kernel rows (fusion.py:42-46) the engine runs as chains of fused launches.
+ENGINE_CHAINS = {"ffn_two_layer", "ffn_gated"}
 
 
 class CompileResult:
@@ -84,7 +92,7 @@ def compile_and_test(kv, func_path: str, fusion: str = "b200", shape: dict | Non
     if status == "not_matched":
         opcodes = " → ".join(o["op"] for o in tensor_ops)
         return CompileResult(False, 0, 0, 0, f"no fusion pattern for: {opcodes}")
-    if status != "compilable" and template not in ENGINE_TEMPLATES:
+    if status != "compilable" and template not in ENGINE_TEMPLATES and pattern not in ENGINE_CHAINS:
         return CompileResult(False, 0, 0, 0, f"{status}: {pattern}")
     if not torch.cuda.is_available():
         raise RuntimeError("compile_and_test needs a CUDA device (the B200 engine has no CPU path)")
@@ -117,6 +125,30 @@ def compile_and_test(kv, func_path: str, fusion: str = "b200", shape: dict | Non
         def ref_fn():
             out = a @ b
             return out * scale if template == "gemm_elem" else out
+    elif pattern == "ffn_two_layer":
+        # X[M,K] -> H[M,N] -> Y[M,K]
+        a, w1, b1, w2, b2 = randn(M, K), randn(K, N), randn(N), randn(N, K), randn(K)
+        w1 /= K ** 0.5
+        w2 /= N ** 0.5
+
+        def run():
+            return two_layer_ffn(a, w1, b1, w2, b2, "relu")
+
+        def ref_fn():
+            return ACTIVATION_PT["relu"](a @ w1 + b1) @ w2 + b2
+    elif pattern == "ffn_gated":
+        # X[M,K] -> H[M,N] (gate * up) -> Y[M,K]
+        a, wg, bg, wu, bu = randn(M, K), randn(K, N), randn(N), randn(K, N), randn(N)
+        wo, bo = randn(N, K), randn(K)
+        wg /= K ** 0.5
+        wu /= K ** 0.5
+        wo /= N ** 0.5
+
+        def run():
+            return gated_ffn(a, wg, bg, wu, bu, wo, bo, "silu")
+
+        def ref_fn():
+            return (ACTIVATION_PT["silu"](a @ wg + bg) * (a @ wu + bu)) @ wo + bo
     elif template == "mlp_chain":
         # X[M,K] -> H[M,N] -> Y[M,K]; residual is X itself.
         a, w1, b1, w2, b2 = randn(M, K), randn(K, N), randn(N), randn(N, K), randn(K)

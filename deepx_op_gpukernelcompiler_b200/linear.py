@@ -145,6 +145,60 @@ def fused_linear(X: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None = N
     return out
 
 
+def fused_gated_linear(X: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor,
+                       bias_g: torch.Tensor | None = None, bias_u: torch.Tensor | None = None,
+                       activation="silu", out: torch.Tensor | None = None,
+                       kernel: str = "auto") -> torch.Tensor:
+    """Y = act(X @ Wg + bias_g) * (X @ Wu + bias_u) in one launch
+    (dx_fused_gated_linear): the first two GEMMs of the gated FFN chain
+    ``ffn_gated`` (fusion.py:44-46), X read once for both weights."""
+    act = activation_code(activation)
+    if kernel not in nat.KERNEL_NAMES:
+        raise ValueError(f"unknown kernel {kernel!r}; expected one of {list(nat.KERNEL_NAMES)}")
+    if X.device.type != "cuda":
+        raise ValueError("fused_gated_linear runs on CUDA tensors only (the engine has no CPU path)")
+    if X.dtype not in DTYPE_CODES:
+        raise ValueError(f"unsupported dtype {X.dtype}; expected float32, float16 or bfloat16")
+    _check_matrix("X", X, None, None)
+    M, K = X.shape
+    _check_matrix("Wg", Wg, K, None)
+    N = Wg.shape[1]
+    _check_matrix("Wu", Wu, K, N)
+    tensors = {"Wg": Wg, "Wu": Wu}
+    for name, b in (("bias_g", bias_g), ("bias_u", bias_u)):
+        if b is not None:
+            if b.dim() != 1 or b.shape[0] != N or not b.is_contiguous():
+                raise ValueError(f"{name} must be a contiguous tensor of shape ({N},)")
+            tensors[name] = b
+    if out is None:
+        out = torch.empty((M, N), dtype=X.dtype, device=X.device)
+    else:
+        _check_matrix("out", out, M, N)
+        tensors["out"] = out
+    for name, t in tensors.items():
+        if t.dtype != X.dtype:
+            raise ValueError(f"{name} dtype {t.dtype} differs from X dtype {X.dtype}")
+        if t.device != X.device:
+            raise ValueError(f"{name} is on {t.device}, X is on {X.device}")
+
+    lib = nat.load()
+    dtype = DTYPE_CODES[X.dtype]
+    kcode = nat.KERNEL_NAMES[kernel]
+    with torch.cuda.device(X.device):
+        stream = torch.cuda.current_stream(X.device).cuda_stream
+        ws = _workspace(X.device, stream,
+                        lib.dx_fused_gated_linear_workspace_size(M, N, K, dtype, kcode))
+        rc = lib.dx_fused_gated_linear(
+            X.data_ptr(), Wg.data_ptr(), Wu.data_ptr(),
+            bias_g.data_ptr() if bias_g is not None else None,
+            bias_u.data_ptr() if bias_u is not None else None,
+            out.data_ptr(), M, N, K, _ld(X), _ld(Wg), _ld(Wu), _ld(out), dtype, act, kcode,
+            ws.data_ptr() if ws is not None else None,
+            ws.numel() if ws is not None else 0, stream)
+    nat.check("dx_fused_gated_linear", rc)
+    return out
+
+
 def selected_kernel(M: int, N: int, K: int, dtype: torch.dtype) -> str:
     """Name of the kernel variant the engine picks for this problem."""
     code = nat.load().dx_select_kernel(M, N, K, DTYPE_CODES[dtype])

@@ -148,6 +148,30 @@ size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K,
 int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype);
 
 /*
+ * Gated dual-GEMM: Y = act(X @ Wg + bias_g) * (X @ Wu + bias_u), the first
+ * two GEMMs of the gated FFN chain (`ffn_gated`, fusion.py:44-46; fixtures
+ * test/fusion_cases/07_ffn_gated.kv and 08_ffn_swiglu.kv, with act = SiLU).
+ * No reference kernel: the reference classifies that chain multi_kernel and
+ * never runs it.  One launch reads X once for both weights: the tcgen05
+ * kernels put Wg's and Wu's columns of a tile into one accumulator and
+ * combine them in the epilogue.  Wg and Wu are [K, N] with pitches ldwg and
+ * ldwu; bias_g, bias_u [N] may be NULL.  No residual.  Variants as for
+ * dx_fused_linear_ex (DX_KERNEL_AUTO normally); the workspace rules are
+ * those of dx_fused_linear, with dx_fused_gated_linear_workspace_size.
+ */
+int dx_fused_gated_linear(const void* X, const void* Wg, const void* Wu,
+                          const void* bias_g, const void* bias_u, void* Y,
+                          int64_t M, int64_t N, int64_t K,
+                          int64_t ldx, int64_t ldwg, int64_t ldwu, int64_t ldy,
+                          int dtype, int act, int kernel,
+                          void* workspace, size_t workspace_bytes,
+                          void* stream);
+
+/* Workspace bytes that dx_fused_gated_linear needs (0: none). */
+size_t dx_fused_gated_linear_workspace_size(int64_t M, int64_t N, int64_t K,
+                                            int dtype, int kernel);
+
+/*
  * Plans — the compile-then-call runtime of the reference design docs: the
  * compile step fixes shape, dtype and op sequence
  * (doc/kvlang-to-tilelang-interface.md:60-77,100-129) and the runtime calls
@@ -183,8 +207,10 @@ const char* dx_last_launch_plan(void);
  * CTA: 16 uint64 slots per CTA in blockIdx order.  GEMM kernels: slot 0 after
  * set-up, slot 1+i when work item i's epilogue finished (i < 14), slot 15 at
  * exit.  Decode kernel: slot 0 after set-up, 1 / 2 first / last TMA issue,
- * 3 last MMA issue, 4+i work item i finished (i < 9), 13 the SM id (not a
- * time), 14 epilogue done, 15 exit.
+ * 3 last MMA issue; for the CTA's last work item 4 accumulator ready, 5 read,
+ * 6 arrival counted, 7 partial published / others' partials found written,
+ * 8 fix-up sums done, 9 item finished; 10+i work item i finished (i < 2),
+ * 12 kernel entry, 13 the SM id (not a time), 14 epilogue done, 15 exit.
  * The buffer must hold 16 * 8 bytes per CTA of the grid (148 SMs: 18,944 B);
  * launches whose grid does not fit are not traced.  NULL turns tracing off.
  * Process-wide setting; the caller owns the buffer. */

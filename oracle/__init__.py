@@ -9,6 +9,10 @@ from .fused_linear import (  # noqa: F401
     activation_f64,
     fused_linear_f32,
     fused_linear_f64,
+    gated_ffn_f32,
+    gated_ffn_f64,
+    gated_linear_f32,
+    gated_linear_f64,
     mlp_residual_f32,
     mlp_residual_f64,
 )

@@ -11,7 +11,11 @@ CPU restatements of the reference's fused-linear oracle
 * ``fused_linear_f32`` — numpy in fp32 (BLAS sgemm, then the epilogue),
   the same arithmetic class as the reference's torch-CPU fp32 oracle; used
   at sizes where the C loop would be slow and as the timed CPU baseline;
-* ``mlp_residual_*`` — the two-GEMM chain H = act(X W1 + b1), Y = H W2 + b2 + X.
+* ``mlp_residual_*`` — the two-GEMM chain H = act(X W1 + b1), Y = H W2 + b2 + X;
+* ``gated_linear_f64`` / ``gated_ffn_f64`` — the gated FFN chain of
+  fusion.py:44-46 (test/fusion_cases/07_ffn_gated.kv: tensor.silu of the gate
+  GEMM, tensor.mul with the up GEMM, then the output GEMM), composed from the
+  same restated matmul/add/activation steps.
 
 Activations: relu; gelu = tanh approximation (fusion.py:89, the reference
 oracle); gelu_erf = 0.5 x (1 + erf(x / sqrt 2)) (kernel_triton.py:61);
@@ -137,3 +141,21 @@ def mlp_residual_f64(X, W1, b1, W2, b2, act="gelu") -> np.ndarray:
 def mlp_residual_f32(X, W1, b1, W2, b2, act="gelu") -> np.ndarray:
     H = fused_linear_f32(X, W1, b1, act)
     return fused_linear_f32(H, W2, b2, None, residual=X)
+
+
+def gated_linear_f64(X, Wg, bg, Wu, bu, act="silu") -> np.ndarray:
+    """act(X Wg + bg) * (X Wu + bu) in double precision (07_ffn_gated.kv:2-7)."""
+    return fused_linear_f64(X, Wg, bg, act) * fused_linear_f64(X, Wu, bu, None)
+
+
+def gated_ffn_f64(X, Wg, bg, Wu, bu, Wo, bo, act="silu") -> np.ndarray:
+    """(act(X Wg + bg) * (X Wu + bu)) Wo + bo in double (07_ffn_gated.kv:2-9)."""
+    return fused_linear_f64(gated_linear_f64(X, Wg, bg, Wu, bu, act), Wo, bo, None)
+
+
+def gated_linear_f32(X, Wg, bg, Wu, bu, act="silu") -> np.ndarray:
+    return fused_linear_f32(X, Wg, bg, act) * fused_linear_f32(X, Wu, bu, None)
+
+
+def gated_ffn_f32(X, Wg, bg, Wu, bu, Wo, bo, act="silu") -> np.ndarray:
+    return fused_linear_f32(gated_linear_f32(X, Wg, bg, Wu, bu, act), Wo, bo, None)

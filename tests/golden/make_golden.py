@@ -22,6 +22,10 @@ What it writes, and from which reference code:
   own ACTIVATION_PT.  The erf-GELU case uses the reference kernels' formula
   0.5*x*(erf(x*0.7071067811865475)+1) (kernel_triton.py:61).  Residual
   cases add R after the activation; the MLP case chains two such calls.
+  Gated cases follow the ``ffn_gated`` chain op by op
+  (test/fusion_cases/07_ffn_gated.kv): the gate through the same expression
+  with ``ACTIVATION_PT['silu']``, the up projection without activation, their
+  product (tensor.mul), and for the full chain one more linear.
 
 Inputs: torch.Generator(seed), X ~ N(0,1), W ~ N(0, 1/K), bias ~ U(-0.1, 0.1),
 generated in fp32 and cast to the case dtype.  Inputs are stored in their
@@ -157,6 +161,27 @@ def make_numeric(fusion) -> tuple[dict, dict]:
                       "dtype": dtype, "act": act, "residual": residual,
                       "mlp": mlp_hidden is not None})
 
+    def add_gated(name, seed, M, K, N, dtype, act="silu", ffn=False):
+        g = torch.Generator().manual_seed(seed)
+        dt = DTYPES[dtype]
+        X = torch.randn(M, K, generator=g).to(dt)
+        Wg = (torch.randn(K, N, generator=g) / math.sqrt(K)).to(dt)
+        bg = (torch.rand(N, generator=g) * 0.2 - 0.1).to(dt)
+        Wu = (torch.randn(K, N, generator=g) / math.sqrt(K)).to(dt)
+        bu = (torch.rand(N, generator=g) * 0.2 - 0.1).to(dt)
+        H = _reference_expr(fusion, X, Wg, bg, act) * _reference_expr(fusion, X, Wu, bu, None)
+        tensors = {"X": X, "Wg": Wg, "bg": bg, "Wu": Wu, "bu": bu}
+        if ffn:
+            Wo = (torch.randn(N, K, generator=g) / math.sqrt(N)).to(dt)
+            bo = (torch.rand(K, generator=g) * 0.2 - 0.1).to(dt)
+            tensors.update({"Wo": Wo, "bo": bo})
+            H = _reference_expr(fusion, H, Wo, bo, None)
+        tensors["Y"] = H
+        for k, v in tensors.items():
+            arrays[f"{name}/{k}"] = _store(v) if k != "Y" else v.float().numpy()
+        cases.append({"name": name, "seed": seed, "M": M, "K": K, "N": N, "dtype": dtype,
+                      "act": act, "residual": False, "mlp": False, "gated": True, "ffn": ffn})
+
     # The reference's CPU-runnable configuration: ReLU(X[256,512] W[512,512] + b), fp32, seed 0.
     add("linear_relu_256x512x512_f32", 0, 256, 512, 512, "f32", "relu")
     # Every compilable activation (fusion.py:16-20) in each dtype, ragged sizes.
@@ -177,6 +202,12 @@ def make_numeric(fusion) -> tuple[dict, dict]:
     add("residual_8x256x192_f16", 207, 8, 256, 192, "f16", None, residual=True)
     # mlp_residual: Y = GELU(X W1 + b1) W2 + b2 + X.
     add("mlp_64x128x256_bf16", 208, 64, 128, None, "bf16", "gelu", mlp_hidden=256)
+    # Gated dual GEMM act(X Wg + bg) * (X Wu + bu) and the full ffn_gated chain.
+    add_gated("gated_silu_37x80x72_f32", 209, 37, 80, 72, "f32")
+    add_gated("gated_silu_16x192x320_f16", 210, 16, 192, 320, "f16")
+    add_gated("gated_silu_130x256x200_bf16", 211, 130, 256, 200, "bf16")
+    add_gated("gated_silu_300x128x264_bf16", 212, 300, 128, 264, "bf16")
+    add_gated("ffn_gated_64x128x256_bf16", 213, 64, 128, 256, "bf16", ffn=True)
     return arrays, {"cases": cases}
 
 

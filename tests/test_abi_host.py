@@ -75,6 +75,35 @@ def test_host_validation(lib, kw, code, needle):
     assert needle in nat.last_error()
 
 
+def _call_gated(lib, **kw):
+    a = dict(X=FAKE, Wg=FAKE, Wu=FAKE, bg=None, bu=None, Y=FAKE, M=4, N=4, K=4, ldx=4, ldwg=4,
+             ldwu=4, ldy=4, dtype=nat.DX_DTYPE_BF16, act=nat.DX_ACT_SILU, kernel=0)
+    a.update(kw)
+    return lib.dx_fused_gated_linear(a["X"], a["Wg"], a["Wu"], a["bg"], a["bu"], a["Y"], a["M"],
+                                     a["N"], a["K"], a["ldx"], a["ldwg"], a["ldwu"], a["ldy"],
+                                     a["dtype"], a["act"], a["kernel"], None, 0, None)
+
+
+@pytest.mark.parametrize("kw,code,needle", [
+    (dict(Wu=None), nat.DX_ERR_INVALID_ARGUMENT, "Wu is NULL"),
+    (dict(ldwu=3), nat.DX_ERR_INVALID_ARGUMENT, "ldwu"),
+    (dict(ldwg=3), nat.DX_ERR_INVALID_ARGUMENT, "ldw"),
+    (dict(act=11), nat.DX_ERR_INVALID_ARGUMENT, "activation"),
+    (dict(kernel=9), nat.DX_ERR_INVALID_ARGUMENT, "kernel"),
+])
+def test_gated_host_validation(lib, kw, code, needle):
+    assert _call_gated(lib, **kw) == code
+    assert needle in nat.last_error()
+
+
+def test_gated_workspace_sizes(lib):
+    # No GPU here: the device-dependent decode size reads as 0; the tensor-core
+    # and SIMT forms never need one.
+    assert lib.dx_fused_gated_linear_workspace_size(4096, 4096, 4096, nat.DX_DTYPE_BF16,
+                                                    nat.DX_KERNEL_UMMA) == 0
+    assert lib.dx_fused_gated_linear_workspace_size(16, 512, 512, nat.DX_DTYPE_F32, 0) == 0
+
+
 def test_empty_problem_is_a_no_op(lib):
     assert _call(lib, M=0) == nat.DX_OK
     assert _call(lib, N=0) == nat.DX_OK

@@ -86,7 +86,8 @@ def kv():
 
 
 @pytest.mark.parametrize("name", ["dense", "dense_relu", "dense_gelu", "dense_silu", "dense_swish",
-                                  "dense_residual", "mlp_block", "scaled_scores"])
+                                  "dense_residual", "mlp_block", "scaled_scores",
+                                  "two_layer_relu", "gated_silu"])
 def test_compile_and_test_runs_engine(kv, name):
     r = compile_and_test(kv, f"/func/fusion_cases/{name}", seed=0, n_iter=5, warmup=2)
     assert r.error is None and r.success, r

@@ -22,11 +22,18 @@ def _run(case, fn):
     t = load(case)
     if case["mlp"]:
         return fn["mlp"](t["X"], t["W1"], t["b1"], t["W2"], t["b2"], case["act"]), t["Y"]
+    if case.get("gated"):
+        if case["ffn"]:
+            return fn["ffn_gated"](t["X"], t["Wg"], t["bg"], t["Wu"], t["bu"], t["Wo"], t["bo"],
+                                   case["act"]), t["Y"]
+        return fn["gated"](t["X"], t["Wg"], t["bg"], t["Wu"], t["bu"], case["act"]), t["Y"]
     return fn["linear"](t["X"], t["W"], t["bias"], case["act"], residual=t.get("R")), t["Y"]
 
 
-F64 = {"linear": oracle.fused_linear_f64, "mlp": oracle.mlp_residual_f64}
-F32 = {"linear": oracle.fused_linear_f32, "mlp": oracle.mlp_residual_f32}
+F64 = {"linear": oracle.fused_linear_f64, "mlp": oracle.mlp_residual_f64,
+       "gated": oracle.gated_linear_f64, "ffn_gated": oracle.gated_ffn_f64}
+F32 = {"linear": oracle.fused_linear_f32, "mlp": oracle.mlp_residual_f32,
+       "gated": oracle.gated_linear_f32, "ffn_gated": oracle.gated_ffn_f32}
 
 
 @pytest.mark.parametrize("case", cases(), ids=lambda c: c["name"])
@@ -46,6 +53,7 @@ def test_golden_covers_every_compilable_activation():
     assert {None, "relu", "gelu", "silu", "swish", "gelu_erf"} <= acts
     assert {c["dtype"] for c in cases()} == {"f32", "f16", "bf16"}
     assert any(c["residual"] for c in cases()) and any(c["mlp"] for c in cases())
+    assert any(c.get("gated") and c["ffn"] for c in cases())
 
 
 def test_reference_cpu_config_is_pinned():
@@ -66,6 +74,15 @@ def test_planted_activation_mistake_is_caught():
     wrong = oracle.fused_linear_f64(t["X"], t["W"], t["bias"], "gelu_erf")
     err = np.abs(wrong - t["Y"].numpy()).max()
     assert err > 10 * ORACLE_ATOL
+
+
+def test_planted_gate_mistake_is_caught():
+    """Apply the activation to the up projection instead of the gate."""
+    case = next(c for c in cases() if c.get("gated") and c["dtype"] == "f32")
+    t = load(case)
+    wrong = (oracle.fused_linear_f64(t["X"], t["Wg"], t["bg"], None)
+             * oracle.fused_linear_f64(t["X"], t["Wu"], t["bu"], case["act"]))
+    assert np.abs(wrong - t["Y"].numpy()).max() > 10 * ORACLE_ATOL
 
 
 def test_planted_bias_mistake_is_caught():

@@ -18,10 +18,21 @@ def kv():
 
 
 def test_compile_and_test_reports_non_compilable(kv):
-    r = compile_and_test(kv, "/func/fusion_cases/two_layer_relu")
-    assert not r.success and r.error == "multi_kernel: ffn_two_layer"
+    r = compile_and_test(kv, "/func/fusion_cases/sequential_gelu")
+    assert not r.success and r.error == "multi_kernel: ffn_sequential"
     r = compile_and_test(kv, "/func/fusion_cases/masked_softmax")
     assert not r.success and r.error == "needs_template: attention_softmax"
+
+
+def test_engine_chains_need_a_gpu(kv):
+    """ffn_two_layer / ffn_gated run as fused chains: on a CPU-only host the
+    call fails loudly instead of falling back."""
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    for name in ("two_layer_relu", "gated_silu"):
+        with pytest.raises(RuntimeError, match="needs a CUDA device"):
+            compile_and_test(kv, f"/func/fusion_cases/{name}")
 
 
 def test_compile_and_test_reports_unmatched():
