@@ -507,6 +507,35 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
                    "frac_of_peak": round(tf / world / tflops_peak, 4), "kernel": "umma"}
     del X, Wt, b, Y
 
+    # Gated FFN's gate/up projections in one dual-GEMM launch:
+    # H = silu(X Wg + bg) * (X Wu + bu), X[8192,4096], Wg/Wu[4096,14336] (per
+    # rank an N-slice of both, no collective).
+    M_g, K_g, N_g = 8192, 4096, 14336
+    n0, n1 = shard_bounds(N_g, world, rank, 64)
+    n_loc = n1 - n0
+    X = torch.randn(M_g, K_g, generator=g, device=dev).to(torch.bfloat16)
+    Wg = (torch.randn(K_g, n_loc, generator=g, device=dev) / math.sqrt(K_g)).to(torch.bfloat16)
+    Wu = (torch.randn(K_g, n_loc, generator=g, device=dev) / math.sqrt(K_g)).to(torch.bfloat16)
+    bg = (torch.rand(n_loc, generator=g, device=dev) * 0.2 - 0.1).to(torch.bfloat16)
+    bu = (torch.rand(n_loc, generator=g, device=dev) * 0.2 - 0.1).to(torch.bfloat16)
+    Y = torch.empty(M_g, n_loc, dtype=torch.bfloat16, device=dev)
+    from deepx_op_gpukernelcompiler_b200 import fused_gated_linear
+
+    def gated():
+        fused_gated_linear(X, Wg, Wu, bg, bu, "silu", out=Y)
+
+    for _ in range(3):
+        gated()
+    torch.cuda.synchronize()
+    _barrier(world)
+    t = _time_launches(gated, steps, flush, stream)
+    ms = _max_over_ranks(sum(t), world, dev) / steps
+    tf = 2 * 2 * M_g * N_g * K_g / (ms * 1e-3) / 1e12
+    out[f"ffn_gated_gate_up_{M_g}x{K_g}x{N_g}_bf16"] = {
+        "value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+        "frac_of_peak": round(tf / world / tflops_peak, 4), "kernel": "umma gated (dual GEMM)"}
+    del X, Wg, Wu, bg, bu, Y
+
     # MLP chain: Y = GELU(X W1 + b1) W2 + b2 + X; column -> row parallel with
     # one all-reduce of Y (NCCL) when world > 1.
     w = WORKLOADS["mlp_residual_16384x4096x16384_bf16"]
