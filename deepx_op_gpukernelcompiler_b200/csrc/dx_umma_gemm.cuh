@@ -15,14 +15,15 @@
 //     shared memory per MMA compared with a single-CTA 128 x BN tile.
 //   umma_fused_linear_kernel   (M < 256) — single CTA, 128 x BN tiles.
 //
-// Roles inside a CTA (192 threads):
+// Roles inside a CTA (320 threads):
 //   warp 0   TMA producer: X tiles [128 x 64] (K-major) and W tiles
 //            [64 x 64] boxes (N-major, W exactly as it lies in memory) into
 //            a STAGES-deep ring of 128-byte-swizzled buffers;
 //   warp 1   TMEM allocator; its lane 0 (in the leader CTA for pairs) issues
 //            the MMAs into one of two TMEM accumulators (double buffer);
-//   warps 2-5 epilogue: each warp owns the 32 TMEM lanes (= tile rows) it may
-//            address, pulls 32 fp32 columns at a time with tcgen05.ld, adds
+//   warps 2-9 epilogue: each warp owns the 32 TMEM lanes (= tile rows) it may
+//            address (two warps per lane quarter, each taking half of the
+//            columns), pulls 32 fp32 columns at a time with tcgen05.ld, adds
 //            bias, applies the activation, adds the residual (TMA-loaded into
 //            the staging buffer), converts, and TMA-stores.  The output tile
 //            crosses HBM exactly once; the next tile's main loop runs in the
@@ -63,7 +64,7 @@ struct UmmaParams {
   int dp_tiles;
   int splits;
   float* partials;  // [tail tile][split][CTA of the tile][128][BN]
-  int* tickets;     // [tail tile][CTA of the tile][4 warps][2]; zero between calls
+  int* tickets;     // [tail tile][CTA of the tile][kEpiWarps][2]; zero between calls
   // Optional timeline (dx_set_trace_buffer): per CTA kTraceSlots device-time
   // stamps: [0] after set-up, [1 + i] when the epilogue finished work item i
   // (first kTraceSlots - 2 items), [kTraceSlots - 1] at exit.
@@ -113,8 +114,16 @@ __device__ __forceinline__ void umma_tile_coords(const UmmaParams& p, int t, int
   nb = r / gm;
 }
 
-constexpr int kEpiWarps = 4;
+// Epilogue warps: two per TMEM lane quarter, each finishing half of a
+// tile's columns, so a tile's epilogue (which overlaps the next tile's main
+// loop but is exposed after the last one) takes half as long.
+constexpr int kEpiWarps = 8;
+constexpr int kEpiHalves = kEpiWarps / 4;
 constexpr int kEpiBufBytes = 32 * 32 * 2;  // [32 rows x 32 cols] of 16-bit
+// Staging buffers per epilogue warp: a chunk's buffer is reused only after
+// the TMA store issued kEpiBufs chunks earlier has read it, so up to
+// kEpiBufs - 1 stores stay in flight behind the producer's loads.
+constexpr int kEpiBufs = 2;
 
 // What one epilogue warp needs to finish accumulators.
 template <typename T>
@@ -125,9 +134,9 @@ struct EpilogueCtx {
   bool bias_vec_ok;
   int M, N, act, has_residual;
   float alpha;
-  uint32_t ebuf0;      // this warp's two staging buffers (shared address)
+  uint32_t ebuf0;      // this warp's kEpiBufs staging buffers (shared address)
   uint8_t* ebuf_ptr0;  // same, generic pointer
-  uint32_t rbar0;      // this warp's two residual-load barriers (8 B apart)
+  uint32_t rbar0;      // this warp's kEpiBufs residual-load barriers (8 B apart)
   uint64_t pol_stream; // evict-first policy for Y stores and R loads
 };
 
@@ -136,8 +145,8 @@ struct EpilogueCtx {
 template <typename T>
 __device__ __forceinline__ void epi_chunk_begin(const EpilogueCtx<T>& c, int n_c, int row_base,
                                                 int lane, uint32_t it) {
-  const int buf = it & 1;
-  if (lane == 0) bulk_wait_group_read<1>();
+  const int buf = it % kEpiBufs;
+  if (lane == 0) bulk_wait_group_read<kEpiBufs - 1>();
   __syncwarp();
   if (c.has_residual && lane == 0) {
     const uint32_t rbar = c.rbar0 + 8u * buf;
@@ -174,7 +183,7 @@ __device__ __forceinline__ bool epi_chunk_end(const EpilogueCtx<T>& c, float (&v
                                               int row_base, int lane, uint32_t& it,
                                               volatile int* abort_flag, uint4 bias_reg, int ch) {
   using Tr = ElemTraits<T>;
-  const int buf = it & 1;
+  const int buf = it % kEpiBufs;
   const uint32_t ebuf = c.ebuf0 + buf * kEpiBufBytes;
   uint8_t* const ebp = c.ebuf_ptr0 + buf * kEpiBufBytes;
   const uint32_t row_off = static_cast<uint32_t>(lane) * 64u;
@@ -205,7 +214,7 @@ __device__ __forceinline__ bool epi_chunk_end(const EpilogueCtx<T>& c, float (&v
   }
   if (c.has_residual) {
     const uint32_t rbar = c.rbar0 + 8u * buf;
-    const uint32_t par = (it >> 1) & 1u;
+    const uint32_t par = (it / kEpiBufs) & 1u;
     if (!mbar_wait(rbar, par, abort_flag)) {
       mbar_wait_drain(rbar, par);  // the load still lands in this buffer
       return false;
@@ -242,25 +251,26 @@ __device__ __forceinline__ bool epi_chunk_end(const EpilogueCtx<T>& c, float (&v
   return true;
 }
 
-// Drains one 128 x BN accumulator: this warp handles TMEM lanes
-// [32q, 32q+32), i.e. global rows row0 + 32q + lane, columns n0 .. n0+BN.
-// `release()` is called (lane 0, after the last TMEM read) to hand the
-// accumulator back to the MMA issuer.  `it` counts staging-buffer uses.
-// Returns false if a bounded wait gave up.
+// Drains this warp's part of one 128 x BN accumulator: TMEM lanes
+// [32q, 32q+32), i.e. global rows row0 + 32q + lane, and the 32-column
+// chunks [ch0, ch1) of columns n0 .. n0+BN.  `release()` is called (lane 0,
+// after the warp's last TMEM read) to hand the accumulator back to the MMA
+// issuer.  `it` counts staging-buffer uses.  Returns false if a bounded wait
+// gave up.
 template <int BN, typename T, typename Release>
 __device__ __forceinline__ bool epilogue_tile(const EpilogueCtx<T>& c, uint32_t tmem_acc, int q,
-                                              int lane, int row0, int n0, uint4 bias_reg,
-                                              uint32_t& it, volatile int* abort_flag,
-                                              Release release) {
+                                              int lane, int row0, int n0, int ch0, int ch1,
+                                              uint4 bias_reg, uint32_t& it,
+                                              volatile int* abort_flag, Release release) {
   const int row_base = row0 + q * 32;
   const bool rows_live = row_base < c.M;
   const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(q * 32) << 16);
-  int n_chunks = 0;  // live chunks: a prefix of the tile's columns
+  int ce = ch0;  // live chunks are a prefix of the tile's columns
   if (rows_live) {
     const int cols = min(BN, c.N - n0);
-    n_chunks = cols > 0 ? (cols + 31) / 32 : 0;
+    ce = min(ch1, cols > 0 ? (cols + 31) / 32 : 0);
   }
-  if (n_chunks == 0) {
+  if (ce <= ch0) {
     tc_fence_before();
     __syncwarp();
     if (lane == 0) release();
@@ -268,16 +278,16 @@ __device__ __forceinline__ bool epilogue_tile(const EpilogueCtx<T>& c, uint32_t 
   }
   // The TMEM load of chunk ch + 1 is in flight while chunk ch is finished.
   uint32_t r[32];
-  tmem_ld_32x32b_x32(lane_addr, r);
+  tmem_ld_32x32b_x32(lane_addr + static_cast<uint32_t>(32 * ch0), r);
 #pragma unroll 1
-  for (int ch = 0; ch < n_chunks; ++ch) {
+  for (int ch = ch0; ch < ce; ++ch) {
     const int n_c = n0 + 32 * ch;
     epi_chunk_begin(c, n_c, row_base, lane, it);
     tmem_wait_ld();
     float v[32];
 #pragma unroll
     for (int j = 0; j < 32; ++j) v[j] = __uint_as_float(r[j]);
-    if (ch + 1 < n_chunks) {
+    if (ch + 1 < ce) {
       tmem_ld_32x32b_x32(lane_addr + static_cast<uint32_t>(32 * (ch + 1)), r);
     } else {
       // Accumulator fully read: hand it back to the MMA issuer.
@@ -286,7 +296,7 @@ __device__ __forceinline__ bool epilogue_tile(const EpilogueCtx<T>& c, uint32_t 
       if (lane == 0) release();
     }
     if (!epi_chunk_end(c, v, n_c, row_base, lane, it, abort_flag, bias_reg, ch)) {
-      if (ch + 1 < n_chunks) tmem_wait_ld();
+      if (ch + 1 < ce) tmem_wait_ld();
       return false;
     }
   }
@@ -297,23 +307,24 @@ __device__ __forceinline__ bool epilogue_tile(const EpilogueCtx<T>& c, uint32_t 
 // BN/2 up columns; output column n0 + j = act(gate_j + bg) * (up_j + bu).
 // `c` must have no bias, no activation, alpha 1 and no residual (they are
 // applied here); the biases arrive spread over the warp as in epi_load_bias.
+// The warp handles output chunks [ch0, ch1) (32 columns each).
 template <int BN, typename T, typename Release>
 __device__ __forceinline__ bool epilogue_tile_gated(const EpilogueCtx<T>& c, uint32_t tmem_acc,
-                                                    int q, int lane, int row0, int n0, int act,
-                                                    bool has_bg, bool has_bu, uint4 bg_reg,
-                                                    uint4 bu_reg, uint32_t& it,
+                                                    int q, int lane, int row0, int n0, int ch0,
+                                                    int ch1, int act, bool has_bg, bool has_bu,
+                                                    uint4 bg_reg, uint4 bu_reg, uint32_t& it,
                                                     volatile int* abort_flag, Release release) {
   using Tr = ElemTraits<T>;
   constexpr int BNO = BN / 2;
   const int row_base = row0 + q * 32;
   const bool rows_live = row_base < c.M;
   const uint32_t lane_addr = tmem_acc + (static_cast<uint32_t>(q * 32) << 16);
-  int n_chunks = 0;
+  int n_chunks = ch0;
   if (rows_live) {
     const int cols = min(BNO, c.N - n0);
-    n_chunks = cols > 0 ? (cols + 31) / 32 : 0;
+    n_chunks = min(ch1, cols > 0 ? (cols + 31) / 32 : 0);
   }
-  if (n_chunks == 0) {
+  if (n_chunks <= ch0) {
     tc_fence_before();
     __syncwarp();
     if (lane == 0) release();
@@ -321,10 +332,10 @@ __device__ __forceinline__ bool epilogue_tile_gated(const EpilogueCtx<T>& c, uin
   }
   // Both halves of chunk ch + 1 are loading while chunk ch is finished.
   uint32_t rg[32], ru[32];
-  tmem_ld_32x32b_x32(lane_addr, rg);
-  tmem_ld_32x32b_x32(lane_addr + static_cast<uint32_t>(BNO), ru);
+  tmem_ld_32x32b_x32(lane_addr + static_cast<uint32_t>(32 * ch0), rg);
+  tmem_ld_32x32b_x32(lane_addr + static_cast<uint32_t>(BNO + 32 * ch0), ru);
 #pragma unroll 1
-  for (int ch = 0; ch < n_chunks; ++ch) {
+  for (int ch = ch0; ch < n_chunks; ++ch) {
     const int n_c = n0 + 32 * ch;
     epi_chunk_begin(c, n_c, row_base, lane, it);
     tmem_wait_ld();
@@ -409,22 +420,25 @@ __device__ __forceinline__ bool wait_counter(const int* ctr, int target, volatil
 // covers 512 contiguous bytes.
 template <int BN, typename T, typename Release, typename PartBase>
 __device__ __forceinline__ bool epilogue_split(const EpilogueCtx<T>& c, uint32_t tmem_acc, int q,
-                                               int lane, int row0, int n0, uint4 bias_reg,
-                                               int split, int splits, int* ctr,
+                                               int lane, int row0, int n0, int ch0, int ch1,
+                                               uint4 bias_reg, int split, int splits, int* ctr,
                                                PartBase part_base, uint32_t& it,
                                                volatile int* abort_flag, Release release) {
   const size_t slab = static_cast<size_t>(q) * 32 * BN;  // this warp's 32 rows
   // float4 index of (column quad j4, this lane's row) within a slab
   auto quad = [lane](int j4) { return static_cast<size_t>(j4) * 32 + lane; };
   float4* const mine = reinterpret_cast<float4*>(part_base(split) + slab);
+  // This warp's chunks [ch0, ch1): written by the same warp of every piece,
+  // counted on this warp's own counter pair, then reduced chunk ch by
+  // piece ch % splits.
 #pragma unroll 1
-  for (int ch = 0; ch < BN / 32; ++ch) {
+  for (int ch = ch0; ch < ch1; ++ch) {
     uint32_t r[32];
     tmem_ld_32x32b_x32(tmem_acc + static_cast<uint32_t>(32 * ch) +
                            (static_cast<uint32_t>(q * 32) << 16),
                        r);
     tmem_wait_ld();
-    if (ch == BN / 32 - 1) {
+    if (ch == ch1 - 1) {
       tc_fence_before();
       __syncwarp();
       if (lane == 0) release();
@@ -446,7 +460,8 @@ __device__ __forceinline__ bool epilogue_split(const EpilogueCtx<T>& c, uint32_t
   const int row_base = row0 + q * 32;
   const bool rows_live = row_base < c.M;
 #pragma unroll 1
-  for (int ch = split; ch < BN / 32; ch += splits) {
+  for (int ch = ch0; ch < ch1; ++ch) {
+    if (ch % splits != split) continue;
     const int n_c = n0 + 32 * ch;
     if (!(rows_live && n_c < c.N)) continue;
     epi_chunk_begin(c, n_c, row_base, lane, it);
@@ -518,15 +533,15 @@ struct UmmaShape {
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
-  static constexpr int OFF_BAR = OFF_EPI + kEpiWarps * 2 * kEpiBufBytes;
+  static constexpr int OFF_BAR = OFF_EPI + kEpiWarps * kEpiBufs * kEpiBufBytes;
   // full[STAGES], empty[STAGES], tmem_full[2], tmem_empty[2],
-  // residual[kEpiWarps][2], drain
+  // residual[kEpiWarps][kEpiBufs], drain
   static constexpr int BAR_FULL = 0;
   static constexpr int BAR_EMPTY = STAGES;
   static constexpr int BAR_TFULL = 2 * STAGES;
   static constexpr int BAR_TEMPTY = 2 * STAGES + 2;
   static constexpr int BAR_RES = 2 * STAGES + 4;
-  static constexpr int BAR_DRAIN = BAR_RES + 2 * kEpiWarps;
+  static constexpr int BAR_DRAIN = BAR_RES + kEpiBufs * kEpiWarps;
   static constexpr int NUM_BARS = BAR_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // tmem base, abort flag
   static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 16;
@@ -567,7 +582,7 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
       mbar_init(bar(S::BAR_TFULL + b), 1);
       mbar_init(bar(S::BAR_TEMPTY + b), kEpiWarps);
     }
-    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(bar(S::BAR_RES + i), 1);
+    for (int i = 0; i < kEpiBufs * kEpiWarps; ++i) mbar_init(bar(S::BAR_RES + i), 1);
     mbar_init(bar(S::BAR_DRAIN), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -681,8 +696,11 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
     __syncwarp();
   } else {
     // --------------------------------------------------------- epilogue
-    const int e = warp - 2;  // epilogue warp index 0..3
+    const int e = warp - 2;  // epilogue warp index 0..kEpiWarps-1
     const int q = warp & 3;  // TMEM lane quarter this warp may address
+    const int hf = e / 4;    // which share of the tile's columns
+    const int ch0 = hf * (BN / 32) / kEpiHalves, ch1 = (hf + 1) * (BN / 32) / kEpiHalves;
+    const int gch0 = hf * (BN / 64) / kEpiHalves, gch1 = (hf + 1) * (BN / 64) / kEpiHalves;
     EpilogueCtx<T> c;
     c.tmY = &tmY;
     c.tmR = &tmR;
@@ -693,9 +711,9 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
     c.act = p.act;
     c.alpha = p.alpha;
     c.has_residual = p.has_residual;
-    c.ebuf0 = base + S::OFF_EPI + e * 2 * kEpiBufBytes;
-    c.ebuf_ptr0 = base_ptr + S::OFF_EPI + e * 2 * kEpiBufBytes;
-    c.rbar0 = bar(S::BAR_RES + e * 2);
+    c.ebuf0 = base + S::OFF_EPI + e * kEpiBufs * kEpiBufBytes;
+    c.ebuf_ptr0 = base_ptr + S::OFF_EPI + e * kEpiBufs * kEpiBufBytes;
+    c.rbar0 = bar(S::BAR_RES + e * kEpiBufs);
     c.pol_stream = make_l2_policy_evict_first();
     // Gated: biases are added before the activation in epilogue_tile_gated;
     // cg / cu only load them.
@@ -726,12 +744,12 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
       auto release = [tempty] { mbar_arrive(tempty); };
       bool done;
       if constexpr (kGated) {
-        done = epilogue_tile_gated<BN, T>(c, acc, q, lane, mb * S::BM, n0o, p.act, cg.bias != nullptr,
-                                          cu.bias != nullptr, bias_reg, bias_up, it, abort_flag,
-                                          release);
+        done = epilogue_tile_gated<BN, T>(c, acc, q, lane, mb * S::BM, n0o, gch0, gch1, p.act,
+                                          cg.bias != nullptr, cu.bias != nullptr, bias_reg,
+                                          bias_up, it, abort_flag, release);
       } else if (w.split < 0) {
-        done = epilogue_tile<BN, T>(c, acc, q, lane, mb * S::BM, nb * BN, bias_reg, it, abort_flag,
-                                    release);
+        done = epilogue_tile<BN, T>(c, acc, q, lane, mb * S::BM, nb * BN, ch0, ch1, bias_reg, it,
+                                    abort_flag, release);
       } else {
         const int tail = w.tile - p.dp_tiles;
         float* const partials = p.partials;
@@ -739,9 +757,9 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
         auto part_base = [partials, tail, splits](int sp) {
           return partials + static_cast<size_t>(tail * splits + sp) * 128 * BN;
         };
-        done = epilogue_split<BN, T>(c, acc, q, lane, mb * S::BM, nb * BN, bias_reg, w.split, splits,
-                                     p.tickets + (tail * 4 + q) * 2, part_base, it, abort_flag,
-                                     release);
+        done = epilogue_split<BN, T>(c, acc, q, lane, mb * S::BM, nb * BN, ch0, ch1, bias_reg,
+                                     w.split, splits, p.tickets + (tail * kEpiWarps + e) * 2,
+                                     part_base, it, abort_flag, release);
       }
       if (!done) break;
       if (e == 0 && lane == 0) trace_mark(p, 1 + i);
@@ -777,13 +795,13 @@ struct Umma2Shape {
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
-  static constexpr int OFF_BAR = OFF_EPI + kEpiWarps * 2 * kEpiBufBytes;
+  static constexpr int OFF_BAR = OFF_EPI + kEpiWarps * kEpiBufs * kEpiBufBytes;
   static constexpr int BAR_FULL = 0;              // leader only: both CTAs' bytes
   static constexpr int BAR_EMPTY = STAGES;        // both CTAs
   static constexpr int BAR_TFULL = 2 * STAGES;    // both CTAs
   static constexpr int BAR_TEMPTY = 2 * STAGES + 2;  // leader only: 8 warp arrivals
   static constexpr int BAR_RES = 2 * STAGES + 4;
-  static constexpr int BAR_DRAIN = BAR_RES + 2 * kEpiWarps;
+  static constexpr int BAR_DRAIN = BAR_RES + kEpiBufs * kEpiWarps;
   static constexpr int NUM_BARS = BAR_DRAIN + 1;
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;
   static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 16;
@@ -827,7 +845,7 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
       mbar_init(bar(S::BAR_TFULL + b), 1);
       mbar_init(bar(S::BAR_TEMPTY + b), 2 * kEpiWarps);
     }
-    for (int i = 0; i < 2 * kEpiWarps; ++i) mbar_init(bar(S::BAR_RES + i), 1);
+    for (int i = 0; i < kEpiBufs * kEpiWarps; ++i) mbar_init(bar(S::BAR_RES + i), 1);
     mbar_init(bar(S::BAR_DRAIN), 1);
     *abort_flag = 0;
     fence_mbar_init();
@@ -943,6 +961,9 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
     // --------------------------------------------- epilogue (both CTAs)
     const int e = warp - 2;
     const int q = warp & 3;
+    const int hf = e / 4;
+    const int ch0 = hf * (BN / 32) / kEpiHalves, ch1 = (hf + 1) * (BN / 32) / kEpiHalves;
+    const int gch0 = hf * (BN / 64) / kEpiHalves, gch1 = (hf + 1) * (BN / 64) / kEpiHalves;
     EpilogueCtx<T> c;
     c.tmY = &tmY;
     c.tmR = &tmR;
@@ -953,9 +974,9 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
     c.act = p.act;
     c.alpha = p.alpha;
     c.has_residual = p.has_residual;
-    c.ebuf0 = base + S::OFF_EPI + e * 2 * kEpiBufBytes;
-    c.ebuf_ptr0 = base_ptr + S::OFF_EPI + e * 2 * kEpiBufBytes;
-    c.rbar0 = bar(S::BAR_RES + e * 2);
+    c.ebuf0 = base + S::OFF_EPI + e * kEpiBufs * kEpiBufBytes;
+    c.ebuf_ptr0 = base_ptr + S::OFF_EPI + e * kEpiBufs * kEpiBufBytes;
+    c.rbar0 = bar(S::BAR_RES + e * kEpiBufs);
     c.pol_stream = make_l2_policy_evict_first();
     // Gated: biases are added before the activation in epilogue_tile_gated;
     // cg / cu only load them.
@@ -987,12 +1008,12 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
       auto release = [tempty_leader] { mbar_arrive_cluster(tempty_leader); };
       bool done;
       if constexpr (kGated) {
-        done = epilogue_tile_gated<BN, T>(c, acc, q, lane, row0, n0o, p.act, cg.bias != nullptr,
-                                          cu.bias != nullptr, bias_reg, bias_up, it, abort_flag,
-                                          release);
+        done = epilogue_tile_gated<BN, T>(c, acc, q, lane, row0, n0o, gch0, gch1, p.act,
+                                          cg.bias != nullptr, cu.bias != nullptr, bias_reg,
+                                          bias_up, it, abort_flag, release);
       } else if (w.split < 0) {
-        done = epilogue_tile<BN, T>(c, acc, q, lane, row0, nb * BN, bias_reg, it, abort_flag,
-                                    release);
+        done = epilogue_tile<BN, T>(c, acc, q, lane, row0, nb * BN, ch0, ch1, bias_reg, it,
+                                    abort_flag, release);
       } else {
         const int tail = w.tile - p.dp_tiles;
         float* const partials = p.partials;
@@ -1001,9 +1022,9 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
         auto part_base = [partials, tail, splits, r](int sp) {
           return partials + (static_cast<size_t>(tail * splits + sp) * 2 + r) * 128 * BN;
         };
-        done = epilogue_split<BN, T>(c, acc, q, lane, row0, nb * BN, bias_reg, w.split, splits,
-                                     p.tickets + ((tail * 2 + r) * 4 + q) * 2, part_base, it,
-                                     abort_flag, release);
+        done = epilogue_split<BN, T>(c, acc, q, lane, row0, nb * BN, ch0, ch1, bias_reg, w.split,
+                                     splits, p.tickets + ((tail * 2 + r) * kEpiWarps + e) * 2,
+                                     part_base, it, abort_flag, release);
       }
       if (!done) break;
       if (e == 0 && lane == 0) trace_mark(p, 1 + i);
