@@ -1,8 +1,9 @@
 """Worker for tests/test_gpu_multi.py: one process per GPU under torchrun.
 
 Checks, on every rank, the sharded engine against the single-GPU engine on
-the same seeded inputs: the column-parallel layer (gathered) and the
-column -> row MLP with its NCCL all-reduce.  Exits non-zero on a mismatch.
+the same seeded inputs: the column-parallel layer (gathered), the
+column -> row MLP and the column -> row gated FFN, each with the NVLink
+reduce-broadcast and with NCCL.  Exits non-zero on a mismatch.
 """
 import os
 import sys
@@ -14,8 +15,10 @@ import torch.distributed as dist
 
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
-from deepx_op_gpukernelcompiler_b200 import _native, fused_linear, mlp_residual  # noqa: E402
-from deepx_op_gpukernelcompiler_b200.shard import ColumnParallelLinear, ParallelMLP  # noqa: E402
+from deepx_op_gpukernelcompiler_b200 import (_native, fused_linear, gated_ffn,  # noqa: E402
+                                             mlp_residual)
+from deepx_op_gpukernelcompiler_b200.shard import (ColumnParallelLinear,  # noqa: E402
+                                                   ParallelGatedFFN, ParallelMLP)
 
 
 def main() -> int:
@@ -57,6 +60,21 @@ def main() -> int:
                 tol = 2e-2 + 2e-2 * ref.abs()
                 if bool((err > tol).any()):
                     failures.append(f"MLP ({mode}, chunks={chunks}, call {rep}) off by up to "
+                                    f"{err.max().item():.4g}")
+
+        Wg = (torch.randn(K, H, generator=g, device=dev) / K ** 0.5).bfloat16()
+        Wu = (torch.randn(K, H, generator=g, device=dev) / K ** 0.5).bfloat16()
+        bg = (torch.rand(H, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
+        bu = (torch.rand(H, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
+        ref = gated_ffn(X, Wg, bg, Wu, bu, W2, b2, "silu").float()
+        for mode in ("nccl", "fused"):
+            ffn = ParallelGatedFFN(Wg, bg, Wu, bu, W2, b2, "silu", mode=mode)
+            for rep in range(2):
+                out = ffn(X).float()
+                torch.cuda.synchronize()
+                err = (out - ref).abs()
+                if bool((err > 2e-2 + 2e-2 * ref.abs()).any()):
+                    failures.append(f"gated FFN ({mode}, call {rep}) off by up to "
                                     f"{err.max().item():.4g}")
         status = _native.device_status(torch.cuda.current_stream(dev).cuda_stream)
         if status:

@@ -14,7 +14,8 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 import oracle
-from deepx_op_gpukernelcompiler_b200.shard import ColumnParallelLinear, ParallelMLP, shard_bounds
+from deepx_op_gpukernelcompiler_b200.shard import (ColumnParallelLinear, ParallelGatedFFN,
+                                                   ParallelMLP, shard_bounds)
 
 
 def _free_port() -> int:
@@ -30,6 +31,26 @@ def oracle_linear(X, W, bias=None, activation=None, residual=None, out=None):
         out.copy_(Y)
         return out
     return Y
+
+
+def oracle_gated(X, Wg, Wu, bg=None, bu=None, activation="silu", out=None):
+    Y = torch.from_numpy(oracle.gated_linear_f64(X, Wg, bg, Wu, bu, activation)).to(X.dtype)
+    if out is not None:
+        out.copy_(Y)
+        return out
+    return Y
+
+
+def _gated_inputs(M=24, K=40, H=200, seed=1):
+    g = torch.Generator().manual_seed(seed)
+    X = torch.randn(M, K, generator=g, dtype=torch.float64)
+    Wg = torch.randn(K, H, generator=g, dtype=torch.float64) / K ** 0.5
+    Wu = torch.randn(K, H, generator=g, dtype=torch.float64) / K ** 0.5
+    bg = torch.rand(H, generator=g, dtype=torch.float64) * 0.2 - 0.1
+    bu = torch.rand(H, generator=g, dtype=torch.float64) * 0.2 - 0.1
+    Wo = torch.randn(H, K, generator=g, dtype=torch.float64) / H ** 0.5
+    bo = torch.rand(K, generator=g, dtype=torch.float64) * 0.2 - 0.1
+    return X, Wg, bg, Wu, bu, Wo, bo
 
 
 def _inputs(M=24, K=40, H=200, seed=0):
@@ -55,8 +76,13 @@ def _worker(rank, world, port, results):
         Y_full = col_g(X)
         mlp = ParallelMLP(W1, b1, W2, b2, "gelu", linear_fn=oracle_linear, chunks=3, align=8)
         Y_mlp = mlp(X)
+        Xg, Wg, bg, Wu, bu, Wo, bo = _gated_inputs()
+        ffn = ParallelGatedFFN(Wg, bg, Wu, bu, Wo, bo, "silu", gated_fn=oracle_gated,
+                               linear_fn=oracle_linear, chunks=2, align=8)
+        Y_gated = ffn(Xg)
         results[rank] = {"n0": col.n0, "n1": col.n1, "Y_local": Y_local.numpy(),
-                         "Y_full": Y_full.numpy(), "Y_mlp": Y_mlp.numpy()}
+                         "Y_full": Y_full.numpy(), "Y_mlp": Y_mlp.numpy(),
+                         "Y_gated": Y_gated.numpy(), "gated_mode": ffn.mode}
     finally:
         dist.destroy_process_group()
 
@@ -72,6 +98,7 @@ def test_column_and_mlp_sharding(world):
     X, W1, b1, W2, b2 = _inputs()
     full = oracle.fused_linear_f64(X, W1, b1, "silu")
     mlp = oracle.mlp_residual_f64(X, W1, b1, W2, b2, "gelu")
+    gated = oracle.gated_ffn_f64(*_gated_inputs(), act="silu")
     covered = []
     for r in range(world):
         n0, n1 = res[r]["n0"], res[r]["n1"]
@@ -79,6 +106,8 @@ def test_column_and_mlp_sharding(world):
         np.testing.assert_allclose(res[r]["Y_local"], full[:, n0:n1], rtol=1e-12, atol=1e-12)
         np.testing.assert_allclose(res[r]["Y_full"], full, rtol=1e-12, atol=1e-12)
         np.testing.assert_allclose(res[r]["Y_mlp"], mlp, rtol=1e-10, atol=1e-10)
+        np.testing.assert_allclose(res[r]["Y_gated"], gated, rtol=1e-10, atol=1e-10)
+        assert res[r]["gated_mode"] == "nccl"
     assert covered[0][0] == 0 and covered[-1][1] == W1.shape[1]
     assert all(a[1] == b[0] for a, b in zip(covered, covered[1:]))
 
