@@ -72,6 +72,8 @@ SIGNATURES = {
     "dx_fused_gated_linear_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, ctypes.c_int,
                                                                ctypes.c_int]),
     "dx_select_kernel": (ctypes.c_int, [_i64, _i64, _i64, ctypes.c_int]),
+    "dx_copy_2d_async": (ctypes.c_int, [_vp, ctypes.c_size_t, _vp, ctypes.c_size_t,
+                                        ctypes.c_size_t, ctypes.c_size_t, _vp]),
     "dx_last_error_string": (ctypes.c_char_p, []),
     "dx_last_launch_plan": (ctypes.c_char_p, []),
     "dx_set_trace_buffer": (ctypes.c_int, [_vp, ctypes.c_size_t]),

@@ -763,6 +763,18 @@ size_t dx_fused_gated_linear_workspace_size(int64_t M, int64_t N, int64_t K, int
   return 0;  // the gated tensor-core kernels take no split tail
 }
 
+int dx_copy_2d_async(void* dst, size_t dst_pitch, const void* src, size_t src_pitch,
+                     size_t width_bytes, size_t rows, void* stream) {
+  t_last_error.clear();
+  if (rows == 0 || width_bytes == 0) return DX_OK;
+  if (dst == nullptr || src == nullptr || dst_pitch < width_bytes || src_pitch < width_bytes)
+    return fail(DX_ERR_INVALID_ARGUMENT, "copy_2d: NULL pointer or pitch below the row width");
+  const cudaError_t e = cudaMemcpy2DAsync(dst, dst_pitch, src, src_pitch, width_bytes, rows,
+                                          cudaMemcpyDefault, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy2DAsync");
+  return DX_OK;
+}
+
 int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype) {
   if (dtype == DX_DTYPE_F32 || K <= 0) return DX_KERNEL_SIMT;
   if ((K * 2) % 16 != 0 || (N * 2) % 16 != 0) return DX_KERNEL_SIMT;

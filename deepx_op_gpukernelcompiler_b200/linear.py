@@ -199,6 +199,113 @@ def fused_gated_linear(X: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor,
     return out
 
 
+# Device buffers and side streams of fused_linear_host, per (device, shape).
+_host_lock = threading.Lock()
+_host_states: dict[tuple, "_HostState"] = {}
+
+
+class _HostState:
+    def __init__(self, device: torch.device, M: int, N: int, K: int, dtype: torch.dtype):
+        self.Xd = torch.empty((M, K), dtype=dtype, device=device)
+        self.Wd = torch.empty((K, N), dtype=dtype, device=device)
+        self.bd = torch.empty((N,), dtype=dtype, device=device)
+        self.Yd = torch.empty((M, N), dtype=dtype, device=device)
+        self.h2d = torch.cuda.Stream(device)
+        self.d2h = torch.cuda.Stream(device)
+
+
+def release_host_buffers() -> None:
+    """Free the device buffers cached by fused_linear_host."""
+    with _host_lock:
+        _host_states.clear()
+
+
+def _block_bounds(n: int, blocks: int, align: int) -> list[tuple[int, int]]:
+    units = (n + align - 1) // align
+    blocks = max(1, min(blocks, units))
+    out = []
+    for j in range(blocks):
+        u0, u1 = j * units // blocks, (j + 1) * units // blocks
+        out.append((min(u0 * align, n), min(u1 * align, n)))
+    return [b for b in out if b[1] > b[0]]
+
+
+def fused_linear_host(X: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None = None,
+                      activation=None, out: torch.Tensor | None = None, device=None,
+                      col_blocks: int = 4, row_blocks: int = 2,
+                      kernel: str = "auto") -> torch.Tensor:
+    """Y = act(X @ W + bias) for tensors in host memory, computed on `device`.
+
+    The problem is cut into row_blocks x col_blocks output blocks (boundaries
+    multiples of 256).  On a copy stream, X's row blocks and W's column
+    blocks go to the device in the order the blocks are computed; each block
+    is one fused launch on the current stream; on a second copy stream each
+    finished block of Y returns to `out` (strided, dx_copy_2d_async) while
+    later blocks are still copied in or computed.  The current stream waits
+    for the last copy, so `out` is complete once it is synchronised.  Pass
+    pinned tensors: pageable memory makes the copies synchronous.  W and bias
+    are copied on every call (host-resident weights)."""
+    if X.device.type != "cpu" or W.device.type != "cpu":
+        raise ValueError("fused_linear_host takes host tensors; use fused_linear for device tensors")
+    if X.dtype not in DTYPE_CODES:
+        raise ValueError(f"unsupported dtype {X.dtype}; expected float32, float16 or bfloat16")
+    _check_matrix("X", X, None, None)
+    M, K = X.shape
+    _check_matrix("W", W, K, None)
+    N = W.shape[1]
+    if bias is not None and (bias.dim() != 1 or bias.shape[0] != N or not bias.is_contiguous()):
+        raise ValueError(f"bias must be a contiguous tensor of shape ({N},)")
+    for name, t in (("W", W), ("bias", bias), ("out", out)):
+        if t is not None and (t.dtype != X.dtype or t.device.type != "cpu"):
+            raise ValueError(f"{name} must be a host tensor of dtype {X.dtype}")
+    if out is None:
+        out = torch.empty((M, N), dtype=X.dtype, pin_memory=True)
+    _check_matrix("out", out, M, N)
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    key = (dev.index, M, N, K, X.dtype)
+    with _host_lock:
+        st = _host_states.get(key)
+        if st is None:
+            st = _host_states[key] = _HostState(dev, M, N, K, X.dtype)
+    lib = nat.load()
+    esz = X.element_size()
+    rows = _block_bounds(M, row_blocks, 256)
+    cols = _block_bounds(N, col_blocks, 256)
+
+    def copy2d(dst_ptr, dst_ld, src_ptr, src_ld, width, nrows, stream):
+        nat.check("dx_copy_2d_async", lib.dx_copy_2d_async(
+            dst_ptr, dst_ld * esz, src_ptr, src_ld * esz, width * esz, nrows, stream))
+
+    with torch.cuda.device(dev):
+        cur = torch.cuda.current_stream(dev)
+        st.h2d.wait_stream(cur)  # the device buffers are free
+        st.d2h.wait_stream(cur)
+        h2d, d2h = st.h2d.cuda_stream, st.d2h.cuda_stream
+        if bias is not None:
+            copy2d(st.bd.data_ptr(), N, bias.data_ptr(), N, N, 1, h2d)
+        ev_w, ev_x = [], []
+        for j, (n0, n1) in enumerate(cols):
+            copy2d(st.Wd.data_ptr() + n0 * esz, N, W.data_ptr() + n0 * esz, _ld(W), n1 - n0, K, h2d)
+            ev_w.append(st.h2d.record_event())
+            if j == 0:
+                for m0, m1 in rows:
+                    copy2d(st.Xd.data_ptr() + m0 * K * esz, K, X.data_ptr() + m0 * _ld(X) * esz,
+                           _ld(X), K, m1 - m0, h2d)
+                    ev_x.append(st.h2d.record_event())
+        for j, (n0, n1) in enumerate(cols):
+            cur.wait_event(ev_w[j])
+            for i, (m0, m1) in enumerate(rows):
+                cur.wait_event(ev_x[i])
+                fused_linear(st.Xd[m0:m1], st.Wd[:, n0:n1],
+                             st.bd[n0:n1] if bias is not None else None, activation,
+                             out=st.Yd[m0:m1, n0:n1], kernel=kernel)
+                st.d2h.wait_event(cur.record_event())
+                copy2d(out.data_ptr() + (m0 * _ld(out) + n0) * esz, _ld(out),
+                       st.Yd.data_ptr() + (m0 * N + n0) * esz, N, n1 - n0, m1 - m0, d2h)
+        cur.wait_stream(st.d2h)
+    return out
+
+
 def selected_kernel(M: int, N: int, K: int, dtype: torch.dtype) -> str:
     """Name of the kernel variant the engine picks for this problem."""
     code = nat.load().dx_select_kernel(M, N, K, DTYPE_CODES[dtype])

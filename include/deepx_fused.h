@@ -167,6 +167,16 @@ int dx_fused_gated_linear(const void* X, const void* Wg, const void* Wu,
                           void* workspace, size_t workspace_bytes,
                           void* stream);
 
+/* Rows of a strided 2-D region copied on `stream` (cudaMemcpy2DAsync with the
+ * direction inferred from the pointers): `rows` rows of `width_bytes` bytes,
+ * row pitches in bytes.  No reference counterpart: the staging step of the
+ * host-buffer entry (Python fused_linear_host), which moves column blocks of
+ * W and Y between pinned host memory and the device so that the copies of one
+ * block overlap the fused launch of another.  Pinned host memory keeps the
+ * copy asynchronous. */
+int dx_copy_2d_async(void* dst, size_t dst_pitch, const void* src, size_t src_pitch,
+                     size_t width_bytes, size_t rows, void* stream);
+
 /* Workspace bytes that dx_fused_gated_linear needs (0: none). */
 size_t dx_fused_gated_linear_workspace_size(int64_t M, int64_t N, int64_t K,
                                             int dtype, int kernel);

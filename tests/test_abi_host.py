@@ -104,6 +104,23 @@ def test_gated_workspace_sizes(lib):
     assert lib.dx_fused_gated_linear_workspace_size(16, 512, 512, nat.DX_DTYPE_F32, 0) == 0
 
 
+def test_copy_2d_validation(lib):
+    assert lib.dx_copy_2d_async(None, 0, None, 0, 0, 5, None) == nat.DX_OK  # empty
+    assert lib.dx_copy_2d_async(FAKE, 8, FAKE, 16, 16, 2, None) == nat.DX_ERR_INVALID_ARGUMENT
+    assert "pitch" in nat.last_error()
+    assert lib.dx_copy_2d_async(None, 16, FAKE, 16, 16, 2, None) == nat.DX_ERR_INVALID_ARGUMENT
+
+
+def test_host_entry_rejects_device_or_mismatched_tensors():
+    from deepx_op_gpukernelcompiler_b200 import fused_linear_host
+    X = torch.zeros(4, 8, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="host tensor"):
+        fused_linear_host(X, torch.zeros(8, 4, dtype=torch.float16))
+    with pytest.raises(ValueError, match="bias"):
+        fused_linear_host(X, torch.zeros(8, 4, dtype=torch.bfloat16),
+                          torch.zeros(3, dtype=torch.bfloat16))
+
+
 def test_empty_problem_is_a_no_op(lib):
     assert _call(lib, M=0) == nat.DX_OK
     assert _call(lib, N=0) == nat.DX_OK

@@ -281,3 +281,27 @@ def test_split_tail(M, K, N, kern):
     assert torch.equal(Ya, Yb), "split reduction is not deterministic"
     assert int(ws[:65536].view(torch.int32).abs().sum().item()) == 0, "tickets not reset"
     _status_clean()
+
+
+@pytest.mark.parametrize("M,K,N,blocks", [(8192, 4096, 14336, (2, 4)), (300, 136, 1000, (3, 5)),
+                                           (1, 64, 520, (1, 2)), (513, 256, 760, (2, 3))])
+def test_host_entry_matches_device_entry(M, K, N, blocks):
+    """fused_linear_host (blocks copied in and out around per-block launches)
+    gives the device entry's result; unpinned and pinned host memory."""
+    from deepx_op_gpukernelcompiler_b200 import fused_linear_host
+    X, W, b, _ = _rand(M, K, N, torch.bfloat16, seed=M + N)
+    ref = fused_linear(X.to(DEV), W.to(DEV), b.to(DEV), "silu").float().cpu()
+    for pinned in (True, False):
+        Xh, Wh, bh = (t.pin_memory() if pinned else t for t in (X, W, b))
+        out = torch.empty(M, N, dtype=torch.bfloat16)
+        if pinned:
+            out = out.pin_memory()
+        fused_linear_host(Xh, Wh, bh, "silu", out=out, device=DEV, row_blocks=blocks[0],
+                          col_blocks=blocks[1])
+        torch.cuda.synchronize()
+        _assert_close(out, ref, torch.bfloat16, f"host {M}x{K}x{N} pinned={pinned}")
+    # No bias, default blocks, output allocated by the call.
+    out = fused_linear_host(X, W, None, None, device=DEV)
+    torch.cuda.synchronize()
+    ref_nb = fused_linear(X.to(DEV), W.to(DEV), None, None).float().cpu()
+    _assert_close(out, ref_nb, torch.bfloat16, "host, no bias")
