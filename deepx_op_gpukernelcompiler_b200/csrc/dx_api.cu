@@ -200,7 +200,13 @@ DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sms, bool gated = fa
   d.n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
   d.kbt = static_cast<int>((K + 63) / 64);
   d.units = static_cast<long long>(d.n_tiles) * d.kbt;
-  const long long want = sms;  // one CTA per SM
+  // One CTA per SM and an even split of the units, unless there are at
+  // least half as many tiles as SMs: then one CTA streams each whole tile —
+  // no split-K partials or fix-up, and those CTAs already saturate HBM
+  // (M=16, N=28672, K=8192: 82.4 us with the split over 148 CTAs, 76.3 us
+  // with 112 whole tiles).
+  long long want = sms;
+  if (2LL * d.n_tiles >= sms && d.n_tiles <= sms) want = d.n_tiles;
   d.grid = static_cast<int>(std::max<long long>(1, std::min<long long>(d.units, want)));
   int ms = 1;
   for (int t = 0; t < d.n_tiles; ++t) {
@@ -610,9 +616,24 @@ bool decode_eligible(const Problem& p) {
   return tma_ok(p.X, p.ldx) && tma_ok(p.W, p.ldw);
 }
 
+// Skinny-M problems the decode kernel streams faster than the single-CTA
+// tensor-core kernel, measured on B200 (fp16, K = 4096 and 8192, N = 3584 to
+// 28672): every gated problem up to M = 64; plain problems up to M = 16, and
+// up to M = 32 when W has at least half as many 256-column tiles as SMs (one
+// whole tile per CTA).  For plain problems with 32 < M <= 64 the tensor-core
+// kernel's 128-row tiles stream W faster (M = 64, N = 28672, K = 8192:
+// 82 us against 97 us).
+bool decode_preferred(int64_t M, int64_t N, int sms, bool gated) {
+  if (gated) return true;
+  const int mn = decode_mn(M);
+  if (mn == 16) return true;
+  if (mn == 32) return 2 * ((N + kDecodeTileN - 1) / kDecodeTileN) >= sms;
+  return false;
+}
+
 int select_variant(const Problem& p, int sms, bool ws_known) {
   if (p.dtype == DX_DTYPE_F32 || p.K == 0) return DX_KERNEL_SIMT;
-  if (decode_eligible(p)) {
+  if (decode_eligible(p) && (decode_preferred(p.M, p.N, sms, p.gated) || !umma_eligible(p))) {
     if (!ws_known) return DX_KERNEL_DECODE;
     const DecodePlan d = decode_plan(p.M, p.N, p.K, sms, p.gated);
     if (p.ws != nullptr && p.ws_bytes >= d.bytes && aligned16(p.ws)) return DX_KERNEL_DECODE;
@@ -778,7 +799,16 @@ int dx_copy_2d_async(void* dst, size_t dst_pitch, const void* src, size_t src_pi
 int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype) {
   if (dtype == DX_DTYPE_F32 || K <= 0) return DX_KERNEL_SIMT;
   if ((K * 2) % 16 != 0 || (N * 2) % 16 != 0) return DX_KERNEL_SIMT;
-  if (M <= kDecodeMaxM && (N + kDecodeTileN - 1) / kDecodeTileN <= kDecodeMaxTiles) return DX_KERNEL_DECODE;
+  int sms = 148;  // B200; the device's own count when one is current
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || device_sms(dev, &sms) != DX_OK) {
+    sms = 148;
+    (void)cudaGetLastError();
+    t_last_error.clear();  // no device: not an error of this query
+  }
+  if (M <= kDecodeMaxM && (N + kDecodeTileN - 1) / kDecodeTileN <= kDecodeMaxTiles &&
+      decode_preferred(M, N, sms, false))
+    return DX_KERNEL_DECODE;
   return DX_KERNEL_UMMA;
 }
 

@@ -130,6 +130,12 @@ def test_empty_problem_is_a_no_op(lib):
 def test_kernel_selection(lib):
     assert lib.dx_select_kernel(256, 512, 512, nat.DX_DTYPE_F32) == nat.DX_KERNEL_SIMT
     assert lib.dx_select_kernel(16, 28672, 8192, nat.DX_DTYPE_F16) == nat.DX_KERNEL_DECODE
+    assert lib.dx_select_kernel(1, 3584, 8192, nat.DX_DTYPE_F16) == nat.DX_KERNEL_DECODE
+    # 16 < M <= 32: decode only when W has >= SMs/2 tiles of 256 columns
+    assert lib.dx_select_kernel(32, 28672, 8192, nat.DX_DTYPE_F16) == nat.DX_KERNEL_DECODE
+    assert lib.dx_select_kernel(32, 3584, 8192, nat.DX_DTYPE_F16) == nat.DX_KERNEL_UMMA
+    # 32 < M <= 64: the single-CTA tensor-core kernel streams W faster
+    assert lib.dx_select_kernel(64, 28672, 8192, nat.DX_DTYPE_BF16) == nat.DX_KERNEL_UMMA
     assert lib.dx_select_kernel(8192, 14336, 4096, nat.DX_DTYPE_BF16) == nat.DX_KERNEL_UMMA
     assert lib.dx_select_kernel(8192, 14336, 4095, nat.DX_DTYPE_BF16) == nat.DX_KERNEL_SIMT
     assert lib.dx_select_kernel(64, 100, 0, nat.DX_DTYPE_BF16) == nat.DX_KERNEL_SIMT
