@@ -217,8 +217,11 @@ DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sms, bool gated = fa
   }
   d.max_seg = ms;
   d.ticket_bytes = kTicketSlabBytes;
-  d.bytes = d.ticket_bytes +
-            static_cast<size_t>(d.n_tiles) * d.max_seg * d.mn * (128 * d.nh) * sizeof(float);
+  // Whole tiles only (every tile streamed by one CTA): no tickets, no
+  // partials, no workspace.
+  d.bytes = ms == 1 ? 0
+                    : d.ticket_bytes + static_cast<size_t>(d.n_tiles) * d.max_seg * d.mn *
+                                           (128 * d.nh) * sizeof(float);
   return d;
 }
 
@@ -491,8 +494,11 @@ int launch_decode(const Problem& pr, int dev, int sms, const DecodePlan& d) {
   p.bias = pr.bias;
   p.residual = pr.R;
   p.Y = pr.Y;
-  p.tickets = static_cast<int*>(pr.ws);
-  p.partials = reinterpret_cast<float*>(static_cast<char*>(pr.ws) + d.ticket_bytes);
+  // Unused by whole-tile plans (max_seg == 1), which may run without a workspace.
+  p.tickets = pr.ws != nullptr ? static_cast<int*>(pr.ws) : nullptr;
+  p.partials = pr.ws != nullptr
+                   ? reinterpret_cast<float*>(static_cast<char*>(pr.ws) + d.ticket_bytes)
+                   : nullptr;
   p.act = pr.act;
   p.alpha = pr.alpha;
   p.gated = pr.gated ? 1 : 0;
@@ -636,7 +642,8 @@ int select_variant(const Problem& p, int sms, bool ws_known) {
   if (decode_eligible(p) && (decode_preferred(p.M, p.N, sms, p.gated) || !umma_eligible(p))) {
     if (!ws_known) return DX_KERNEL_DECODE;
     const DecodePlan d = decode_plan(p.M, p.N, p.K, sms, p.gated);
-    if (p.ws != nullptr && p.ws_bytes >= d.bytes && aligned16(p.ws)) return DX_KERNEL_DECODE;
+    if (d.bytes == 0 || (p.ws != nullptr && p.ws_bytes >= d.bytes && aligned16(p.ws)))
+      return DX_KERNEL_DECODE;
   }
   if (umma_eligible(p)) return DX_KERNEL_UMMA;
   return DX_KERNEL_SIMT;
@@ -703,7 +710,7 @@ int run(const Problem& p, int kernel) {
                   "16-byte-aligned X/W with row pitches that are multiples of 16 bytes",
                   kDecodeMaxM, (long long)(kDecodeMaxTiles * kDecodeTileN));
     const DecodePlan d = decode_plan(p.M, p.N, p.K, sms, p.gated);
-    if (p.ws == nullptr || p.ws_bytes < d.bytes || !aligned16(p.ws))
+    if (d.bytes > 0 && (p.ws == nullptr || p.ws_bytes < d.bytes || !aligned16(p.ws)))
       return fail(DX_ERR_WORKSPACE, "decode kernel needs a 16-byte-aligned workspace of %zu bytes",
                   d.bytes);
   }

@@ -167,6 +167,27 @@ def test_k_zero_gives_act_of_bias():
     assert torch.equal(Y.cpu(), torch.relu(b).expand(5, 16))
 
 
+@pytest.mark.parametrize("M", [1, 4, 16])
+def test_whole_tile_decode_needs_no_workspace(M):
+    """With at least half as many 256-column tiles as SMs the decode kernel
+    streams one whole tile per CTA and needs no workspace: AUTO picks it even
+    when the caller passes none (M = 1 included)."""
+    lib = nat.load()
+    K, N = 1024, 28672
+    X, W, b, _ = _rand(M, K, N, torch.float16, seed=M)
+    Xd, Wd, bd = X.to(DEV), W.to(DEV), b.to(DEV)
+    Y = torch.empty(M, N, dtype=torch.float16, device=DEV)
+    assert lib.dx_fused_linear_workspace_size(M, N, K, nat.DX_DTYPE_F16, nat.DX_KERNEL_DECODE) == 0
+    rc = lib.dx_fused_linear(Xd.data_ptr(), Wd.data_ptr(), bd.data_ptr(), None, Y.data_ptr(),
+                             M, N, K, K, N, 0, N, nat.DX_DTYPE_F16, nat.DX_ACT_GELU_ERF, None, 0,
+                             None)
+    assert rc == nat.DX_OK, nat.last_error()
+    assert nat.last_launch_plan().startswith("decode"), nat.last_launch_plan()
+    torch.cuda.synchronize()
+    _assert_close(Y, oracle.fused_linear_f64(X, W, b, "gelu_erf"), torch.float16, f"M={M}")
+    _status_clean()
+
+
 def test_decode_without_workspace_is_rejected():
     lib = nat.load()
     X, W, b, _ = _rand(16, 128, 256, torch.float16, seed=1)

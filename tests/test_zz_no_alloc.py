@@ -69,11 +69,17 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
-    # 64 padded rows x 65536 columns of partial sums: 16 MiB > the 8 MiB array.
-    X, W, b, _ = _inputs(64, 64, 65536, torch.float16, 3)
-    Y = torch.empty(64, 65536, dtype=torch.float16, device=DEV)
-    rc = nat.load().dx_fused_linear_decode_noalloc(
-        X.data_ptr(), W.data_ptr(), b.data_ptr(), None, Y.data_ptr(), 64, 65536, 64, 64, 65536,
-        0, 65536, nat.DX_DTYPE_F16, nat.DX_ACT_NONE, torch.cuda.current_stream(DEV).cuda_stream)
+    # 64 tiles of 256 columns (fewer than half the SMs, so K is split): up to
+    # 3 segments x 64 padded rows x 256 columns of fp32 partial sums per tile,
+    # 12.6 MiB > the 8 MiB array.
+    M, K, N = 64, 8192, 16384
+    lib = nat.load()
+    assert lib.dx_fused_linear_workspace_size(M, N, K, nat.DX_DTYPE_F16,
+                                              nat.DX_KERNEL_DECODE) > (8 << 20)
+    X, W, b, _ = _inputs(M, K, N, torch.float16, 3)
+    Y = torch.empty(M, N, dtype=torch.float16, device=DEV)
+    rc = lib.dx_fused_linear_decode_noalloc(
+        X.data_ptr(), W.data_ptr(), b.data_ptr(), None, Y.data_ptr(), M, N, K, K, N,
+        0, N, nat.DX_DTYPE_F16, nat.DX_ACT_NONE, torch.cuda.current_stream(DEV).cuda_stream)
     assert rc == nat.DX_ERR_WORKSPACE
     assert "static scratch" in nat.last_error()
