@@ -44,7 +44,7 @@ extern "C" {
 /* ---- return codes ------------------------------------------------------ */
 #define DX_OK                     0
 #define DX_ERR_INVALID_ARGUMENT  -1   /* bad shape, stride, pointer or enum   */
-#define DX_ERR_UNSUPPORTED       -2   /* valid request this build cannot run  */
+#define DX_ERR_UNSUPPORTED       -2   /* valid request the library cannot run */
 #define DX_ERR_CUDA              -3   /* a CUDA runtime/driver call failed    */
 #define DX_ERR_WORKSPACE         -4   /* workspace missing or too small       */
 #define DX_ERR_DEVICE_TIMEOUT    -5   /* a kernel's bounded wait ran out      */
