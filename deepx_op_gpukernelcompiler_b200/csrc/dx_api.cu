@@ -726,6 +726,25 @@ int run(const Problem& p, int kernel) {
   }
 }
 
+// One CTA waits, through the kernels' bounded mbarrier wait, on a barrier
+// that nothing completes: after kWaitLimitNs the wait gives up, raises the
+// device status word and the thread records 2 in *result (1 had the wait
+// completed).  Exercises the failure path without a fault or a hang.
+__global__ void selftest_wait_kernel(int* result) {
+  __shared__ __align__(8) uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    dx::mbar_init(dx::smem_u32(&bar), 1);
+    abort_flag = 0;
+    dx::fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const bool ok = dx::mbar_wait(dx::smem_u32(&bar), 0u, &abort_flag);
+    *result = ok ? 1 : 2;
+  }
+}
+
 }  // namespace
 
 extern "C" {
@@ -959,6 +978,15 @@ int dx_device_status(void* stream, int* status) {
     if (e != cudaSuccess) return cuda_fail(e, "clear device status");
   }
   *status = v;
+  return DX_OK;
+}
+
+int dx_selftest_bounded_wait(int* result, void* stream) {
+  t_last_error.clear();
+  if (result == nullptr) return fail(DX_ERR_INVALID_ARGUMENT, "result is NULL");
+  selftest_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(result);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch selftest_wait_kernel");
   return DX_OK;
 }
 

@@ -226,6 +226,14 @@ const char* dx_last_launch_plan(void);
  * Process-wide setting; the caller owns the buffer. */
 int dx_set_trace_buffer(void* device_buffer, size_t bytes);
 
+/* Failure-path self-test (no reference counterpart): launches one CTA on
+ * `stream` that waits, through the same bounded wait every kernel uses, on a
+ * barrier nothing completes.  About a second later the wait gives up, the
+ * device status word gets DX_DEVICE_STATUS_TIMEOUT and the device int
+ * *result is set to 2 (1 would mean the wait completed).  The context stays
+ * usable; read the status with dx_device_status. */
+int dx_selftest_bounded_wait(int* result, void* stream);
+
 /* Synchronises `stream`, then reads and clears the calling device's status
  * word (DX_DEVICE_STATUS_* bits) into *status. */
 int dx_device_status(void* stream, int* status);

@@ -326,3 +326,21 @@ def test_host_entry_matches_device_entry(M, K, N, blocks):
     torch.cuda.synchronize()
     ref_nb = fused_linear(X.to(DEV), W.to(DEV), None, None).float().cpu()
     _assert_close(out, ref_nb, torch.bfloat16, "host, no bias")
+
+
+def test_bounded_wait_reports_timeout_and_context_survives():
+    """A wait that nothing completes gives up after its bound (about a second),
+    sets DX_DEVICE_STATUS_TIMEOUT and returns; the next launches run normally."""
+    lib = nat.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    assert nat.device_status(stream) == 0
+    flag = torch.zeros(1, dtype=torch.int32, device=DEV)
+    nat.check("dx_selftest_bounded_wait", lib.dx_selftest_bounded_wait(flag.data_ptr(), stream))
+    assert nat.device_status(stream) == nat.DX_DEVICE_STATUS_TIMEOUT
+    assert flag.item() == 2
+    assert nat.device_status(stream) == 0  # read-and-clear
+    X, W, b, _ = _rand(300, 256, 512, torch.bfloat16, seed=77)
+    Y = fused_linear(X.to(DEV), W.to(DEV), b.to(DEV), "silu")
+    torch.cuda.synchronize()
+    _assert_close(Y, oracle.fused_linear_f64(X, W, b, "silu"), torch.bfloat16, "after timeout")
+    _status_clean()
