@@ -199,7 +199,8 @@ def fused_gated_linear(X: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor,
     return out
 
 
-# Device buffers and side streams of fused_linear_host, per (device, shape).
+# Device buffers and side streams of fused_linear_host, per (device, calling
+# stream, shape): calls on different streams never share buffers.
 _host_lock = threading.Lock()
 _host_states: dict[tuple, "_HostState"] = {}
 
@@ -262,7 +263,8 @@ def fused_linear_host(X: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | Non
         out = torch.empty((M, N), dtype=X.dtype, pin_memory=True)
     _check_matrix("out", out, M, N)
     dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
-    key = (dev.index, M, N, K, X.dtype)
+    caller = torch.cuda.current_stream(dev).cuda_stream
+    key = (dev.index, caller, M, N, K, X.dtype)
     with _host_lock:
         st = _host_states.get(key)
         if st is None:
