@@ -149,6 +149,9 @@ class Plan:
             ctypes.byref(handle), request.M, request.N, request.K, DTYPE_CODES[request.dtype],
             activation_code(act), request.scale, nat.KERNEL_NAMES[kernel]))
         self._handle = handle
+        # The native plan holds one workspace pointer: setting it and calling
+        # must not interleave between threads (each stream has its own workspace).
+        self._call_lock = threading.Lock()
 
     def __del__(self):
         handle = getattr(self, "_handle", None)
@@ -169,7 +172,7 @@ class Plan:
             raise ValueError(f"{r.pattern} {'needs' if self.has_residual else 'takes no'} residual")
         if out is None:
             out = torch.empty((r.M, r.N), dtype=r.dtype, device=x.device)
-        with torch.cuda.device(x.device):
+        with torch.cuda.device(x.device), self._call_lock:
             stream = torch.cuda.current_stream(x.device).cuda_stream
             need = self._lib.dx_plan_workspace_size(self._handle)
             ws = _workspace(x.device, stream, need)
