@@ -192,7 +192,10 @@ size_t dx_fused_gated_linear_workspace_size(int64_t M, int64_t N, int64_t K,
  * patterns, the attention scale for `attention_score` (fusion.py:24).
  * `kernel` is a DX_KERNEL_* variant (DX_KERNEL_AUTO normally).  A plan holds
  * no device memory; give it the workspace dx_plan_workspace_size() asks for
- * (zero-filled once, one call at a time) with dx_plan_set_workspace.
+ * (zero-filled once, one call at a time) with dx_plan_set_workspace.  The
+ * workspace pointer is plan state: threads that share a plan serialise
+ * dx_plan_set_workspace + dx_plan_call (the launch is asynchronous, so the
+ * critical section is short), or use one plan per stream.
  */
 typedef struct dx_plan dx_plan;
 int dx_plan_create(dx_plan** plan, int64_t M, int64_t N, int64_t K, int dtype, int act,
