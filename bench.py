@@ -283,9 +283,18 @@ def run_gpu(args) -> None:
     Y = torch.empty(w.M, n_loc, dtype=dt, device=dev)
     flush_buf = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
     stream = torch.cuda.current_stream(dev)
+    if w.gated:
+        if not args.profile:
+            raise SystemExit(f"{w.name} runs in --profile mode (its bench line is an extra)")
+        from deepx_op_gpukernelcompiler_b200 import fused_gated_linear
+        Wu = (torch.randn(w.K, n_loc, generator=gen, device=dev) / math.sqrt(w.K)).to(dt)
+        bu = (torch.rand(n_loc, generator=gen, device=dev) * 0.2 - 0.1).to(dt)
 
     def step():
-        fused_linear(X, Wt, b, w.act, out=Y)
+        if w.gated:
+            fused_gated_linear(X, Wt, Wu, b, bu, w.act, out=Y)
+        else:
+            fused_linear(X, Wt, b, w.act, out=Y)
 
     def flush():
         flush_buf.zero_()

@@ -1,10 +1,11 @@
 """Seeded synthetic workloads of the fused-linear hot path.
 
-Each workload is a fused linear (or the two-layer MLP chain) at a fixed
-shape, dtype, activation and seed.  Inputs are drawn with a torch Generator
-seeded with the workload's seed, in the order X, W, bias (MLP: X, W1, b1,
-W2, b2): X ~ N(0, 1), W ~ N(0, 1/fan_in), bias ~ U(-0.1, 0.1), generated in
-fp32 and then cast to the workload dtype.  Comparisons use the cast inputs
+Each workload is a fused linear (or the two-layer MLP chain, or the gated
+dual GEMM) at a fixed shape, dtype, activation and seed.  Inputs are drawn
+with a torch Generator seeded with the workload's seed, in the order X, W,
+bias (MLP: X, W1, b1, W2, b2; gated: X, Wg, bg, Wu, bu): X ~ N(0, 1),
+W ~ N(0, 1/fan_in), bias ~ U(-0.1, 0.1), generated in fp32 and then cast to
+the workload dtype.  Comparisons use the cast inputs
 upcast back to fp32.
 
 Tolerances: fp32 rtol = atol = 1e-4; fp16/bf16 (fp32 accumulate) rtol =
@@ -31,6 +32,7 @@ class Workload:
     act: str | None
     seed: int
     mlp: bool = False  # two-layer chain: Y = act(X W1 + b1) W2 + b2 + X
+    gated: bool = False  # dual GEMM: Y = act(X Wg + bg) * (X Wu + bu)
 
     @property
     def torch_dtype(self) -> torch.dtype:
@@ -39,7 +41,7 @@ class Workload:
     @property
     def flops(self) -> int:
         """Algorithmic GEMM work, 2*M*N*K per GEMM (epilogue excluded)."""
-        return (4 if self.mlp else 2) * self.M * self.N * self.K
+        return (4 if (self.mlp or self.gated) else 2) * self.M * self.N * self.K
 
     @property
     def min_bytes(self) -> int:
@@ -48,6 +50,8 @@ class Workload:
         if self.mlp:
             return e * (2 * self.M * self.K + 2 * self.K * self.N + self.N + self.K
                         + self.M * self.K)
+        if self.gated:
+            return e * (self.M * self.K + 2 * self.K * self.N + 2 * self.N + self.M * self.N)
         return e * (self.M * self.K + self.K * self.N + self.N + self.M * self.N)
 
     @property
@@ -63,6 +67,8 @@ WORKLOADS = {
         Workload("decode_gelu_erf_16x8192x28672_f16", 16, 8192, 28672, "f16", "gelu_erf", 3),
         Workload("mlp_residual_16384x4096x16384_bf16", 16384, 4096, 16384, "bf16", "gelu_tanh", 4,
                  mlp=True),
+        Workload("ffn_gated_silu_8192x4096x14336_bf16", 8192, 4096, 14336, "bf16", "silu", 5,
+                 gated=True),
     ]
 }
 
@@ -94,4 +100,8 @@ def make_inputs(w: Workload, device="cpu", M: int | None = None,
     X = normal(M, K)
     W = normal(K, N, std=1.0 / math.sqrt(K))
     b = uniform(N)
+    if w.gated:
+        Wu = normal(K, N, std=1.0 / math.sqrt(K))
+        bu = uniform(N)
+        return {"X": X, "Wg": W, "bg": b, "Wu": Wu, "bu": bu}
     return {"X": X, "W": W, "bias": b}

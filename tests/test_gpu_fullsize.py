@@ -15,7 +15,7 @@ import torch.nn.functional as F
 
 import oracle
 from deepx_op_gpukernelcompiler_b200 import _native as nat
-from deepx_op_gpukernelcompiler_b200 import fused_linear, mlp_residual
+from deepx_op_gpukernelcompiler_b200 import fused_gated_linear, fused_linear, mlp_residual
 from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS, make_inputs
 
 pytestmark = pytest.mark.gpu
@@ -48,7 +48,7 @@ def _check(got, ref, tol, what):
                                  f"|diff| {err.max().item():.4g}")
 
 
-@pytest.mark.parametrize("name", [n for n, w in WORKLOADS.items() if not w.mlp])
+@pytest.mark.parametrize("name", [n for n, w in WORKLOADS.items() if not (w.mlp or w.gated)])
 def test_fullsize_linear(name):
     w = WORKLOADS[name]
     inp = make_inputs(w)  # CPU, seeded
@@ -78,3 +78,19 @@ def test_fullsize_mlp_chain():
     ref = _fp32_linear(H, W2, b2, None, R=X)
     torch.cuda.synchronize()
     _check(Y, ref, w.tolerance, f"{w.name} vs fp32 chain")
+
+
+def test_fullsize_gated():
+    w = next(w for w in WORKLOADS.values() if w.gated)
+    inp = make_inputs(w)
+    X, Wg, bg, Wu, bu = (inp[k].to(DEV) for k in ("X", "Wg", "bg", "Wu", "bu"))
+    Y = fused_gated_linear(X, Wg, Wu, bg, bu, w.act)
+    plan = nat.last_launch_plan()
+    ref = _fp32_linear(X, Wg, bg, w.act) * _fp32_linear(X, Wu, bu, None)
+    torch.cuda.synchronize()
+    _check(Y, ref, w.tolerance, f"{w.name} [{plan.split()[0]}] vs fp32 expression")
+    r0 = int(np.random.default_rng(w.seed).integers(0, w.M - 8))
+    ref64 = oracle.gated_linear_f64(inp["X"][r0:r0 + 8], inp["Wg"], inp["bg"], inp["Wu"],
+                                    inp["bu"], w.act)
+    _check(Y[r0:r0 + 8].cpu(), torch.from_numpy(ref64).float(), w.tolerance,
+           f"{w.name} rows {r0}:{r0 + 8} vs fp64 oracle")
