@@ -1,7 +1,7 @@
 // dx_collective.cuh — the reduction of a row-parallel linear over ranks.
 //
-// A row-parallel GEMM (the second layer of the MLP chain, with its K
-// dimension sharded over ranks) leaves every rank with a partial Y in its own
+// A row-parallel GEMM (the output projection of the MLP or gated FFN chain,
+// its K dimension sharded over ranks) leaves every rank with a partial Y in its own
 // peer-mapped buffer.  Every rank then runs this kernel on its own slab of
 // rows: it reads the slab from all `world` partial buffers (peer loads over
 // NVLink, 16 B per thread, consecutive threads on consecutive columns), adds

@@ -11,10 +11,12 @@
 //     (one per 128-column half) per K=16 step into two TMEM accumulators of
 //     128 lanes x MN fp32 columns.  Each W row segment read is 512 B long and
 //     each 2 KB X tile serves 32 KB of W.
-//   * split-K with an even partition of the (n-tile, k-block) work units
-//     over all CTAs (one per SM, deep pipeline), so every SM streams the
-//     same number of bytes regardless of N/K; a CTA's range crosses at most
-//     a few n-tiles.
+//   * the (n-tile, k-block) work units are partitioned evenly over the
+//     grid, each CTA taking one contiguous range (deep pipeline, one CTA per
+//     SM).  The host picks the grid: one CTA per whole tile when there are
+//     at least half as many tiles as SMs (no split-K at all), else one CTA
+//     per SM, so that every SM streams the same number of bytes and a CTA's
+//     range crosses at most a few n-tiles (split-K).
 //   * partial sums of a tile that several CTAs share go to a workspace as
 //     fp32; the last CTA to arrive at a tile (atomic counter) sums the
 //     others' partials and its own registers in fixed segment order —
