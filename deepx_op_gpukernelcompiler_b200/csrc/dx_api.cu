@@ -624,16 +624,22 @@ bool decode_eligible(const Problem& p) {
 
 // Skinny-M problems the decode kernel streams faster than the single-CTA
 // tensor-core kernel, measured on B200 (fp16, K = 4096 and 8192, N = 3584 to
-// 28672): every gated problem up to M = 64; plain problems up to M = 16, and
-// up to M = 32 when W has at least half as many 256-column tiles as SMs (one
-// whole tile per CTA).  For plain problems with 32 < M <= 64 the tensor-core
+// 28672): every gated problem up to M = 64; plain problems up to M = 16
+// (except narrow W with 8 < M), and up to M = 32 when W has at least half as
+// many 256-column tiles as SMs (one whole tile per CTA).  For plain problems with 32 < M <= 64 the tensor-core
 // kernel's 128-row tiles stream W faster (M = 64, N = 28672, K = 8192:
 // 82 us against 97 us).
 bool decode_preferred(int64_t M, int64_t N, int sms, bool gated) {
   if (gated) return true;
   const int mn = decode_mn(M);
-  if (mn == 16) return true;
-  if (mn == 32) return 2 * ((N + kDecodeTileN - 1) / kDecodeTileN) >= sms;
+  const int64_t n_tiles = (N + kDecodeTileN - 1) / kDecodeTileN;
+  // 8 < M <= 16 with fewer than 20 tiles (N < 5120): the split-K fix-up of
+  // many segments per tile costs more than the tensor-core kernel's split
+  // tail (M = 16, N = 3584: 25.0 us against 27.0 at K = 8192, 20.9 against
+  // 22.9 at K = 4096).  Below 8 rows the tensor-core kernel's TMA path is
+  // slow, so the decode kernel keeps those.
+  if (mn == 16) return M <= 8 || n_tiles >= 20;
+  if (mn == 32) return 2 * n_tiles >= sms;
   return false;
 }
 

@@ -91,8 +91,8 @@ def test_kvspace_backed_cache_records_versions():
     first = PlanCache(kv)
     first.get(DOC_REQUEST)
     small = json.loads(json.dumps(DOC_REQUEST))
-    small["inputs"][0]["shape"] = [16, 256]
-    small["outputs"][0]["shape"] = [16, 512]
+    small["inputs"][0]["shape"] = [4, 256]
+    small["outputs"][0]["shape"] = [4, 512]
     first.get(small)
     assert first.misses == 2 and first.kv_hits == 0
     recs = first.records("__fusion_0")
