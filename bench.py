@@ -43,6 +43,7 @@ METRIC = "fused GEMM+bias+act TFLOP/s & % bf16 peak at 1/2/4/8 B200; decode HBM 
 DEFAULT_WORKLOAD = "ffn_up_silu_8192x4096x14336_bf16"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 L2_FLUSH_BYTES = 256 << 20
+L2_BYTES = 128 << 20  # B200 L2 (126 MB), rounded up
 DATA = "synthetic: seeded X~N(0,1), W~N(0,1/K), bias~U(-0.1,0.1)"
 
 
@@ -467,7 +468,7 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
     # Rotated weight copies, together at least 3x the L2 size: every step
     # streams W from HBM without an L2 flush (whose dirty lines would be
     # written back during the timed launch).
-    copies = max(2, math.ceil(3 * (128 << 20) / (w.K * n_loc * 2)))
+    copies = max(2, math.ceil(3 * L2_BYTES / (w.K * n_loc * 2)))
     Ws = [(torch.randn(w.K, n_loc, generator=g, device=dev) / math.sqrt(w.K)).to(w.torch_dtype)
           for _ in range(copies)]
     b = (torch.rand(n_loc, generator=g, device=dev) * 0.2 - 0.1).to(w.torch_dtype)
@@ -596,6 +597,63 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
     return out
 
 
+def run_skinny(args) -> None:
+    """The evidence for the skinny-M kernel choice: the decode kernel against
+    the single-CTA tensor-core kernel on decode-shaped problems (fp16, W
+    rotated over copies larger than 3x L2, no flush), plain and gated, one
+    JSON line per (M, K, N) with both times and the variant AUTO picks."""
+    import numpy as np
+    import torch
+
+    from deepx_op_gpukernelcompiler_b200 import _native, fused_gated_linear, fused_linear
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, n):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        return float(np.median(_time_launches(fn, n, lambda: None, stream, 150.0))) * 1e3
+
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    for gated in (False, True):
+        for K in (4096, 8192):
+            for N in (3584, 7168, 14336, 28672):
+                nw = 2 if gated else 1
+                copies = max(2, math.ceil(3 * L2_BYTES / (nw * K * N * 2)))
+                Ws = [(torch.randn(K, N, generator=g, device=dev) / math.sqrt(K)).half()
+                      for _ in range(copies * nw)]
+                b = torch.zeros(N, dtype=torch.float16, device=dev)
+                for M in (1, 8, 16, 32, 64):
+                    X = torch.randn(M, K, generator=g, device=dev).half()
+                    Y = torch.empty(M, N, dtype=torch.float16, device=dev)
+                    res = {}
+                    for kern in ("decode", "umma_1cta", "auto"):
+                        it = [0]
+
+                        def fn(kern=kern):
+                            i = it[0] % copies
+                            it[0] += 1
+                            if gated:
+                                fused_gated_linear(X, Ws[2 * i], Ws[2 * i + 1], b, b, "silu",
+                                                   out=Y, kernel=kern)
+                            else:
+                                fused_linear(X, Ws[i], b, "gelu_erf", out=Y, kernel=kern)
+                        res[kern] = round(timed(fn, max(5, min(args.steps, 12))), 1)
+                        if kern == "auto":
+                            res["auto_kernel"] = _native.last_launch_plan().split()[0]
+                    byts = 2 * (M * K + nw * K * N + nw * N + M * N)
+                    print(json.dumps({"skinny": "gated" if gated else "plain", "M": M, "K": K,
+                                      "N": N, "us": res,
+                                      "auto_GBps": round(byts / res["auto"] / 1e3, 1)}),
+                          flush=True)
+                del Ws
+                torch.cuda.empty_cache()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -609,6 +667,9 @@ def main() -> None:
                     help="run only W warm-up and K timed launches of the workload (for ncu)")
     ap.add_argument("--shard-of", type=int, default=1,
                     help="with --profile: run rank 0's column shard of an N-way split on one GPU")
+    ap.add_argument("--skinny", action="store_true",
+                    help="time the decode and single-CTA tensor-core kernels on decode shapes "
+                         "(the evidence for AUTO's skinny-M choice), one JSON line per shape")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -618,6 +679,8 @@ def main() -> None:
               file=sys.stderr)
     if args.impl == "reference":
         run_reference(args)
+    elif args.skinny:
+        run_skinny(args)
     else:
         run_gpu(args)
 

@@ -624,15 +624,18 @@ bool decode_eligible(const Problem& p) {
 
 // Skinny-M problems the decode kernel streams faster than the single-CTA
 // tensor-core kernel, measured on B200 (fp16, K = 4096 and 8192, N = 3584 to
-// 28672): every gated problem up to M = 64; plain problems up to M = 16
-// (except narrow W with 8 < M), and up to M = 32 when W has at least half as
-// many 256-column tiles as SMs (one whole tile per CTA).  For plain problems with 32 < M <= 64 the tensor-core
+// 28672; `bench.py --skinny`): gated problems up to M = 32, and up to M = 64
+// for narrow W; plain problems up to M = 16 (except narrow W with 8 < M), and
+// up to M = 32 when W has at least half as many 256-column tiles as SMs (one
+// whole tile per CTA).  For plain problems with 32 < M <= 64 the tensor-core
 // kernel's 128-row tiles stream W faster (M = 64, N = 28672, K = 8192:
 // 82 us against 97 us).
 bool decode_preferred(int64_t M, int64_t N, int sms, bool gated) {
-  if (gated) return true;
   const int mn = decode_mn(M);
   const int64_t n_tiles = (N + kDecodeTileN - 1) / kDecodeTileN;
+  // Gated, 32 < M <= 64 and N >= 5120: the tensor-core kernel streams both
+  // weights faster (K = 4096, N = 28672: 89 us against 99).
+  if (gated) return mn <= 32 || n_tiles < 20;
   // 8 < M <= 16 with fewer than 20 tiles (N < 5120): the split-K fix-up of
   // many segments per tile costs more than the tensor-core kernel's split
   // tail (M = 16, N = 3584: 25.0 us against 27.0 at K = 8192, 20.9 against
@@ -811,7 +814,8 @@ size_t dx_fused_gated_linear_workspace_size(int64_t M, int64_t N, int64_t K, int
   if (cudaGetDevice(&dev) != cudaSuccess || device_sms(dev, &sms) != DX_OK) return 0;
   const int tn = decode_tile_n(M, true);
   const bool fits = M <= kDecodeMaxM && (N + tn - 1) / tn <= kDecodeMaxTiles;
-  if (kernel == DX_KERNEL_AUTO) kernel = fits ? DX_KERNEL_DECODE : DX_KERNEL_UMMA;
+  if (kernel == DX_KERNEL_AUTO)
+    kernel = (fits && decode_preferred(M, N, sms, true)) ? DX_KERNEL_DECODE : DX_KERNEL_UMMA;
   if (kernel == DX_KERNEL_DECODE && fits) return decode_plan(M, N, K, sms, true).bytes;
   return 0;  // the gated tensor-core kernels take no split tail
 }
