@@ -448,7 +448,7 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
     """The other workloads of the metric: decode HBM GB/s, the square GEMM and
     the MLP chain (all ranks take part; timings are max over ranks)."""
     import torch
-    from deepx_op_gpukernelcompiler_b200 import fused_linear
+    from deepx_op_gpukernelcompiler_b200 import _native, fused_linear
     from deepx_op_gpukernelcompiler_b200.shard import ParallelMLP, shard_bounds
     from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS
 
@@ -482,13 +482,14 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
     for _ in range(5):
         dec()
     torch.cuda.synchronize()
+    dec_plan = _native.last_launch_plan()
     _barrier(world)
     t = _time_launches(dec, steps, lambda: None, stream)
     ms = _max_over_ranks(sum(t), world, dev) / steps
     bytes_rank = 2 * (w.M * w.K + w.K * n_loc + n_loc + w.M * n_loc)
     bytes_total = w.min_bytes
     out[w.name] = {"value": round(bytes_total / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
-                   "ms": round(ms, 4), "kernel": "decode",
+                   "ms": round(ms, 4), "kernel": dec_plan,
                    "roofline": {"bound": "hbm", "achieved": round(bytes_rank / (sum(t) / steps * 1e-3) / 1e9, 1),
                                 "peak": hbm, "unit": "GB/s",
                                 "frac": round(bytes_rank / (sum(t) / steps * 1e-3) / 1e9 / hbm, 4)},
@@ -511,12 +512,13 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
     for _ in range(5):
         sq()
     torch.cuda.synchronize()
+    sq_plan = _native.last_launch_plan()
     _barrier(world)
     t = _time_launches(sq, steps, flush, stream)
     ms = _max_over_ranks(sum(t), world, dev) / steps
     tf = w.flops / (ms * 1e-3) / 1e12
     out[w.name] = {"value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
-                   "frac_of_peak": round(tf / world / tflops_peak, 4), "kernel": "umma"}
+                   "frac_of_peak": round(tf / world / tflops_peak, 4), "kernel": sq_plan}
     del X, Wt, b, Y
 
     # Gated FFN's gate/up projections in one dual-GEMM launch:
