@@ -121,3 +121,32 @@ def test_kvspace_record_collision_is_rejected():
     kv.set(record_key(req), json.dumps({"request": bogus}))
     with pytest.raises(CompileError, match="collision"):
         PlanCache(kv).get(DOC_REQUEST)
+
+
+def test_plan_cache_is_thread_safe():
+    """Concurrent lookups of the same and different requests build each plan
+    once and hand every thread the same object."""
+    import threading
+    _build.build()
+    cache = PlanCache()
+    reqs = []
+    for m in (16, 64, 256, 512):
+        r = json.loads(json.dumps(DOC_REQUEST))
+        r["inputs"][0]["shape"] = [m, 256]
+        r["outputs"][0]["shape"] = [m, 512]
+        reqs.append(r)
+    got = [[None] * 32 for _ in reqs]
+
+    def worker(t):
+        for i, r in enumerate(reqs):
+            got[i][t] = cache.get(r)
+
+    threads = [threading.Thread(target=worker, args=(t,)) for t in range(32)]
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    assert len(cache) == len(reqs) and cache.misses == len(reqs)
+    assert cache.hits == 32 * len(reqs) - len(reqs)
+    for row in got:
+        assert all(p is row[0] for p in row)
