@@ -180,3 +180,17 @@ def test_two_layer_ffn_chain():
     ref = oracle.fused_linear_f64(oracle.fused_linear_f64(X, W1, b1, "relu"), W2, b2, None)
     Y = two_layer_ffn(*(t.to(DEV) for t in (X, W1, b1, W2, b2)), "relu")
     _assert_close(Y, ref, torch.bfloat16, "ffn_two_layer")
+
+
+def test_gated_k_zero_is_act_of_bias_times_bias():
+    """K = 0: X Wg and X Wu are zero, so Y = act(bg) * bu (the SIMT path)."""
+    M, N = 5, 40
+    bg = (torch.rand(N) * 0.2 - 0.1).bfloat16()
+    bu = (torch.rand(N) * 0.2 - 0.1).bfloat16()
+    X = torch.empty(M, 0, dtype=torch.bfloat16, device=DEV)
+    W = torch.empty(0, N, dtype=torch.bfloat16, device=DEV)
+    Y = fused_gated_linear(X, W, W, bg.to(DEV), bu.to(DEV), "silu")
+    torch.cuda.synchronize()
+    assert nat.last_launch_plan().startswith("simt_gated")
+    ref = oracle.activation_f64(bg.double().numpy(), "silu") * bu.double().numpy()
+    _assert_close(Y, np.broadcast_to(ref, (M, N)), torch.bfloat16, "K=0")
