@@ -21,7 +21,9 @@
 //     fp32; the last CTA to arrive at a tile (atomic counter) sums the
 //     others' partials and its own registers in fixed segment order —
 //     deterministic, no float atomics — applies bias, activation and
-//     residual, stores Y, and resets the counter to 0.
+//     residual, stores Y, and resets the counter to 0.  When that tile is
+//     the CTA's last work item the partials come in by bulk copies into the
+//     then idle W stage ring, all in flight at once.
 //   * gated form (p.gated): Y = act(X Wg + bg) * (X Wu + bu).  A work unit
 //     covers NH/2 x 128 output columns: its first NH/2 UMMA halves read Wg's
 //     columns, the others Wu's same columns; the epilogue combines them.
@@ -46,7 +48,7 @@ struct DecodeParams {
   const void* bias;     // N elements or nullptr
   const void* residual; // [M, N] (ldr) or nullptr
   void* Y;
-  float* partials;      // [n_tiles][max_seg][MN][256] fp32
+  float* partials;      // [n_tiles][max_seg][4][NH][MN][32] fp32 (DecodeShape::QBLK)
   int* tickets;         // [n_tiles][4] (per warp quarter): arrivals | written << 16;
                         // zero between calls
   int act;
@@ -91,13 +93,22 @@ struct DecodeShape {
   static constexpr int BAR_TFULL = 2 * STAGES;
   static constexpr int BAR_TEMPTY = 2 * STAGES + 2;
   static constexpr int BAR_DRAIN = 2 * STAGES + 4;
-  static constexpr int NUM_BARS = BAR_DRAIN + 1;
+  static constexpr int BAR_FIX = 2 * STAGES + 5;  // one per epilogue warp quarter
+  static constexpr int NUM_BARS = BAR_FIX + 4;
+  // Split-K partial sums, per tile: [segment][warp quarter][NH][MN][32 lanes]
+  // fp32, so one warp quarter's share of a segment is one contiguous block.
+  static constexpr int QBLK = NH * MN * 32;
+  // Fix-up staging: once a CTA's last accumulator is ready its W stage ring
+  // is idle, and each epilogue warp takes a quarter of it for the other
+  // segments' blocks (FIX_CAP blocks per batch of bulk copies).
+  static constexpr int FIX_CAP = STAGES * W_BYTES / (4 * QBLK * 4);
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // tmem base, abort flag
   static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 16;
   static_assert(MN == 16 || MN == 32 || MN == 64, "decode batch tile");
   static_assert(NH == 2 || (NH == 4 && MN == 16), "halves per unit");
   static_assert(X_BYTES % 1024 == 0, "X stage alignment");
   static_assert(SMEM_BYTES <= 227 * 1024, "shared memory budget");
+  static_assert(FIX_CAP >= 1 && (QBLK * 4) % 16 == 0, "fix-up staging");
 };
 
 // CTA whose work range holds unit u (ranges are [g*U/G, (g+1)*U/G)).
@@ -165,6 +176,7 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
       mbar_init(bar(S::BAR_TEMPTY + b), 4);
     }
     mbar_init(bar(S::BAR_DRAIN), 1);
+    for (int w = 0; w < 4; ++w) mbar_init(bar(S::BAR_FIX + w), 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -356,15 +368,17 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
         // Tile shared with other CTAs.  One counter word per (tile, warp
         // quarter): arrivals in the low 16 bits, partials written in the high
         // 16 bits.  Each CTA arrives first; the last to arrive keeps its sums
-        // in registers, every other one publishes its partial ([MN][256] fp32,
-        // lanes contiguous in n) and then counts it written.  Each warp
-        // finishes its own 2 x 32 columns, so no cross-warp barrier can be
-        // left waiting on an exit.
+        // in registers, every other one publishes its partial (this warp's
+        // [NH][MN][32] block of the segment, lanes contiguous in n) and then
+        // counts it written.  Each warp finishes its own NH x 32 columns, so
+        // no cross-warp barrier can be left waiting on an exit.
         const int first = decode_cta_of(static_cast<long long>(t) * p.kbt, U, p.grid);
         const int last = decode_cta_of(static_cast<long long>(t + 1) * p.kbt - 1, U, p.grid);
         const int nseg = last - first + 1;
         const int own = g - first;
         float* const part_t = p.partials + static_cast<size_t>(t) * p.max_seg * MN * S::NT;
+        // Offset of (half h, row m) in this warp's block of a segment.
+        auto pidx = [q, lane](int h, int m) { return (q * NH + h) * (MN * 32) + m * 32 + lane; };
         int* const ctr = p.tickets + t * 4 + q;
         int old = 0;
         if (lane == 0) old = atomicAdd(ctr, 1);
@@ -376,7 +390,8 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
           for (int h = 0; h < NH; ++h)
 #pragma unroll
             for (int m = 0; m < MN; ++m)
-              if (m < M) mine[m * S::NT + h * 128 + n_local] = acc[h][m];
+              if (m < M) mine[pidx(h, m)] = acc[h][m];
+          fence_proxy_async_global();  // the last CTA may read it with bulk copies
           __threadfence();
           __syncwarp();
           if (lane == 0) atomicAdd(ctr, 1 << 16);
@@ -406,7 +421,7 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
           for (int h = 0; h < NH; ++h)
 #pragma unroll
             for (int m = 0; m < MN; ++m) {
-              if (m < M) mine[m * S::NT + h * 128 + n_local] = acc[h][m];
+              if (m < M) mine[pidx(h, m)] = acc[h][m];
               acc[h][m] = 0.0f;
             }
           for (int sg = 0; sg < nseg; ++sg) {
@@ -416,11 +431,77 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
               float fv[MN];
 #pragma unroll
               for (int m = 0; m < MN; ++m)
-                fv[m] = m < M ? __ldcg(src + m * S::NT + h * 128 + n_local) : 0.0f;
+                fv[m] = m < M ? __ldcg(src + pidx(h, m)) : 0.0f;
 #pragma unroll
               for (int m = 0; m < MN; ++m) acc[h][m] += fv[m];
             }
           }
+        } else if (u == u_end) {
+          // The CTA's last item: every MMA that read its W stage ring has
+          // completed, so this warp's quarter of the ring stages the other
+          // segments' blocks (first M rows of each half), FIX_CAP segments per
+          // batch of bulk copies: one L2 round trip per batch.  The sum order
+          // is the register path's, so the bits do not depend on the path.
+          const int n_other = nseg - 1;
+          const uint32_t sbuf = sW + static_cast<uint32_t>(q * S::FIX_CAP * S::QBLK * 4);
+          const float* const lbuf =
+              reinterpret_cast<const float*>(base_ptr + S::OFF_W) + q * S::FIX_CAP * S::QBLK;
+          const uint32_t fbar = bar(S::BAR_FIX + q);
+          const uint32_t rows_bytes = static_cast<uint32_t>(M) * 32u * 4u;
+          float sum[NH][MN];
+#pragma unroll
+          for (int h = 0; h < NH; ++h)
+#pragma unroll
+            for (int m = 0; m < MN; ++m) sum[h][m] = 0.0f;
+          uint32_t fph = 0;
+          bool fok = true;
+          fence_proxy_async_global();
+          for (int o0 = 0; o0 < n_other; o0 += S::FIX_CAP) {
+            const int nb = n_other - o0 < S::FIX_CAP ? n_other - o0 : S::FIX_CAP;
+            if (lane == 0) mbar_arrive_expect_tx(fbar, static_cast<uint32_t>(nb * NH) * rows_bytes);
+            __syncwarp();
+            for (int j = lane; j < nb * NH; j += 32) {
+              const int i = j / NH, h = j - (j / NH) * NH;
+              const int o = o0 + i;
+              const int sg = o < own ? o : o + 1;
+              bulk_load_g2s(sbuf + static_cast<uint32_t>((i * S::QBLK + h * MN * 32) * 4),
+                            part_t + static_cast<size_t>(sg) * MN * S::NT + (q * NH + h) * (MN * 32),
+                            rows_bytes, fbar);
+            }
+            if (!__all_sync(0xffffffffu, mbar_wait(fbar, fph, abort_flag))) {
+              if (lane == 0) mbar_wait_drain(fbar, fph);  // copies in flight land first
+              fok = false;
+              break;
+            }
+            for (int i = 0; i < nb; ++i) {
+              if (o0 + i == own) {  // segment `own` precedes this one (segment own + 1)
+#pragma unroll
+                for (int h = 0; h < NH; ++h)
+#pragma unroll
+                  for (int m = 0; m < MN; ++m) sum[h][m] += acc[h][m];
+              }
+#pragma unroll
+              for (int h = 0; h < NH; ++h)
+#pragma unroll
+                for (int m = 0; m < MN; ++m)
+                  if (m < M) sum[h][m] += lbuf[i * S::QBLK + (h * MN + m) * 32 + lane];
+            }
+            // All lanes have read the batch before the next one overwrites it.
+            __syncwarp();
+            fence_proxy_async_smem();
+            fph ^= 1u;
+          }
+          if (!fok) break;
+          if (own == n_other) {  // this CTA's segment is the tile's last
+#pragma unroll
+            for (int h = 0; h < NH; ++h)
+#pragma unroll
+              for (int m = 0; m < MN; ++m) sum[h][m] += acc[h][m];
+          }
+#pragma unroll
+          for (int h = 0; h < NH; ++h)
+#pragma unroll
+            for (int m = 0; m < MN; ++m) acc[h][m] = sum[h][m];
         } else {
           // This CTA's segment comes from registers.  The loads of SB other
           // segments are issued before any of them is added, so a tile split
@@ -448,7 +529,7 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
 #pragma unroll
                   for (int m = 0; m < MN; ++m)
                     f[sb][hh][m] = (o < n_other && m < M)
-                                       ? __ldcg(src + m * S::NT + (h0 + hh) * 128 + n_local)
+                                       ? __ldcg(src + pidx(h0 + hh, m))
                                        : 0.0f;
               }
 #pragma unroll

@@ -229,6 +229,26 @@ def test_decode_tickets_reset_across_shapes():
     _status_clean()
 
 
+
+@pytest.mark.parametrize("M,K,N", [(16, 8192, 3584), (3, 4096, 1024), (16, 2048, 512)])
+def test_decode_fixup_bitwise_across_repeats(M, K, N):
+    """The last CTA to reach a split tile sums the partials either from bulk
+    copies staged in shared memory (when the tile is its last work item, in
+    batches when the tile has many segments) or from registers.  Both add in
+    the same fixed segment order, so repeats whose arrival order differs
+    agree to the last bit (M = 3: only the first rows are staged)."""
+    X, W, b, _ = _rand(M, K, N, torch.float16, seed=M + N)
+    Xd, Wd, bd = X.to(DEV), W.to(DEV), b.to(DEV)
+    Y0 = fused_linear(Xd, Wd, bd, "gelu_erf", kernel="decode")
+    assert "grid=" in nat.last_launch_plan()
+    for rep in range(6):
+        Y = fused_linear(Xd, Wd, bd, "gelu_erf", kernel="decode")
+        assert torch.equal(Y, Y0), f"repeat {rep} differs"
+    torch.cuda.synchronize()
+    _assert_close(Y0, oracle.fused_linear_f64(X, W, b, "gelu_erf"), torch.float16,
+                  f"decode {M}x{K}x{N}")
+    _status_clean()
+
 def test_nonzero_stream():
     s = torch.cuda.Stream()
     X, W, b, _ = _rand(256, 512, 512, torch.bfloat16, seed=2)
