@@ -564,29 +564,48 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
         if (lane == 0) *ctr = 0;  // every CTA of the tile has arrived and written
         if (tr) decode_trace(p, 8);
       }
-      if (p.gated) {
+      // Rows in groups of 4: the activation runs over a group's values at
+      // once (act_apply_all), so their math chains overlap.
 #pragma unroll
-        for (int hp = 0; hp < NH / 2; ++hp) {
-          const int n = t * (S::NT / 2) + hp * 128 + n_local;
-          if (n < p.N) {
+      for (int m0 = 0; m0 < MN; m0 += 4) {
+        if (m0 >= M) continue;
+        if (p.gated) {
+          float gv[NH / 2 * 4];
 #pragma unroll
-            for (int m = 0; m < MN; ++m)
-              if (m < M)
-                Y[m * p.ldy + n] = Tr::from_float(act_apply(acc[hp][m] + bv[hp], p.act) *
-                                                  (acc[hp + NH / 2][m] + bv[hp + NH / 2]));
+          for (int hp = 0; hp < NH / 2; ++hp)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) gv[hp * 4 + i] = acc[hp][m0 + i] + bv[hp];
+          act_apply_all(gv, p.act);
+#pragma unroll
+          for (int hp = 0; hp < NH / 2; ++hp) {
+            const int n = t * (S::NT / 2) + hp * 128 + n_local;
+            if (n < p.N) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i)
+                if (m0 + i < M)
+                  Y[(m0 + i) * p.ldy + n] = Tr::from_float(
+                      gv[hp * 4 + i] * (acc[hp + NH / 2][m0 + i] + bv[hp + NH / 2]));
+            }
           }
-        }
-      } else {
+        } else {
+          float yv[NH * 4];
 #pragma unroll
-        for (int h = 0; h < NH; ++h) {
-          const int n = t * S::NT + h * 128 + n_local;
-          if (n < p.N) {
+          for (int h = 0; h < NH; ++h)
 #pragma unroll
-            for (int m = 0; m < MN; ++m) {
-              if (m < M) {
-                float y = act_apply(fmaf(p.alpha, acc[h][m], bv[h]), p.act);
-                if (res != nullptr) y += Tr::to_float(res[m * p.ldr + n]);
-                Y[m * p.ldy + n] = Tr::from_float(y);
+            for (int i = 0; i < 4; ++i) yv[h * 4 + i] = fmaf(p.alpha, acc[h][m0 + i], bv[h]);
+          act_apply_all(yv, p.act);
+#pragma unroll
+          for (int h = 0; h < NH; ++h) {
+            const int n = t * S::NT + h * 128 + n_local;
+            if (n < p.N) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int m = m0 + i;
+                if (m < M) {
+                  float y = yv[h * 4 + i];
+                  if (res != nullptr) y += Tr::to_float(res[m * p.ldr + n]);
+                  Y[m * p.ldy + n] = Tr::from_float(y);
+                }
               }
             }
           }

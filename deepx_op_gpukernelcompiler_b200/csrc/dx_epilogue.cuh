@@ -55,6 +55,27 @@ __device__ __forceinline__ float act_apply(float x, int act) {
   }
 }
 
+template <int A, bool kFast, int N>
+__device__ __forceinline__ void act_loop(float (&v)[N]) {
+#pragma unroll
+  for (int j = 0; j < N; ++j) v[j] = act_apply<kFast>(v[j], A);
+}
+
+// The activation over a register array, the switch outside the element
+// loop: each case is straight-line code whose independent per-element
+// chains (erff, tanh) the compiler interleaves, instead of one branch per
+// element.
+template <bool kFast = true, int N>
+__device__ __forceinline__ void act_apply_all(float (&v)[N], int act) {
+  switch (act) {
+    case kActRelu: act_loop<kActRelu, kFast>(v); break;
+    case kActGeluTanh: act_loop<kActGeluTanh, kFast>(v); break;
+    case kActGeluErf: act_loop<kActGeluErf, kFast>(v); break;
+    case kActSilu: act_loop<kActSilu, kFast>(v); break;
+    default: break;
+  }
+}
+
 template <typename T>
 struct ElemTraits;
 

@@ -208,10 +208,7 @@ __device__ __forceinline__ bool epi_chunk_end(const EpilogueCtx<T>& c, float (&v
       }
     }
   }
-  if (c.act != kActNone) {
-#pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = act_apply(v[j], c.act);
-  }
+  act_apply_all(v, c.act);
   if (c.has_residual) {
     const uint32_t rbar = c.rbar0 + 8u * buf;
     const uint32_t par = (it / kEpiBufs) & 1u;
@@ -378,8 +375,9 @@ __device__ __forceinline__ bool epilogue_tile_gated(const EpilogueCtx<T>& c, uin
         }
       }
     }
+    act_apply_all(g, act);
 #pragma unroll
-    for (int j = 0; j < 32; ++j) g[j] = act_apply(g[j], act) * u[j];
+    for (int j = 0; j < 32; ++j) g[j] *= u[j];
     if (!epi_chunk_end(c, g, n_c, row_base, lane, it, abort_flag, make_uint4(0u, 0u, 0u, 0u), ch)) {
       if (ch + 1 < n_chunks) tmem_wait_ld();
       return false;
