@@ -623,13 +623,13 @@ def run_skinny(args) -> None:
     g.manual_seed(11)
     for gated in (False, True):
         for K in (4096, 8192):
-            for N in (3584, 7168, 14336, 28672):
+            for N in (1792, 3584, 7168, 14336, 28672):
                 nw = 2 if gated else 1
                 copies = max(2, math.ceil(3 * L2_BYTES / (nw * K * N * 2)))
                 Ws = [(torch.randn(K, N, generator=g, device=dev) / math.sqrt(K)).half()
                       for _ in range(copies * nw)]
                 b = torch.zeros(N, dtype=torch.float16, device=dev)
-                for M in (1, 8, 16, 32, 64):
+                for M in (1, 4, 8, 12, 16, 32, 64):
                     X = torch.randn(M, K, generator=g, device=dev).half()
                     Y = torch.empty(M, N, dtype=torch.float16, device=dev)
                     res = {}

@@ -187,16 +187,33 @@ struct DecodePlan {
 
 // Halves per work unit: 2; the gated form with M <= 16 uses 4 (256 columns
 // of each weight, so both weights are read in 512-byte row segments).
-int decode_halves(int64_t M, bool gated) { return gated && decode_mn(M) == 16 ? 4 : 2; }
+// Whether a decode plan over tiles `tile_n` columns wide streams one whole
+// tile per CTA (at least half as many tiles as SMs, at most one per SM).
+bool decode_whole_tiles(int64_t N, int64_t tile_n, int sms) {
+  const int64_t t = (N + tile_n - 1) / tile_n;
+  return 2 * t >= sms && t <= sms;
+}
+
+// Halves per work unit: 2, or 4 for the gated form with M <= 16 (256 columns
+// of each weight, 512-byte row segments) unless 128-column units give whole
+// tiles and 256-column units do not (gated M = 16, K = 8192, N = 14336: 112
+// whole tiles in 76 us against 56 split tiles in 84 us).
+int decode_halves(int64_t M, int64_t N, int sms, bool gated) {
+  if (!gated || decode_mn(M) != 16) return 2;
+  return decode_whole_tiles(N, 128, sms) && !decode_whole_tiles(N, 256, sms) ? 2 : 4;
+}
 
 // Output columns per work unit: 256 (plain), 64 x halves (gated).
-int decode_tile_n(int64_t M, bool gated) { return gated ? 64 * decode_halves(M, true) : kDecodeTileN; }
+int decode_tile_n(int nh, bool gated) { return gated ? 64 * nh : kDecodeTileN; }
+
+// Narrowest output tile of either halves choice: bounds the tile count.
+int decode_min_tile_n(bool gated) { return gated ? 128 : kDecodeTileN; }
 
 DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sms, bool gated = false) {
   DecodePlan d;
   d.mn = decode_mn(M);
-  d.nh = decode_halves(M, gated);
-  const int tile_n = decode_tile_n(M, gated);
+  d.nh = decode_halves(M, N, sms, gated);
+  const int tile_n = decode_tile_n(d.nh, gated);
   d.n_tiles = static_cast<int>((N + tile_n - 1) / tile_n);
   d.kbt = static_cast<int>((K + 63) / 64);
   d.units = static_cast<long long>(d.n_tiles) * d.kbt;
@@ -616,39 +633,41 @@ bool umma_eligible(const Problem& p) {
 
 bool decode_eligible(const Problem& p) {
   if (p.dtype == DX_DTYPE_F32 || p.K == 0 || p.M > kDecodeMaxM) return false;
-  const int tn = decode_tile_n(p.M, p.gated);
+  const int tn = decode_min_tile_n(p.gated);
   if ((p.N + tn - 1) / tn > kDecodeMaxTiles) return false;
   if (p.gated && !tma_ok(p.W2, p.ldw2)) return false;
   return tma_ok(p.X, p.ldx) && tma_ok(p.W, p.ldw);
 }
 
 // Skinny-M problems the decode kernel streams faster than the single-CTA
-// tensor-core kernel, measured on B200 (fp16, K = 4096 and 8192, N = 3584 to
-// 28672; `bench.py --skinny`): gated problems up to M = 32, and up to M = 64
-// for narrow W; plain problems up to M = 16 (except narrow W with 8 < M), and
-// up to M = 32 when W has at least half as many 256-column tiles as SMs (one
-// whole tile per CTA).  For plain problems with 32 < M <= 64 the tensor-core
-// kernel's 128-row tiles stream W faster (M = 64, N = 28672, K = 8192:
-// 82 us against 97 us).
-bool decode_preferred(int64_t M, int64_t N, int sms, bool gated) {
+// tensor-core kernel, measured on B200 (fp16, K = 4096 and 8192, N = 1792 to
+// 28672, M = 1 to 64; `bench.py --skinny`):
+//   * gated: up to M = 32; 32 < M <= 64 with narrow W (fewer than 20
+//     256-column tiles) or K >= 8192 (K = 8192, N = 7168, M = 64: 58 us
+//     against 64).  With K = 4096 and wide W the tensor-core kernel streams
+//     both weights faster (N = 7168: 37 us against 41).
+//   * plain, M < 16: always (below 8 rows the tensor-core kernel's TMA path is
+//     slow, and rows that fill part of an 8-row group cost it too: M = 12,
+//     K = 4096, N = 3584: 21 us against 31).
+//   * plain, M = 16: with at least 20 tiles, or with K * N >= 2^23; only the
+//     smallest W goes to the tensor-core kernel (K = 4096, N = 1792: 19 us
+//     against 23, where the decode kernel's split-K fix-up dominates).
+//   * plain, 16 < M <= 32: when W has at least half as many 256-column tiles
+//     as SMs (one whole tile per CTA).
+// For plain problems with 32 < M <= 64 the tensor-core kernel's 128-row tiles
+// stream W faster (M = 64, N = 28672, K = 8192: 84 us against 91).
+bool decode_preferred(int64_t M, int64_t N, int64_t K, int sms, bool gated) {
   const int mn = decode_mn(M);
   const int64_t n_tiles = (N + kDecodeTileN - 1) / kDecodeTileN;
-  // Gated, 32 < M <= 64 and N >= 5120: the tensor-core kernel streams both
-  // weights faster (K = 4096, N = 28672: 89 us against 99).
-  if (gated) return mn <= 32 || n_tiles < 20;
-  // 8 < M <= 16 with fewer than 20 tiles (N < 5120): the split-K fix-up of
-  // many segments per tile costs more than the tensor-core kernel's split
-  // tail (M = 16, N = 3584: 25.0 us against 27.0 at K = 8192, 20.9 against
-  // 22.9 at K = 4096).  Below 8 rows the tensor-core kernel's TMA path is
-  // slow, so the decode kernel keeps those.
-  if (mn == 16) return M <= 8 || n_tiles >= 20;
+  if (gated) return mn <= 32 || n_tiles < 20 || K >= 8192;
+  if (mn == 16) return M < 16 || n_tiles >= 20 || K * N >= (int64_t(1) << 23);
   if (mn == 32) return 2 * n_tiles >= sms;
   return false;
 }
 
 int select_variant(const Problem& p, int sms, bool ws_known) {
   if (p.dtype == DX_DTYPE_F32 || p.K == 0) return DX_KERNEL_SIMT;
-  if (decode_eligible(p) && (decode_preferred(p.M, p.N, sms, p.gated) || !umma_eligible(p))) {
+  if (decode_eligible(p) && (decode_preferred(p.M, p.N, p.K, sms, p.gated) || !umma_eligible(p))) {
     if (!ws_known) return DX_KERNEL_DECODE;
     const DecodePlan d = decode_plan(p.M, p.N, p.K, sms, p.gated);
     if (d.bytes == 0 || (p.ws != nullptr && p.ws_bytes >= d.bytes && aligned16(p.ws)))
@@ -812,10 +831,10 @@ size_t dx_fused_gated_linear_workspace_size(int64_t M, int64_t N, int64_t K, int
   if (M <= 0 || N <= 0 || K <= 0 || dtype == DX_DTYPE_F32 || kernel == DX_KERNEL_SIMT) return 0;
   int dev = 0, sms = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || device_sms(dev, &sms) != DX_OK) return 0;
-  const int tn = decode_tile_n(M, true);
+  const int tn = decode_min_tile_n(true);
   const bool fits = M <= kDecodeMaxM && (N + tn - 1) / tn <= kDecodeMaxTiles;
   if (kernel == DX_KERNEL_AUTO)
-    kernel = (fits && decode_preferred(M, N, sms, true)) ? DX_KERNEL_DECODE : DX_KERNEL_UMMA;
+    kernel = (fits && decode_preferred(M, N, K, sms, true)) ? DX_KERNEL_DECODE : DX_KERNEL_UMMA;
   if (kernel == DX_KERNEL_DECODE && fits) return decode_plan(M, N, K, sms, true).bytes;
   return 0;  // the gated tensor-core kernels take no split tail
 }
@@ -843,7 +862,7 @@ int dx_select_kernel(int64_t M, int64_t N, int64_t K, int dtype) {
     t_last_error.clear();  // no device: not an error of this query
   }
   if (M <= kDecodeMaxM && (N + kDecodeTileN - 1) / kDecodeTileN <= kDecodeMaxTiles &&
-      decode_preferred(M, N, sms, false))
+      decode_preferred(M, N, K, sms, false))
     return DX_KERNEL_DECODE;
   return DX_KERNEL_UMMA;
 }

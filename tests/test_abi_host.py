@@ -131,8 +131,11 @@ def test_kernel_selection(lib):
     assert lib.dx_select_kernel(256, 512, 512, nat.DX_DTYPE_F32) == nat.DX_KERNEL_SIMT
     assert lib.dx_select_kernel(16, 28672, 8192, nat.DX_DTYPE_F16) == nat.DX_KERNEL_DECODE
     assert lib.dx_select_kernel(1, 3584, 8192, nat.DX_DTYPE_F16) == nat.DX_KERNEL_DECODE
-    # 8 < M <= 16 with fewer than 20 tiles: the tensor-core kernel's split tail
-    assert lib.dx_select_kernel(16, 3584, 8192, nat.DX_DTYPE_F16) == nat.DX_KERNEL_UMMA
+    # M = 16 with fewer than 20 tiles: the tensor-core kernel only for the
+    # smallest W (K * N < 2^23); M < 16 always streams through the decode kernel
+    assert lib.dx_select_kernel(16, 1792, 4096, nat.DX_DTYPE_F16) == nat.DX_KERNEL_UMMA
+    assert lib.dx_select_kernel(12, 1792, 4096, nat.DX_DTYPE_F16) == nat.DX_KERNEL_DECODE
+    assert lib.dx_select_kernel(16, 3584, 8192, nat.DX_DTYPE_F16) == nat.DX_KERNEL_DECODE
     assert lib.dx_select_kernel(16, 7168, 8192, nat.DX_DTYPE_F16) == nat.DX_KERNEL_DECODE
     # 16 < M <= 32: decode only when W has >= SMs/2 tiles of 256 columns
     assert lib.dx_select_kernel(32, 28672, 8192, nat.DX_DTYPE_F16) == nat.DX_KERNEL_DECODE

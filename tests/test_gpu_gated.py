@@ -102,6 +102,25 @@ def test_gated_shapes_all_variants(M, K, N, dtype):
         _assert_close(Y, ref, dtype, f"{M}x{K}x{N} {dtype} [{kern}]")
 
 
+
+@pytest.mark.parametrize("M,N,halves", [(16, 14336, 2), (3, 14336, 2), (16, 28672, 4), (8, 3584, 4)])
+def test_gated_decode_unit_width(M, N, halves):
+    """Gated M <= 16 streams 256 columns of each weight per work unit (4 UMMA
+    halves), except when 128-column units give one whole tile per CTA and
+    256-column units do not (N = 14336 on 148 SMs: 112 whole tiles against 56
+    split ones); both widths match the oracle."""
+    K = 512
+    X, Wg, bg, Wu, bu = _rand(M, K, N, torch.float16, seed=M + N)
+    ref = oracle.gated_linear_f64(X, Wg, bg, Wu, bu, "silu")
+    d = [t.to(DEV) for t in (X, Wg, bg, Wu, bu)]
+    Y = fused_gated_linear(d[0], d[1], d[3], d[2], d[4], "silu", kernel="decode")
+    torch.cuda.synchronize()
+    plan = nat.last_launch_plan()
+    assert plan.startswith("decode_gated"), plan
+    if torch.cuda.get_device_properties(DEV).multi_processor_count == 148:
+        assert f"halves={halves} " in plan, plan
+    _assert_close(Y, ref, torch.float16, f"{M}x{K}x{N} gated decode")
+
 @pytest.mark.parametrize("act", ["gelu", "relu", None])
 def test_gated_other_activations_no_bias(act):
     M, K, N = 200, 384, 520
