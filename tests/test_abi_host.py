@@ -121,6 +121,26 @@ def test_host_entry_rejects_device_or_mismatched_tensors():
                           torch.zeros(3, dtype=torch.bfloat16))
 
 
+
+def test_host_entry_load_order():
+    """The host-buffer entry copies X's row blocks and W's column blocks in an
+    expanding square (the next row block while the loaded columns are at
+    least as wide as the loaded rows are tall), each block exactly once."""
+    from deepx_op_gpukernelcompiler_b200.linear import _block_bounds, _load_order
+    rows, cols = _block_bounds(8192, 8, 256), _block_bounds(14336, 8, 256)
+    order = _load_order(rows, cols)
+    assert order[:4] == [("r", 0), ("c", 0), ("r", 1), ("c", 1)]
+    assert sorted(i for k, i in order if k == "r") == list(range(8))
+    assert sorted(i for k, i in order if k == "c") == list(range(8))
+    tall = wide = 0
+    for k, i in order[:-1]:  # the loaded region stays near-square
+        tall += rows[i][1] - rows[i][0] if k == "r" else 0
+        wide += cols[i][1] - cols[i][0] if k == "c" else 0
+        if tall and wide:
+            assert max(tall, wide) <= 2 * min(tall, wide) + 1792
+    assert _load_order(_block_bounds(512, 1, 256), _block_bounds(512, 1, 256)) == [("r", 0), ("c", 0)]
+    assert _load_order(_block_bounds(4096, 4, 256), _block_bounds(256, 1, 256))[-1] == ("r", 3)
+
 def test_empty_problem_is_a_no_op(lib):
     assert _call(lib, M=0) == nat.DX_OK
     assert _call(lib, N=0) == nat.DX_OK

@@ -249,6 +249,39 @@ def test_decode_fixup_bitwise_across_repeats(M, K, N):
                   f"decode {M}x{K}x{N}")
     _status_clean()
 
+
+@pytest.mark.parametrize("kern,M", [("decode", 16), ("umma", 256)])
+@pytest.mark.parametrize("act", ["gelu_erf", "gelu", "silu"])
+def test_activation_accuracy_across_range(kern, M, act):
+    """Y = act(X W + b) with W = I, so each output is act(x) of one fp16
+    input, x over [-12, 12].  GELU-erf (published erfc approximation) is
+    within one fp16 ulp of the fp64 value, or 1e-6 where the value is that
+    small.  GELU-tanh and SiLU take the hardware tanh (relative error about
+    2^-11 of tanh, so up to 2.5e-4 |x| absolute where 1 + tanh cancels)."""
+    K = N = 256
+    x = torch.linspace(-12.0, 12.0, M * K).reshape(M, K).to(torch.float16)
+    W = torch.zeros(K, N, dtype=torch.float16)
+    W[torch.arange(K), torch.arange(K)] = 1.0
+    b = torch.zeros(N, dtype=torch.float16)
+    Y = fused_linear(x.to(DEV), W.to(DEV), b.to(DEV), act, kernel=kern)
+    torch.cuda.synchronize()
+    v = x.double()
+    if act == "gelu_erf":
+        ref = 0.5 * v * torch.special.erfc(-v / 2 ** 0.5)
+    elif act == "gelu":
+        ref = 0.5 * v * (1 + torch.tanh((2 / torch.pi) ** 0.5 * (v + 0.044715 * v ** 3)))
+    else:
+        ref = v * torch.sigmoid(v)
+    got = Y.cpu().double()
+    ulp = torch.finfo(torch.float16).eps * ref.abs().clamp_min(2.0 ** -14)
+    err = (got - ref).abs()
+    if act == "gelu_erf":
+        bad = (err > ulp) & (err > 1e-6)
+    else:
+        bad = err > ulp + 2.5e-4 * v.abs()
+    assert not bad.any(), (f"{act} [{kern}]: {int(bad.sum())} off, e.g. x={float(v[bad][0]):.4f} "
+                           f"got {float(got[bad][0]):.6g} want {float(ref[bad][0]):.6g}")
+
 def test_nonzero_stream():
     s = torch.cuda.Stream()
     X, W, b, _ = _rand(256, 512, 512, torch.bfloat16, seed=2)
@@ -324,7 +357,8 @@ def test_split_tail(M, K, N, kern):
     _status_clean()
 
 
-@pytest.mark.parametrize("M,K,N,blocks", [(8192, 4096, 14336, (2, 4)), (300, 136, 1000, (3, 5)),
+@pytest.mark.parametrize("M,K,N,blocks", [(8192, 4096, 14336, (2, 4)), (8192, 4096, 14336, (8, 8)),
+                                           (300, 136, 1000, (3, 5)),
                                            (1, 64, 520, (1, 2)), (513, 256, 760, (2, 3))])
 def test_host_entry_matches_device_entry(M, K, N, blocks):
     """fused_linear_host (blocks copied in and out around per-block launches)
