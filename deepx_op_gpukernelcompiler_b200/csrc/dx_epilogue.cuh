@@ -97,8 +97,8 @@ __device__ __forceinline__ void act_loop(float (&v)[N]) {
 
 // The activation over a register array, the switch outside the element
 // loop: each case is straight-line code whose independent per-element
-// chains (erff, tanh) the compiler interleaves, instead of one branch per
-// element.
+// chains (erfc polynomial, tanh) the compiler interleaves, instead of one
+// branch per element.
 template <bool kFast = true, int N>
 __device__ __forceinline__ void act_apply_all(float (&v)[N], int act) {
   switch (act) {

@@ -265,8 +265,9 @@ def fused_linear_host(X: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | Non
     1792 columns: a strided copy of rows narrower than 3.5 KB runs at half
     the PCIe rate, and smaller blocks cost more per copy and per launch than
     an earlier first output block saves — 8192x4096x14336 bf16: 6.13 ms at
-    4 x 8, 6.26 ms at 2 x 4, 6.71 ms at 8 x 8).  On a copy stream, X's row blocks and W's column blocks go
-    to the device in an expanding-square order (_load_order); each output
+    4 x 8, 6.26 ms at 2 x 4, 6.71 ms at 8 x 8).  On a copy stream, X's row
+    blocks and W's column blocks go to the device in an expanding-square
+    order (_load_order); each output
     block is one fused launch on the current stream as soon as its row and
     column blocks are in; on a second copy stream each finished block of Y
     returns to `out` (strided, dx_copy_2d_async) while later blocks are still
