@@ -85,7 +85,7 @@ class ClockSampler:
         "hw_power_brake_slowdown": 0x80, "sw_power_cap": 0x4,
     }
 
-    def __init__(self, uuid: str | None, period: float = 0.02):
+    def __init__(self, uuid: str | None, period: float = 0.002):
         self.samples: list[tuple[float, int, float, int]] = []
         self.max_mhz = None
         self._stop = threading.Event()
@@ -143,60 +143,62 @@ def _cpu_threads() -> int:
         return os.cpu_count() or 1
 
 
-def cpu_reference_step(X32, W32, b32, act: str) -> float:
-    """One bounded step of the CPU reference arm; returns seconds."""
+def cpu_reference_step(X, W, b, act: str) -> float:
+    """One step of the CPU reference arm: the reference's own expression
+    act(a @ b + bias) (kernel.py:64-66, fusion.py:87-92) in torch fp32 on
+    the host cores, from the oracle's restatement; returns seconds."""
     import oracle
     t0 = time.perf_counter()
-    oracle.fused_linear_f32(X32, W32, b32, act)
+    oracle.torch_cpu.fused_linear(X, W, b, act)
     return time.perf_counter() - t0
 
 
-def cpu_baseline(w, W_host=None, target_s: float = 8.0) -> dict:
-    """The oracle's fp32 restatement timed on the host cores on a bounded
-    sample (rows of X) of the workload; value in TFLOP/s."""
-    import numpy as np
-    import torch
+def _cpu_sample(w, rows: int, W_host=None):
+    """fp32 host copies of a bounded row sample of the workload's inputs."""
     from deepx_op_gpukernelcompiler_b200.workloads import make_inputs
+    inp = make_inputs(w, device="cpu", M=rows)
+    W = (W_host if W_host is not None else inp["W"]).float().contiguous()
+    return inp["X"].float().contiguous(), W, inp["bias"].float().contiguous()
 
+
+def cpu_baseline(w, W_host=None, target_s: float = 8.0) -> dict:
+    """The reference's CPU expression (torch fp32, all host cores) timed on a
+    bounded row sample of the workload; value in TFLOP/s."""
+    import oracle
+    threads = oracle.torch_cpu.use_threads()
     rows0 = min(w.M, 64)
-    inp = make_inputs(w, device="cpu", M=rows0)
-    W32 = (W_host if W_host is not None else inp["W"]).float().numpy()
-    b32 = inp["bias"].float().numpy()
-    X32 = inp["X"].float().numpy()
-    cpu_reference_step(X32, W32, b32, w.act)  # warm BLAS threads
-    t = cpu_reference_step(X32, W32, b32, w.act)
+    X, W, b = _cpu_sample(w, rows0, W_host)
+    cpu_reference_step(X, W, b, w.act)  # warm the thread pool
+    t = cpu_reference_step(X, W, b, w.act)
     rows = int(min(w.M, max(rows0, rows0 * target_s / max(t, 1e-6) / 2)))
-    Xs = np.random.default_rng(0).standard_normal((rows, w.K), dtype=np.float32)
-    Xs = torch.from_numpy(Xs).to(w.torch_dtype).float().numpy()
+    X, _, _ = _cpu_sample(w, rows, W_host)
     reps, elapsed = 0, 0.0
     while reps < 2 or elapsed < target_s * 0.5:
-        elapsed += cpu_reference_step(Xs, W32, b32, w.act)
+        elapsed += cpu_reference_step(X, W, b, w.act)
         reps += 1
         if elapsed > target_s * 1.5:
             break
-    flops = 2.0 * rows * w.K * W32.shape[1] * reps
+    flops = 2.0 * rows * w.K * W.shape[1] * reps
     return {"value": round(flops / elapsed / 1e12, 4), "unit": "TFLOP/s",
-            "cores": _cpu_threads(), "kind": "port",
-            "sample": f"{reps} x act(X[{rows},{w.K}] @ W[{w.K},{W32.shape[1]}] + b) in fp32 "
-                      f"(numpy/OpenBLAS), {elapsed:.1f} s"}
+            "cores": threads, "kind": "port",
+            "sample": f"{reps} x act(X[{rows},{w.K}] @ W[{w.K},{W.shape[1]}] + b) in fp32, torch "
+                      f"CPU on {threads} threads (kernel.py:64-66 restated), {elapsed:.1f} s"}
 
 
 def run_reference(args) -> None:
     rank, world, _ = _dist_env()
     if rank != 0:
         return
-    import numpy as np
-    from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS, make_inputs
+    import oracle
+    from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS
 
+    threads = oracle.torch_cpu.use_threads()
     w = WORKLOADS[args.workload]
     rows = 512 if w.M >= 512 else w.M
-    inp = make_inputs(w, device="cpu", M=rows)
-    X32 = inp["X"].float().numpy()
-    W32 = inp["W"].float().numpy()
-    b32 = inp["bias"].float().numpy()
+    X, W, b = _cpu_sample(w, rows)
     for _ in range(args.warmup):
-        cpu_reference_step(X32, W32, b32, w.act)
-    times = [cpu_reference_step(X32, W32, b32, w.act) for _ in range(args.steps)]
+        cpu_reference_step(X, W, b, w.act)
+    times = [cpu_reference_step(X, W, b, w.act) for _ in range(args.steps)]
     total = sum(times)
     flops_step = 2.0 * rows * w.K * w.N
     value = flops_step * len(times) / total / 1e12
@@ -207,15 +209,67 @@ def run_reference(args) -> None:
         "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": DATA,
         "config": {"workload": w.name, "M": w.M, "K": w.K, "N": w.N, "act": w.act,
                    "sample_rows_per_step": rows, "parallelism": "host cores (rank 0)"},
-        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": _cpu_threads(),
+        "cpu_baseline": {"value": round(value, 4), "unit": "TFLOP/s", "cores": threads,
                          "kind": "port",
                          "sample": f"per step act(X[{rows},{w.K}] @ W[{w.K},{w.N}] + b), fp32 "
-                                   "numpy/OpenBLAS restatement of kernel.py:64-66"},
+                                   f"torch CPU on {threads} threads: the reference expression "
+                                   "kernel.py:64-66 with fusion.py:87-92 activations, restated"},
         "e2e": {"value": round(value, 4), "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
         "gpu_launches": 0,
     }
     print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------ parity
+def _sample_rows(M: int, rows: int = 16) -> list[tuple[int, int]]:
+    """First, middle and last row blocks of an M-row output."""
+    mid = max(0, M // 2 - rows // 2)
+    return sorted({(0, min(rows, M)), (mid, min(M, mid + rows)), (max(0, M - rows), M)})
+
+
+def _row_index(M: int):
+    import numpy as np
+    return np.concatenate([np.arange(a, b) for a, b in _sample_rows(M)])
+
+
+def _parity(got_rows, want, rtol: float, atol: float) -> dict:
+    """Row sample of the engine's output against the fp64 oracle's rows."""
+    import numpy as np
+    g = got_rows.float().cpu().numpy()
+    err = np.abs(g - want)
+    ok = bool((err <= atol + rtol * np.abs(want)).all())
+    return {"ok": ok, "max_abs_err": float(err.max()) if err.size else 0.0,
+            "rows": int(g.shape[0]), "tol": [rtol, atol]}
+
+
+def _linear_parity(X, W, b, act, Y, rtol=2e-2, atol=2e-2) -> dict:
+    """act(X W + b) on sampled rows of X, fp64 oracle, against Y's rows."""
+    import oracle
+    idx = _row_index(X.shape[0])
+    want = oracle.fused_linear_f64(X[idx].float().cpu().numpy(), W.float().cpu().numpy(),
+                                   b.float().cpu().numpy() if b is not None else None, act)
+    return _parity(Y[idx], want, rtol, atol)
+
+
+def _row_parallel_parity(X, first_fn, W2, b2, residual: bool, out, world, dev) -> dict:
+    """Sampled rows of Y = sum_r first_r(X) W2_r + b2 (+ X), each rank adding
+    its own term in fp64 (oracle) and the terms summed over ranks, against
+    this rank's output rows."""
+    import oracle
+    import torch
+    import torch.distributed as dist
+    idx = _row_index(X.shape[0])
+    Xr = X[idx].float().cpu().numpy()
+    H = first_fn(Xr)
+    part = torch.from_numpy(oracle.fused_linear_f64(H, W2.float().cpu().numpy(), None, None))
+    part = part.to(dev)
+    if world > 1:
+        dist.all_reduce(part)
+    want = part.cpu().numpy() + b2.float().cpu().numpy()
+    if residual:
+        want = want + Xr
+    return _parity(out[idx], want, 2e-2, 2e-2)
 
 
 # ------------------------------------------------------------ GPU arm
@@ -331,6 +385,8 @@ def run_gpu(args) -> None:
     if status:
         raise RuntimeError(f"device status {status}: a kernel wait timed out")
 
+    parity = {"headline_shard": _linear_parity(X, Wt, b, w.act, Y)}
+
     local_ms = sum(times)
     total_ms = _max_over_ranks(local_ms, world, dev)
     ms_step = total_ms / args.steps
@@ -406,7 +462,16 @@ def run_gpu(args) -> None:
 
     extra = {"sustained": sustained, "pytorch_gpu": pytorch_gpu}
     if not args.no_extra:
-        extra.update(run_extras(args, world, rank, dev, peaks, flush))
+        extra.update(run_extras(args, world, rank, dev, peaks, flush, parity))
+    # Parity of every rank's outputs: the line says ok only if all ranks agree.
+    ok_all = all(v["ok"] for v in parity.values())
+    if world > 1:
+        flag = torch.tensor([1 if ok_all else 0], device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN)
+        ok_all = bool(flag.item())
+    if clocks and clocks.get("sm_mhz"):
+        # Clock-normalised step time: thousands of SM cycles per step.
+        clocks["kcycles_per_step"] = round(ms_step * clocks["sm_mhz"], 1)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
@@ -434,6 +499,9 @@ def run_gpu(args) -> None:
                            "per output block, dx_copy_2d_async for the copies)"},
             "gpu_launches": args.steps,
             "clocks": clocks,
+            "parity": {"ok": ok_all, "all_ranks": world, "oracle": "fp64 C restatement of "
+                       "act(a @ b + bias) (kernel.py:64-66) on sampled rows",
+                       "items": parity},
             "extra": extra,
         }
         if cpu is not None:
@@ -444,12 +512,14 @@ def run_gpu(args) -> None:
         dist.destroy_process_group()
 
 
-def run_extras(args, world, rank, dev, peaks, flush) -> dict:
-    """The other workloads of the metric: decode HBM GB/s, the square GEMM and
-    the MLP chain (all ranks take part; timings are max over ranks)."""
+def run_extras(args, world, rank, dev, peaks, flush, parity) -> dict:
+    """The other workloads of the metric: decode HBM GB/s, the square GEMM,
+    the fp32 configuration, the gated dual GEMM and the two row-parallel
+    chains (all ranks take part; timings are max over ranks).  Each adds its
+    oracle check of sampled output rows to `parity`."""
     import torch
     from deepx_op_gpukernelcompiler_b200 import _native, fused_linear
-    from deepx_op_gpukernelcompiler_b200.shard import ParallelMLP, shard_bounds
+    from deepx_op_gpukernelcompiler_b200.shard import shard_bounds
     from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS
 
     out = {}
@@ -486,6 +556,8 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
     _barrier(world)
     t = _time_launches(dec, steps, lambda: None, stream)
     ms = _max_over_ranks(sum(t), world, dev) / steps
+    fused_linear(X, Ws[0], b, w.act, out=Y)
+    parity["decode_shard"] = _linear_parity(X, Ws[0], b, w.act, Y)
     bytes_rank = 2 * (w.M * w.K + w.K * n_loc + n_loc + w.M * n_loc)
     bytes_total = w.min_bytes
     out[w.name] = {"value": round(bytes_total / (ms * 1e-3) / 1e9, 1), "unit": "GB/s",
@@ -516,9 +588,34 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
     _barrier(world)
     t = _time_launches(sq, steps, flush, stream)
     ms = _max_over_ranks(sum(t), world, dev) / steps
+    parity["square_shard"] = _linear_parity(X, Wt, b, w.act, Y)
     tf = w.flops / (ms * 1e-3) / 1e12
     out[w.name] = {"value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
                    "frac_of_peak": round(tf / world / tflops_peak, 4), "kernel": sq_plan}
+    del X, Wt, b, Y
+
+    # The reference's CPU-runnable configuration on the GPU: ReLU(X[256,512]
+    # W[512,512] + b) in exact fp32 (every rank runs the whole problem).
+    w = WORKLOADS["linear_relu_256x512x512_f32"]
+    from deepx_op_gpukernelcompiler_b200.workloads import make_inputs
+    inp = make_inputs(w, device="cpu")
+    X, Wt, b = (inp[k].to(dev) for k in ("X", "W", "bias"))
+    Y = torch.empty(w.M, w.N, dtype=torch.float32, device=dev)
+
+    def f32():
+        fused_linear(X, Wt, b, w.act, out=Y)
+
+    for _ in range(5):
+        f32()
+    torch.cuda.synchronize()
+    f32_plan = _native.last_launch_plan()
+    _barrier(world)
+    t = _time_launches(f32, steps, flush, stream)
+    ms = _max_over_ranks(sum(t), world, dev) / steps
+    parity["fp32_relu_256x512x512"] = _linear_parity(X, Wt, b, w.act, Y, 1e-4, 1e-4)
+    out[w.name] = {"value": round(ms * 1e3, 2), "unit": "us per launch (lower is better)",
+                   "tflops": round(w.flops / (ms * 1e-3) / 1e12, 3), "kernel": f32_plan,
+                   "bound": "latency (0.134 GFLOP, exact fp32 FFMA)"}
     del X, Wt, b, Y
 
     # Gated FFN's gate/up projections in one dual-GEMM launch:
@@ -544,58 +641,144 @@ def run_extras(args, world, rank, dev, peaks, flush) -> dict:
     _barrier(world)
     t = _time_launches(gated, steps, flush, stream)
     ms = _max_over_ranks(sum(t), world, dev) / steps
+    idx = _row_index(M_g)
+    import oracle
+    parity["gated_dual_gemm_shard"] = _parity(Y[idx], oracle.gated_linear_f64(
+        X[idx].float().cpu().numpy(), Wg.float().cpu().numpy(), bg.float().cpu().numpy(),
+        Wu.float().cpu().numpy(), bu.float().cpu().numpy(), "silu"), 2e-2, 2e-2)
     tf = 2 * 2 * M_g * N_g * K_g / (ms * 1e-3) / 1e12
     out[f"ffn_gated_gate_up_{M_g}x{K_g}x{N_g}_bf16"] = {
         "value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
         "frac_of_peak": round(tf / world / tflops_peak, 4), "kernel": "umma gated (dual GEMM)"}
     del X, Wg, Wu, bg, bu, Y
 
-    # MLP chain: Y = GELU(X W1 + b1) W2 + b2 + X; column -> row parallel with
-    # one all-reduce of Y (NCCL) when world > 1.
+    out.update(run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g))
+    return out
+
+
+def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
+    """The two-layer MLP chain Y = GELU(X W1 + b1) W2 + b2 + X at
+    X[16384,4096], hidden 16384: one GPU runs the two fused launches; N GPUs
+    run column -> row parallel with the overlapped NVLink reduction (several
+    chunkings, the fastest reported as the value) and with NCCL.  X and b2
+    are the same on every rank (seeded alike), the weight shards differ."""
+    import torch
+
+    import oracle
+    from deepx_op_gpukernelcompiler_b200.shard import ParallelGatedFFN, ParallelMLP, shard_bounds
+    from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS
+
+    out = {}
+    stream = torch.cuda.current_stream(dev)
+    tflops_peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
     w = WORKLOADS["mlp_residual_16384x4096x16384_bf16"]
     h0, h1 = shard_bounds(w.N, world, rank, 64)
     h_loc = h1 - h0
     dt = w.torch_dtype
-    X = torch.randn(w.M, w.K, generator=g, device=dev).to(dt)
+    g_shared = torch.Generator(device=dev)
+    g_shared.manual_seed(w.seed)
+    X = torch.randn(w.M, w.K, generator=g_shared, device=dev).to(dt)
+    b2 = (torch.rand(w.K, generator=g_shared, device=dev) * 0.2 - 0.1).to(dt)
     W1 = (torch.randn(w.K, h_loc, generator=g, device=dev) / math.sqrt(w.K)).to(dt)
     b1 = (torch.rand(h_loc, generator=g, device=dev) * 0.2 - 0.1).to(dt)
     W2 = (torch.randn(h_loc, w.K, generator=g, device=dev) / math.sqrt(w.N)).to(dt)
-    b2 = (torch.rand(w.K, generator=g, device=dev) * 0.2 - 0.1).to(dt)
     H = torch.empty(w.M, h_loc, dtype=dt, device=dev)
     Yo = torch.empty(w.M, w.K, dtype=dt, device=dev)
-    if world > 1:
-        mlp = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, mode="fused")
-        run = lambda: mlp(X, hidden=H)  # noqa: E731
-    else:
-        from deepx_op_gpukernelcompiler_b200 import mlp_residual
-        run = lambda: mlp_residual(X, W1, b1, W2, b2, w.act, hidden=H, out=Yo)  # noqa: E731
-    for _ in range(3):
-        run()
-    torch.cuda.synchronize()
-    _barrier(world)
-    msteps = max(3, steps // 2)
-    t = _time_launches(run, msteps, flush, stream)
-    ms = _max_over_ranks(sum(t), world, dev) / msteps
-    tf = w.flops / (ms * 1e-3) / 1e12
-    out[w.name] = {"value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
-                   "frac_of_peak": round(tf / world / tflops_peak, 4),
-                   "parallelism": f"column->row x{world}" + (
-                       " + NVLink reduce-broadcast (symmetric memory)" if world > 1 else ""),
-                   "gpu_launches_per_step": 2 if world == 1 else 3}
-    if world > 1:
-        # The same chain with an NCCL all-reduce of Y in 4 asynchronous chunks.
-        mlp_n = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, chunks=4, mode="nccl")
-        run_n = lambda: mlp_n(X, hidden=H, out=Yo)  # noqa: E731
+    W1c, b1c = W1.float().cpu().numpy(), b1.float().cpu().numpy()
+
+    def first_ref(Xr):
+        return oracle.fused_linear_f64(Xr, W1c, b1c, w.act)
+
+    msteps = max(3, min(args.steps, 20) // 2)
+
+    def time_run(run, host_us):
         for _ in range(3):
-            run_n()
+            run()
         torch.cuda.synchronize()
         _barrier(world)
-        t = _time_launches(run_n, msteps, flush, stream)
-        ms = _max_over_ranks(sum(t), world, dev) / msteps
+        t = _time_launches(run, msteps, flush, stream, host_us)
+        return _max_over_ranks(sum(t), world, dev) / msteps
+
+    if world == 1:
+        from deepx_op_gpukernelcompiler_b200 import mlp_residual
+        ms = time_run(lambda: mlp_residual(X, W1, b1, W2, b2, w.act, hidden=H, out=Yo), 200.0)
+        parity["mlp_chain"] = _row_parallel_parity(X, first_ref, W2, b2, True, Yo, world, dev)
+        tf = w.flops / (ms * 1e-3) / 1e12
+        out[w.name] = {"value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+                       "frac_of_peak": round(tf / tflops_peak, 4),
+                       "parallelism": "one GPU, two fused launches", "gpu_launches_per_step": 2}
+    else:
+        mlp = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, mode="fused")
+        sweep = {}
+        for chunks, first in ((4, None), (4, 2), (8, 2), (8, 4), (2, None)):
+            mlp.chunks, mlp.first_chunks = chunks, first
+            ms = time_run(lambda: mlp(X, hidden=H, out=Yo), 1500.0)
+            sweep[f"chunks={chunks},first={first or chunks}"] = round(ms, 4)
+        best = min(sweep, key=sweep.get)
+        chunks, first = (int(v.split("=")[1]) for v in best.split(","))
+        mlp.chunks, mlp.first_chunks = chunks, first
+        ms = time_run(lambda: mlp(X, hidden=H, out=Yo), 1500.0)
+        assert mlp.last_path == "fused"
+        parity["mlp_fused"] = _row_parallel_parity(X, first_ref, W2, b2, True, Yo, world, dev)
+        tf = w.flops / (ms * 1e-3) / 1e12
+        out[w.name] = {"value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+                       "frac_of_peak": round(tf / world / tflops_peak, 4),
+                       "parallelism": f"column->row x{world}, reduction overlapped with the "
+                                      f"GEMMs ({chunks} row chunks, first GEMM in {first} "
+                                      "launches; dx_row_reduce over NVLink)",
+                       "chunking_ms": sweep,
+                       "gpu_launches_per_step": chunks + first + chunks + 1}
+        # The same chain with an NCCL all-reduce of Y in 4 asynchronous chunks.
+        mlp_n = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, chunks=4, mode="nccl")
+        Yn = torch.empty_like(Yo)
+        ms = time_run(lambda: mlp_n(X, hidden=H, out=Yn), 1500.0)
+        parity["mlp_nccl"] = _row_parallel_parity(X, first_ref, W2, b2, True, Yn, world, dev)
         tf = w.flops / (ms * 1e-3) / 1e12
         out[w.name + "_nccl"] = {"value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
                                  "frac_of_peak": round(tf / world / tflops_peak, 4),
-                                 "parallelism": f"column->row x{world} + NCCL all-reduce (4 chunks)"}
+                                 "parallelism": f"column->row x{world} + NCCL all-reduce "
+                                                "(4 chunks)"}
+        del mlp, mlp_n, Yn
+    del X, W1, b1, W2, b2, H, Yo
+
+    # The gated FFN chain (ffn_gated, fusion.py:44-46): Y = (silu(X Wg + bg) *
+    # (X Wu + bu)) Wo + bo, X[8192,4096], hidden 14336; one GPU runs the
+    # engine chain, N GPUs the column -> row sharding with the overlapped
+    # reduction.
+    M_g, K_g, N_g = 8192, 4096, 14336
+    h0, h1 = shard_bounds(N_g, world, rank, 64)
+    h_loc = h1 - h0
+    g_shared.manual_seed(5)
+    X = torch.randn(M_g, K_g, generator=g_shared, device=dev).to(torch.bfloat16)
+    bo = (torch.rand(K_g, generator=g_shared, device=dev) * 0.2 - 0.1).to(torch.bfloat16)
+    Wg = (torch.randn(K_g, h_loc, generator=g, device=dev) / math.sqrt(K_g)).to(torch.bfloat16)
+    Wu = (torch.randn(K_g, h_loc, generator=g, device=dev) / math.sqrt(K_g)).to(torch.bfloat16)
+    bg = (torch.rand(h_loc, generator=g, device=dev) * 0.2 - 0.1).to(torch.bfloat16)
+    bu = (torch.rand(h_loc, generator=g, device=dev) * 0.2 - 0.1).to(torch.bfloat16)
+    Wo = (torch.randn(h_loc, K_g, generator=g, device=dev) / math.sqrt(N_g)).to(torch.bfloat16)
+    Hg = torch.empty(M_g, h_loc, dtype=torch.bfloat16, device=dev)
+    Yg = torch.empty(M_g, K_g, dtype=torch.bfloat16, device=dev)
+    if world == 1:
+        from deepx_op_gpukernelcompiler_b200 import gated_ffn
+        run = lambda: gated_ffn(X, Wg, bg, Wu, bu, Wo, bo, "silu", hidden=Hg, out=Yg)  # noqa
+        launches = 2
+    else:
+        ffn = ParallelGatedFFN.from_shards(Wg, bg, Wu, bu, Wo, bo, "silu", mode="fused")
+        run = lambda: ffn(X, hidden=Hg, out=Yg)  # noqa: E731
+        launches = 4 + 4 + 5
+    ms = time_run(run, 1500.0)
+    Wgc, Wuc = Wg.float().cpu().numpy(), Wu.float().cpu().numpy()
+    bgc, buc = bg.float().cpu().numpy(), bu.float().cpu().numpy()
+    parity["gated_ffn_chain"] = _row_parallel_parity(
+        X, lambda Xr: oracle.gated_linear_f64(Xr, Wgc, bgc, Wuc, buc, "silu"), Wo, bo, False, Yg,
+        world, dev)
+    tf = 2 * M_g * K_g * N_g * 3 / (ms * 1e-3) / 1e12
+    out[f"ffn_gated_chain_{M_g}x{K_g}x{N_g}_bf16"] = {
+        "value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
+        "frac_of_peak": round(tf / world / tflops_peak, 4),
+        "parallelism": "one GPU" if world == 1 else
+        f"column->row x{world}, reduction overlapped with the GEMMs",
+        "gpu_launches_per_step": launches}
     return out
 
 

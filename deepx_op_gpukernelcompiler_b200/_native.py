@@ -65,6 +65,13 @@ SIGNATURES = {
                                            ctypes.c_int, _i64, _i64, _i64, _vp, _vp, _i64,
                                            ctypes.POINTER(ctypes.c_void_p), _i64, ctypes.c_int,
                                            _vp]),
+    "dx_row_reduce": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p),
+                                     ctypes.POINTER(ctypes.c_void_p),
+                                     ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
+                                     _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _i64, _i64,
+                                     ctypes.c_int, _vp, _vp, _i64, _vp, _i64, ctypes.c_int,
+                                     ctypes.c_int, ctypes.c_int, _vp]),
+    "dx_row_flag_words": (ctypes.c_int, []),
     "dx_fused_linear_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, ctypes.c_int, ctypes.c_int]),
     "dx_fused_gated_linear": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
                                              _i64, _i64, _i64, ctypes.c_int, ctypes.c_int,

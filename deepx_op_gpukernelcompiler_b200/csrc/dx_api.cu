@@ -105,6 +105,53 @@ int device_sms(int dev, int* sms) {
   return DX_OK;
 }
 
+// ------------------------------------------------- timeout reporting
+// One pinned, device-mapped int per device: the host-visible copy of the
+// device status word (dx::g_status_mirror).  Installed on a device by the
+// first call that is not being captured into a graph; afterwards every entry
+// point reads its device's word before launching, without synchronising.
+constexpr int kMaxDevices = 64;
+int* g_host_status = nullptr;  // kMaxDevices words, pinned and mapped
+bool g_mirror_installed[kMaxDevices] = {};
+
+int install_status_mirror(int dev, cudaStream_t s) {
+  if (dev < 0 || dev >= kMaxDevices) return DX_OK;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_mirror_installed[dev]) return DX_OK;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
+    (void)cudaGetLastError();
+    return DX_OK;  // set up by a later call outside the capture
+  }
+  if (g_host_status == nullptr) {
+    void* h = nullptr;
+    cudaError_t e = cudaHostAlloc(&h, kMaxDevices * sizeof(int),
+                                  cudaHostAllocMapped | cudaHostAllocPortable);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaHostAlloc(status mirror)");
+    std::memset(h, 0, kMaxDevices * sizeof(int));
+    g_host_status = static_cast<int*>(h);
+  }
+  int* dptr = nullptr;
+  cudaError_t e = cudaHostGetDevicePointer(reinterpret_cast<void**>(&dptr), g_host_status + dev, 0);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaHostGetDevicePointer(status mirror)");
+  e = cudaMemcpyToSymbol(dx::g_status_mirror, &dptr, sizeof(dptr));
+  if (e != cudaSuccess) return cuda_fail(e, "install status mirror");
+  g_mirror_installed[dev] = true;
+  return DX_OK;
+}
+
+// DX_ERR_DEVICE_TIMEOUT when an earlier launch on `dev` reported a wait that
+// ran out and dx_device_status has not cleared it since.
+int check_status_mirror(int dev) {
+  if (g_host_status == nullptr || dev < 0 || dev >= kMaxDevices) return DX_OK;
+  if (reinterpret_cast<volatile int*>(g_host_status)[dev] == 0) return DX_OK;
+  return fail(DX_ERR_DEVICE_TIMEOUT,
+              "an earlier launch on device %d gave up a bounded wait, so its output is "
+              "incomplete (and a split-K workspace may hold stale tickets); dx_device_status "
+              "reads and clears the condition",
+              dev);
+}
+
 int ensure_smem_attr(int dev, const void* fn, int smem_bytes, bool max_carveout) {
   std::lock_guard<std::mutex> lk(g_mu);
   auto key = std::make_pair(dev, fn);
@@ -721,6 +768,8 @@ int run(const Problem& p, int kernel) {
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   int sms = 0;
   if ((rc = device_sms(dev, &sms))) return rc;
+  if ((rc = install_status_mirror(dev, p.stream))) return rc;
+  if ((rc = check_status_mirror(dev))) return rc;
 
   int variant = kernel == DX_KERNEL_AUTO ? select_variant(p, sms, true) : kernel;
   if (variant == DX_KERNEL_UMMA || variant == DX_KERNEL_UMMA_1CTA || variant == DX_KERNEL_DECODE) {
@@ -892,6 +941,8 @@ int dx_reduce_broadcast(void* const* P, int world, int rank, int64_t rows_per_ra
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if ((rc = device_sms(dev, &sms))) return rc;
+  if ((rc = install_status_mirror(dev, static_cast<cudaStream_t>(stream)))) return rc;
+  if ((rc = check_status_mirror(dev))) return rc;
   const long long work = rows_per_rank * (N / 8);
   const int grid = static_cast<int>(std::max<long long>(
       1, std::min<long long>((work + 511) / 512, 8LL * sms)));
@@ -909,6 +960,93 @@ int dx_reduce_broadcast(void* const* P, int world, int rank, int64_t rows_per_ra
         ldy);
   e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch reduce_broadcast_kernel");
+  return DX_OK;
+}
+
+int dx_row_flag_words(void) { return dx::kRowFlagWords; }
+
+int dx_row_reduce(void* const* P, void* const* S, int* const* F, int world, int rank, int64_t M,
+                  int64_t N, int64_t ldp, int64_t a_row0, int64_t a_rows, int a_chunk,
+                  int64_t b_row0, int64_t b_rows, int b_chunk, const void* bias, const void* R,
+                  int64_t ldr, void* Y, int64_t ldy, int epoch, int grid, int dtype,
+                  void* stream) {
+  t_last_error.clear();
+  if (P == nullptr || S == nullptr || F == nullptr || Y == nullptr)
+    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: NULL buffer array or output");
+  if (world < 1 || world > dx::kRowMaxWorld || rank < 0 || rank >= world)
+    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: world must be 1..%d and 0 <= rank < world",
+                dx::kRowMaxWorld);
+  if (dtype != DX_DTYPE_F16 && dtype != DX_DTYPE_BF16)
+    return fail(DX_ERR_UNSUPPORTED, "row_reduce supports fp16/bf16");
+  if (M <= 0 || M % world != 0 || M > 0x7fffffffLL || N <= 0 || N % 8 != 0 || N > 0x7fffffffLL)
+    return fail(DX_ERR_INVALID_ARGUMENT,
+                "row_reduce needs M > 0 divisible by world (M=%lld, world=%d) and N %% 8 == 0",
+                (long long)M, world);
+  if (ldp < N || ldp % 8 != 0 || ldy < N || ldy % 8 != 0 || (R != nullptr && (ldr < N || ldr % 8)))
+    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: pitches must be >= N and multiples of 8");
+  if (epoch <= 0) return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: epoch must be positive");
+  auto bad_chunk = [&](int64_t row0, int64_t rows, int chunk) {
+    return rows < 0 || (rows > 0 && (row0 < 0 || row0 % world != 0 || rows % world != 0 ||
+                                     row0 + rows > M || chunk < 0 ||
+                                     chunk >= dx::kRowMaxChunks));
+  };
+  if (bad_chunk(a_row0, a_rows, a_chunk) || bad_chunk(b_row0, b_rows, b_chunk))
+    return fail(DX_ERR_INVALID_ARGUMENT,
+                "row_reduce: a chunk must lie in [0, M), start and span multiples of world, "
+                "and have an index below %d",
+                dx::kRowMaxChunks);
+  if ((bias != nullptr && !aligned16(bias)) || (R != nullptr && !aligned16(R)) || !aligned16(Y))
+    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce needs 16-byte-aligned bias, R and Y");
+  dx::RowReduceArgs a{};
+  for (int r = 0; r < world; ++r) {
+    if (P[r] == nullptr || !aligned16(P[r]) || S[r] == nullptr || !aligned16(S[r]) ||
+        F[r] == nullptr || (reinterpret_cast<uintptr_t>(F[r]) & 3u) != 0)
+      return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: buffers of rank %d NULL or misaligned", r);
+    a.P.p[r] = P[r];
+    a.S.p[r] = S[r];
+    a.F.p[r] = F[r];
+  }
+  int dev = 0, sms = 0, rc;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if ((rc = device_sms(dev, &sms))) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = install_status_mirror(dev, s))) return rc;
+  if ((rc = check_status_mirror(dev))) return rc;
+  if (a_rows == 0 && b_rows == 0) return DX_OK;
+  a.world = world;
+  a.rank = rank;
+  a.N = static_cast<int>(N);
+  a.ldp = ldp;
+  a.ldr = ldr;
+  a.ldy = ldy;
+  a.slab_base = static_cast<long long>(epoch & 1) * (M / world);
+  a.a_row0 = a_row0;
+  a.a_rows = static_cast<int>(a_rows);
+  a.a_chunk = a_chunk;
+  a.b_row0 = b_row0;
+  a.b_rows = static_cast<int>(b_rows);
+  a.b_chunk = b_chunk;
+  a.bias = bias;
+  a.R = R;
+  a.Y = Y;
+  a.epoch = epoch;
+  if (grid <= 0 || grid > sms) grid = sms;
+  const void* fn = dtype == DX_DTYPE_F16
+                       ? reinterpret_cast<const void*>(dx::row_reduce_kernel<__half>)
+                       : reinterpret_cast<const void*>(dx::row_reduce_kernel<__nv_bfloat16>);
+  // Same shared-memory configuration preference as the GEMM kernels, so the
+  // CTAs can be placed on SMs those kernels occupy.
+  if ((rc = ensure_smem_attr(dev, fn, 0, true))) return rc;
+  set_plan("row_reduce world=%d rank=%d A=[%lld,+%lld) B=[%lld,+%lld) N=%lld grid=%d epoch=%d",
+           world, rank, (long long)a_row0, (long long)a_rows, (long long)b_row0,
+           (long long)b_rows, (long long)N, grid, epoch);
+  if (dtype == DX_DTYPE_F16)
+    dx::row_reduce_kernel<__half><<<grid, dx::kRowThreads, 0, s>>>(a);
+  else
+    dx::row_reduce_kernel<__nv_bfloat16><<<grid, dx::kRowThreads, 0, s>>>(a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch row_reduce_kernel");
   return DX_OK;
 }
 
@@ -1006,6 +1144,13 @@ int dx_device_status(void* stream, int* status) {
     e = cudaMemcpyToSymbol(dx::g_device_status, &zero, sizeof(int));
     if (e != cudaSuccess) return cuda_fail(e, "clear device status");
   }
+  int dev = 0;
+  if (g_host_status != nullptr && cudaGetDevice(&dev) == cudaSuccess && dev >= 0 &&
+      dev < kMaxDevices) {
+    volatile int* mirror = reinterpret_cast<volatile int*>(g_host_status) + dev;
+    v |= *mirror;
+    *mirror = 0;
+  }
   *status = v;
   return DX_OK;
 }
@@ -1091,6 +1236,7 @@ extern "C" int dx_fused_linear_decode_noalloc(const void* X, const void* W, cons
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   int sms = 0;
   if ((rc = device_sms(dev, &sms))) return rc;
+  if ((rc = check_status_mirror(dev))) return rc;
   const DecodePlan d = decode_plan(M, N, K, sms);
   if (d.bytes > kStaticScratchBytes)
     return fail(DX_ERR_WORKSPACE,

@@ -11,6 +11,7 @@
 #pragma once
 
 #include "dx_epilogue.cuh"
+#include "dx_ptx.cuh"
 
 namespace dx {
 
@@ -93,6 +94,190 @@ __global__ void __launch_bounds__(256)
     }
   }
   __threadfence_system();
+}
+
+// =====================================================================
+// Chunked row-parallel reduction that overlaps the GEMMs.
+//
+// The second GEMM of a row-parallel chain runs in row chunks.  After chunk c
+// of every rank's partial is complete, one launch of row_reduce_kernel on a
+// side stream (concurrent with the next chunk's GEMMs on the main stream)
+//   phase A (reduce-scatter, chunk c): sums this rank's slab of the chunk's
+//     rows — rows c0 + rank*rows/world ... — over all ranks' partials (peer
+//     loads, rank order, fp32), adds bias and residual once, rounds, and
+//     writes the slab into this rank's output and into its own peer-readable
+//     slab buffer;
+//   phase B (all-gather, an earlier chunk): copies every other rank's slab of
+//     that chunk from the peer's slab buffer into this rank's output.
+// The output is written only by its own rank, so it can be any device buffer
+// the caller owns.  Ranks synchronise through flag words in peer-mapped
+// memory, each stamped with the step's epoch (a counter that grows by one per
+// step on every rank): PART(c, s) = rank s's partial of chunk c is complete,
+// RED(c, s) = rank s's slab of chunk c is in its slab buffer.
+// Every wait is bounded (kRowWaitLimitNs); on expiry the kernel reports the
+// timeout in the status word and returns.
+//
+// Launch with at most one CTA per SM: 128 threads and <= 80 registers per
+// thread, no dynamic shared memory, so a CTA fits beside a resident tensor-
+// core GEMM CTA (320 threads x 168 registers, ~231 KB of shared memory) and
+// the two kernels run on the same SMs at once.
+// =====================================================================
+constexpr int kRowMaxWorld = 8;
+constexpr int kRowMaxChunks = 64;
+constexpr int kRowThreads = 128;
+// Flag words per rank: PART[chunk][src], RED[chunk][src], arrival counters.
+constexpr int kRowFlagWords = 2 * kRowMaxChunks * kRowMaxWorld + kRowMaxChunks;
+constexpr uint64_t kRowWaitLimitNs = 2000ull * 1000ull * 1000ull;  // 2 s
+
+__host__ __device__ constexpr int row_part_flag(int chunk, int src) {
+  return chunk * kRowMaxWorld + src;
+}
+__host__ __device__ constexpr int row_red_flag(int chunk, int src) {
+  return (kRowMaxChunks + chunk) * kRowMaxWorld + src;
+}
+__host__ __device__ constexpr int row_counter(int chunk) {
+  return 2 * kRowMaxChunks * kRowMaxWorld + chunk;
+}
+
+struct FlagPtrs {
+  int* p[kRowMaxWorld];
+};
+
+struct RowReduceArgs {
+  RankPtrs P;        // partials [M][ldp], every rank
+  RankPtrs S;        // slab buffers [2 * M / world][N], every rank
+  FlagPtrs F;        // flag words, every rank
+  int world, rank, N;
+  long long ldp, ldr, ldy;
+  long long slab_base;  // first slab-buffer row of this step (epoch parity)
+  long long a_row0;     // phase A chunk: first row, rows (0: no phase A), flag index
+  int a_rows, a_chunk;
+  long long b_row0;     // phase B chunk
+  int b_rows, b_chunk;
+  const void* bias;     // [N] or nullptr
+  const void* R;        // residual [M][ldr] or nullptr
+  void* Y;              // this rank's output [M][ldy]
+  int epoch;
+};
+
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Waits until flags[first + s] has reached `epoch` for every s < count other
+// than `skip`.  Bounded: false (and the status word set) after the limit.
+__device__ __forceinline__ bool row_wait_flags(const int* flags, int first, int count, int skip,
+                                               int epoch) {
+  const uint64_t t0 = global_timer_ns();
+  for (int s = 0; s < count; ++s) {
+    if (s == skip) continue;
+    while (ld_acquire_sys(flags + first + s) - epoch < 0) {
+      if (global_timer_ns() - t0 > kRowWaitLimitNs) {
+        report_timeout();
+        return false;
+      }
+      __nanosleep(128);
+    }
+  }
+  return true;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads, 6) row_reduce_kernel(const RowReduceArgs a) {
+  const int tid = threadIdx.x;
+  const int groups = a.N / 8;  // 16-byte column groups per row
+  const long long nthreads = static_cast<long long>(gridDim.x) * kRowThreads;
+  const long long gtid = static_cast<long long>(blockIdx.x) * kRowThreads + tid;
+  T* const Y = static_cast<T*>(a.Y);
+
+  if (a.a_rows > 0) {
+    // This launch follows the GEMM that wrote chunk a_chunk of the local
+    // partial: announce it to every rank (each CTA stamps the same epoch, so
+    // the announcement never waits for one particular CTA to be scheduled).
+    if (tid < a.world) {
+      __threadfence_system();
+      st_release_sys(a.F.p[tid] + row_part_flag(a.a_chunk, a.rank), a.epoch);
+    }
+    // One thread waits; the block-wide vote passes its verdict to the rest
+    // (no shared memory, which the co-resident GEMM CTA leaves almost none of).
+    const int ok = tid == 0
+        ? (row_wait_flags(a.F.p[a.rank], row_part_flag(a.a_chunk, 0), a.world, -1, a.epoch) ? 1 : 0)
+        : 1;
+    if (!__syncthreads_and(ok)) return;
+
+    const int slab = a.a_rows / a.world;
+    const long long row0 = a.a_row0 + static_cast<long long>(a.rank) * slab;
+    const long long srow0 = a.slab_base + a.a_row0 / a.world;
+    const long long total = static_cast<long long>(slab) * groups;
+    const T* const bias = static_cast<const T*>(a.bias);
+    const T* const R = static_cast<const T*>(a.R);
+    T* const Sown = static_cast<T*>(a.S.p[a.rank]);
+    for (long long i = gtid; i < total; i += nthreads) {
+      const int r = static_cast<int>(i / groups);
+      const int c8 = static_cast<int>(i - static_cast<long long>(r) * groups) * 8;
+      uint4 part[8];
+#pragma unroll
+      for (int src = 0; src < kRowMaxWorld; ++src)
+        if (src < a.world)
+          part[src] = __ldcg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.P.p[src]) +
+                                                            (row0 + r) * a.ldp + c8));
+      const uint4 o = rb_finish<T>(part, a.world, bias, R, (row0 + r) * a.ldr + c8, c8);
+      *reinterpret_cast<uint4*>(Y + (row0 + r) * a.ldy + c8) = o;
+      __stcg(reinterpret_cast<uint4*>(Sown + (srow0 + r) * static_cast<long long>(a.N) + c8), o);
+    }
+    // The last CTA to finish announces the slab to every rank.
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence_system();
+      int* const ctr = a.F.p[a.rank] + row_counter(a.a_chunk);
+      if (atomicAdd(ctr, 1) == static_cast<int>(gridDim.x) - 1) {
+        atomicExch(ctr, 0);
+        __threadfence_system();
+        for (int s = 0; s < a.world; ++s)
+          st_release_sys(a.F.p[s] + row_red_flag(a.a_chunk, a.rank), a.epoch);
+      }
+    }
+  }
+
+  if (a.b_rows > 0) {
+    const int ok = tid == 0
+        ? (row_wait_flags(a.F.p[a.rank], row_red_flag(a.b_chunk, 0), a.world, a.rank, a.epoch) ? 1 : 0)
+        : 1;
+    if (!__syncthreads_and(ok)) return;
+    const int slab = a.b_rows / a.world;
+    const long long srow0 = a.slab_base + a.b_row0 / a.world;
+    const long long per_src = static_cast<long long>(slab) * groups;
+    const long long total = per_src * (a.world - 1);
+    constexpr int kUnroll = 4;
+    for (long long i0 = gtid; i0 < total; i0 += kUnroll * nthreads) {
+      uint4 v[kUnroll];
+      long long dst[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const long long i = i0 + u * nthreads;
+        dst[u] = -1;
+        if (i < total) {
+          int k = static_cast<int>(i / per_src);
+          const long long j = i - k * per_src;
+          const int src = k + (k >= a.rank ? 1 : 0);
+          const int r = static_cast<int>(j / groups);
+          const int c8 = static_cast<int>(j - static_cast<long long>(r) * groups) * 8;
+          v[u] = __ldcg(reinterpret_cast<const uint4*>(
+              static_cast<const T*>(a.S.p[src]) + (srow0 + r) * static_cast<long long>(a.N) + c8));
+          dst[u] = (a.b_row0 + static_cast<long long>(src) * slab + r) * a.ldy + c8;
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u)
+        if (dst[u] >= 0) *reinterpret_cast<uint4*>(Y + dst[u]) = v[u];
+    }
+  }
 }
 
 }  // namespace dx

@@ -131,7 +131,7 @@ __device__ __forceinline__ bool decode_wait_written(const int* ctr, int target,
       if (*abort_flag) return false;
       if (global_timer_ns() - t0 > kWaitLimitNs) {
         *abort_flag = 1;
-        atomicOr(&g_device_status, 1);
+        report_timeout();
         return false;
       }
     }

@@ -17,9 +17,22 @@ namespace dx {
 // one translation unit (dx_api.cu), which owns this definition.
 __device__ int g_device_status = 0;
 
+// Host-mapped copy of the status word (pinned host memory the host library
+// maps once per device), or nullptr before that set-up.  The host reads it at
+// the start of every later call without synchronising, so a launch whose wait
+// ran out makes the next call on the device fail instead of passing silently.
+__device__ int* g_status_mirror = nullptr;
+
 // A wait gives up after this many nanoseconds of device time (~1 s).  Normal
 // waits in these kernels last micro-seconds.
 constexpr uint64_t kWaitLimitNs = 1000ull * 1000ull * 1000ull;
+
+// Records a wait that ran out in the status word and its host-mapped copy.
+__device__ __forceinline__ void report_timeout() {
+  atomicOr(&g_device_status, 1);
+  int* const mirror = *static_cast<int* volatile*>(&g_status_mirror);
+  if (mirror != nullptr) atomicOr_system(mirror, 1);
+}
 
 __device__ __forceinline__ uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
@@ -77,7 +90,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatil
       if (*abort_flag) return false;
       if (global_timer_ns() - t0 > kWaitLimitNs) {
         *abort_flag = 1;
-        atomicOr(&g_device_status, 1);
+        report_timeout();
         return false;
       }
     }
@@ -90,7 +103,7 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
   const uint64_t t0 = global_timer_ns();
   while (!mbar_try_wait(bar, parity)) {
     if (global_timer_ns() - t0 > kWaitLimitNs) {
-      atomicOr(&g_device_status, 1);
+      report_timeout();
       return false;
     }
   }

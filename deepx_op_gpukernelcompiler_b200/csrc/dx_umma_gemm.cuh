@@ -398,7 +398,7 @@ __device__ __forceinline__ bool wait_counter(const int* ctr, int target, volatil
       if (*abort_flag) return false;
       if (global_timer_ns() - t0 > kWaitLimitNs) {
         *abort_flag = 1;
-        atomicOr(&g_device_status, 1);
+        report_timeout();
         return false;
       }
     }

@@ -27,6 +27,7 @@ from __future__ import annotations
 
 import torch
 
+from . import _native
 from .fusion import ACTIVATION_PT, classify
 from .kernel_b200 import make_linear_kernel
 from .kvfunc import read_func
@@ -183,4 +184,10 @@ def compile_and_test(kv, func_path: str, fusion: str = "b200", shape: dict | Non
     diff = (out.float() - ref.float()).abs().max().item()
     tl_ms = _time_ms(run, n_iter, warmup)
     pt_ms = _time_ms(ref_fn, n_iter, 0)
+    # A launch whose bounded wait ran out leaves an incomplete output; the
+    # timing loop has synchronised, so the status word is final here.
+    status = _native.device_status(torch.cuda.current_stream().cuda_stream)
+    if status:
+        return CompileResult(False, diff, tl_ms, pt_ms,
+                             f"device status {status}: a kernel gave up a bounded wait")
     return CompileResult(diff < 0.5, diff, tl_ms, pt_ms)

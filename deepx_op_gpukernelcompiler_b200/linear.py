@@ -380,3 +380,31 @@ def reduce_broadcast(partial: torch.Tensor, p_ptrs, rank: int, rows_per_rank: in
             _ld(residual) if residual is not None else 0, _ptr_array(y_ptrs), ldy,
             DTYPE_CODES[partial.dtype], stream)
     nat.check("dx_reduce_broadcast", rc)
+
+
+def row_flag_words() -> int:
+    """int32 flag words each rank's flag buffer needs for row_reduce."""
+    return int(nat.load().dx_row_flag_words())
+
+
+def row_reduce(p_ptrs, s_ptrs, f_ptrs, rank: int, M: int, N: int, ldp: int,
+               reduce_chunk: tuple[int, int, int] | None,
+               gather_chunk: tuple[int, int, int] | None,
+               bias: torch.Tensor | None, residual: torch.Tensor | None, out: torch.Tensor,
+               epoch: int, dtype: torch.dtype, stream: int, grid: int = 0) -> None:
+    """One call of the chunked row-parallel reduction (dx_row_reduce) on
+    `stream`: reduce-scatter of `reduce_chunk` and all-gather of
+    `gather_chunk`, each given as (first row, rows, chunk index) or None.
+    `p_ptrs` / `s_ptrs` / `f_ptrs` are the peer-mapped addresses of every
+    rank's partial, slab and flag buffers; `out` is this rank's output."""
+    world = len(p_ptrs)
+    a0, an, ac = reduce_chunk if reduce_chunk is not None else (0, 0, 0)
+    b0, bn, bc = gather_chunk if gather_chunk is not None else (0, 0, 0)
+    rc = nat.load().dx_row_reduce(
+        _ptr_array(p_ptrs), _ptr_array(s_ptrs), _ptr_array(f_ptrs), world, rank, M, N, ldp,
+        a0, an, ac, b0, bn, bc,
+        bias.data_ptr() if bias is not None else None,
+        residual.data_ptr() if residual is not None else None,
+        _ld(residual) if residual is not None else 0, out.data_ptr(), _ld(out), epoch, grid,
+        DTYPE_CODES[dtype], stream)
+    nat.check("dx_row_reduce", rc)

@@ -11,15 +11,18 @@ standard way, one process per GPU over ``torch.distributed`` (NCCL on GPUs):
   W1 column-sharded, W2 row-sharded with the same hidden slice, so
   H_r = act(X W1_r + b1_r) stays local and Y = sum_r H_r W2_r needs one
   all-reduce.  Two implementations:
-    - ``mode="fused"`` (GPUs, default): the second GEMM writes its partial
-      into a peer-mapped (symmetric-memory) buffer; after a device barrier
-      each rank reads its row slab from every rank's partial over NVLink,
-      sums in rank order, adds b2 and X once and writes the finished rows
-      into every rank's output (one engine kernel, dx_reduce_broadcast) —
-      no NCCL on the path;
+    - ``mode="fused"`` (GPUs, default): the rows are cut into chunks; each
+      chunk's two GEMMs run on the main stream, the second writing its
+      partial into a peer-mapped (symmetric-memory) buffer, and one engine
+      kernel (dx_row_reduce) on a side stream reduce-scatters that chunk
+      over NVLink (peer loads, rank order, b2 and X added once) and gathers
+      the previous chunk, while the next chunk's GEMMs compute — no NCCL on
+      the path; the output is a buffer the caller owns;
     - ``mode="nccl"``: b2 and X are fused into rank 0's second launch and
       Y is summed with NCCL all-reduce (in M-chunks issued asynchronously
-      when ``chunks > 1``).  This mode also runs on CPU ranks (gloo).
+      when ``chunks > 1``).  This mode also runs on CPU ranks (gloo), and
+      takes the shapes the fused mode cannot (M not a multiple of the world
+      size — e.g. decode rows — N not a multiple of 8, fp32).
 * ``ParallelGatedFFN`` — the ``ffn_gated`` chain (fusion.py:44-46)
   Y = (act(X Wg + bg) * (X Wu + bu)) Wo + bo: Wg and Wu column-sharded on
   the same hidden slice (one gated dual-GEMM launch per rank), Wo
@@ -108,30 +111,80 @@ class ColumnParallelLinear:
         return torch.cat([p[:, :sz] for p, sz in zip(parts, sizes)], dim=1)
 
 
+MAX_ROW_CHUNKS = 64  # chunk indices dx_row_reduce keeps flags for
+
+
+def row_chunks(M: int, world: int, chunks: int) -> list[tuple[int, int]]:
+    """(first row, rows) of the row chunks of the overlapped reduction: up to
+    `chunks` near-equal chunks whose starts and sizes are multiples of
+    32 * world when M allows (so every rank's slab of a chunk is a whole
+    number of 32-row groups), else of world."""
+    if world <= 0 or M % world:
+        raise ValueError(f"M ({M}) must be a multiple of the world size ({world})")
+    unit = world * 32 if M % (world * 32) == 0 else world
+    units = M // unit
+    n = max(1, min(int(chunks), units, MAX_ROW_CHUNKS))
+    edges = [(i * units // n) * unit for i in range(n + 1)]
+    return [(a, b - a) for a, b in zip(edges, edges[1:]) if b > a]
+
+
+def first_groups(n_chunks: int, groups: int | None) -> list[tuple[int, int]]:
+    """[start, end) chunk-index ranges that one launch of the first GEMM
+    covers: `groups` near-equal runs of consecutive chunks (None: one per
+    chunk)."""
+    g = n_chunks if groups is None else max(1, min(int(groups), n_chunks))
+    edges = [i * n_chunks // g for i in range(g + 1)]
+    return [(a, b) for a, b in zip(edges, edges[1:]) if b > a]
+
+
 class _RowParallelBuffers:
-    """Symmetric (peer-mapped) partial and output buffers of one shape."""
+    """Peer-mapped (symmetric-memory) buffers of the overlapped reduction for
+    one (M, N, dtype): every rank's partial [M, N], slab buffer
+    [2 * M / world, N] and flag words, plus the side stream the reduction
+    runs on."""
 
     def __init__(self, M: int, N: int, dtype, device, group):
         import torch.distributed._symmetric_memory as symm_mem
+
+        from .linear import row_flag_words
         world = dist.get_world_size(group)
-        if M % world:
-            raise ValueError(f"fused row-parallel needs M ({M}) divisible by world ({world})")
         self.key = (M, N, dtype)
-        self.rows_per_rank = M // world
         self.part = symm_mem.empty(M, N, dtype=dtype, device=device)
-        self.out = symm_mem.empty(M, N, dtype=dtype, device=device)
+        self.slab = symm_mem.empty(2 * M // world, N, dtype=dtype, device=device)
+        self.flags = symm_mem.empty(row_flag_words(), dtype=torch.int32, device=device)
+        self.flags.zero_()
+        torch.cuda.current_stream(device).synchronize()
         pg = group if group is not None else dist.group.WORLD
-        self.h_part = symm_mem.rendezvous(self.part, pg)
-        self.h_out = symm_mem.rendezvous(self.out, pg)
-        self.part_ptrs = list(self.h_part.buffer_ptrs)
-        self.out_ptrs = list(self.h_out.buffer_ptrs)
+        self.handles = [symm_mem.rendezvous(t, pg) for t in (self.part, self.slab, self.flags)]
+        self.part_ptrs, self.slab_ptrs, self.flag_ptrs = (list(h.buffer_ptrs)
+                                                          for h in self.handles)
+        # Every rank's flags are zero before any peer stamps them.
+        dist.barrier(group=group)
+        self.epoch = 0
+        self.stream = torch.cuda.Stream(device)
 
 
 class _RowParallelOutput:
     """The row-parallel second GEMM and its reduction, shared by the FFN
-    classes: Y = sum_r H_r W2_r + b2 (+ R), W2_r this rank's row shard."""
+    classes: Y = sum_r H_r W2_r + b2 (+ R), W2_r this rank's row shard.
 
-    def _init_output(self, W2_shard, b2_full, group, linear_fn, chunks, mode, on_gpu):
+    ``mode="fused"`` (the default on GPUs with world > 1): the engine's
+    overlapped reduction.  The rows are cut into ``chunks`` chunks; on the
+    main stream each chunk's first GEMM (grouped into ``first_chunks``
+    launches) and second GEMM run in turn, the second writing its partial
+    into a peer-mapped buffer; after each, one dx_row_reduce launch on a side
+    stream reduce-scatters that chunk over NVLink (peer loads, rank order,
+    b2 and R added once) and gathers the previous chunk's slabs, concurrently
+    with the next chunk's GEMMs.  The result lands in a buffer the caller
+    owns (``out``, or a new tensor).  Shapes it cannot take (M not a
+    multiple of the world size, N not a multiple of 8, fp32, world > 8) run
+    the NCCL path instead.
+    ``mode="nccl"``: the whole first GEMM, then the second in ``chunks``
+    row chunks, each summed by an asynchronous NCCL all-reduce (b2 and R
+    fused into rank 0's launch).  Also runs on CPU ranks (gloo)."""
+
+    def _init_output(self, W2_shard, b2_full, group, linear_fn, chunks, mode, on_gpu,
+                     first_chunks=None):
         self.group = group
         self.world, self.rank = _group_info(group)
         self.mode = mode or ("fused" if (linear_fn is None and on_gpu and self.world > 1)
@@ -141,12 +194,29 @@ class _RowParallelOutput:
         self.b2_all = b2_full.contiguous() if b2_full is not None else None
         self.b2 = self.b2_all if self.rank == 0 else None
         self.linear_fn = linear_fn or _default_linear()
-        self.chunks = max(1, int(chunks))
+        self.chunks = max(1, int(chunks)) if chunks is not None else (
+            4 if self.mode == "fused" else 1)
+        self.first_chunks = first_chunks
+        self.last_path = None  # "fused" or "nccl": what the last call ran
 
-    def _row_parallel(self, H: torch.Tensor, R: torch.Tensor | None,
-                      out: torch.Tensor | None) -> torch.Tensor:
-        if self.mode == "fused":
-            return self._row_parallel_fused(H, R, out)
+    def _fused_ok(self, M: int, N: int, dtype) -> bool:
+        return (self.mode == "fused" and 1 < self.world <= 8 and M % self.world == 0
+                and N % 8 == 0 and dtype in (torch.float16, torch.bfloat16))
+
+    def _run(self, first, M: int, H: torch.Tensor, R: torch.Tensor | None,
+             out: torch.Tensor | None) -> torch.Tensor:
+        """Y for rows [0, M): `first(r0, r1)` fills H[r0:r1] (the chain's
+        first GEMM), then the row-parallel second GEMM and its reduction."""
+        N = self.W2.shape[1]
+        if self._fused_ok(M, N, H.dtype):
+            self.last_path = "fused"
+            return self._run_overlapped(first, M, H, R, out)
+        self.last_path = "nccl"
+        first(0, M)
+        return self._row_parallel_nccl(H, R, out)
+
+    def _row_parallel_nccl(self, H: torch.Tensor, R: torch.Tensor | None,
+                           out: torch.Tensor | None) -> torch.Tensor:
         M = H.shape[0]
         Y = out if out is not None else torch.empty((M, self.W2.shape[1]), dtype=H.dtype,
                                                     device=H.device)
@@ -165,34 +235,47 @@ class _RowParallelOutput:
             h.wait()
         return Y
 
-    def _row_parallel_fused(self, H: torch.Tensor, R: torch.Tensor | None,
-                            out: torch.Tensor | None) -> torch.Tensor:
-        """Y = sum_r H_r W2_r + b2 (+ R): local partial, then reduce-broadcast."""
-        from .linear import fused_linear, reduce_broadcast
-        M, N = H.shape[0], self.W2.shape[1]
+    def _run_overlapped(self, first, M: int, H: torch.Tensor, R: torch.Tensor | None,
+                        out: torch.Tensor | None) -> torch.Tensor:
+        from .linear import row_reduce
+        N = self.W2.shape[1]
+        dev = H.device
         key = (M, N, H.dtype)
         if self._bufs is None or self._bufs.key != key:
-            self._bufs = _RowParallelBuffers(M, N, H.dtype, H.device, self.group)
+            self._bufs = None
+            self._bufs = _RowParallelBuffers(M, N, H.dtype, dev, self.group)
         bufs = self._bufs
-        rpr = bufs.rows_per_rank
-        fused_linear(H, self.W2, None, None, out=bufs.part)
-        bufs.h_part.barrier(channel=0)  # every rank's partial is complete
-        reduce_broadcast(bufs.part, bufs.part_ptrs, self.rank, rpr, self.b2_all, R,
-                         bufs.out_ptrs, N)
-        # Every rank's rows have landed, and no rank still reads a partial
-        # that the next call will overwrite.
-        bufs.h_out.barrier(channel=1)
-        if out is None:
-            return bufs.out
-        out.copy_(bufs.out)
-        return out
+        Y = out if out is not None else torch.empty((M, N), dtype=H.dtype, device=dev)
+        chunks = row_chunks(M, self.world, self.chunks)
+        starts = {a: b for a, b in first_groups(len(chunks), self.first_chunks)}
+        main = torch.cuda.current_stream(dev)
+        side = bufs.stream
+        bufs.epoch += 1
+        common = dict(rank=self.rank, M=M, N=N, ldp=N, bias=self.b2_all, residual=R, out=Y,
+                      epoch=bufs.epoch, dtype=H.dtype, stream=side.cuda_stream)
+        ptrs = (bufs.part_ptrs, bufs.slab_ptrs, bufs.flag_ptrs)
+        side.wait_stream(main)  # Y, R and b2 are ready; earlier users of Y are done
+        prev = None
+        for j, (r0, rn) in enumerate(chunks):
+            if j in starts:
+                g0 = chunks[j][0]
+                g_last = chunks[starts[j] - 1]
+                first(g0, g_last[0] + g_last[1])
+            self.linear_fn(H[r0:r0 + rn], self.W2, None, None, out=bufs.part[r0:r0 + rn])
+            side.wait_stream(main)  # this chunk of the local partial is complete
+            row_reduce(*ptrs, reduce_chunk=(r0, rn, j), gather_chunk=prev, **common)
+            prev = (r0, rn, j)
+        row_reduce(*ptrs, reduce_chunk=None, gather_chunk=prev, **common)
+        main.wait_stream(side)
+        return Y
 
 
 class ParallelMLP(_RowParallelOutput):
     """Y = act(X W1 + b1) W2 + b2 + X with W1 column- and W2 row-sharded."""
 
     def __init__(self, W1_full, b1_full, W2_full, b2_full, activation="gelu", group=None,
-                 linear_fn=None, chunks: int = 1, align: int = 64, mode: str | None = None):
+                 linear_fn=None, chunks: int | None = None, align: int = 64,
+                 mode: str | None = None, first_chunks: int | None = None):
         world, rank = _group_info(group)
         hidden = W1_full.shape[1]
         if W2_full.shape[0] != hidden:
@@ -202,22 +285,29 @@ class ParallelMLP(_RowParallelOutput):
         self.b1 = b1_full[self.h0:self.h1].contiguous() if b1_full is not None else None
         self.activation = activation
         self._init_output(W2_full[self.h0:self.h1, :].contiguous(), b2_full, group, linear_fn,
-                          chunks, mode, on_gpu=W1_full.is_cuda)
+                          chunks, mode, on_gpu=W1_full.is_cuda, first_chunks=first_chunks)
 
     @classmethod
     def from_shards(cls, W1_shard, b1_shard, W2_shard, b2_full, activation="gelu", group=None,
-                    linear_fn=None, chunks: int = 1, mode: str | None = None):
+                    linear_fn=None, chunks: int | None = None, mode: str | None = None,
+                    first_chunks: int | None = None):
         self = cls.__new__(cls)
         self.W1, self.b1 = W1_shard, b1_shard
         self.activation = activation
         self._init_output(W2_shard, b2_full, group, linear_fn, chunks, mode,
-                          on_gpu=W1_shard.is_cuda)
+                          on_gpu=W1_shard.is_cuda, first_chunks=first_chunks)
         return self
 
     def __call__(self, X: torch.Tensor, hidden: torch.Tensor | None = None,
                  out: torch.Tensor | None = None) -> torch.Tensor:
-        H = self.linear_fn(X, self.W1, self.b1, self.activation, out=hidden)
-        return self._row_parallel(H, X, out)
+        M = X.shape[0]
+        H = hidden if hidden is not None else torch.empty(
+            (M, self.W1.shape[1]), dtype=X.dtype, device=X.device)
+
+        def first(r0: int, r1: int) -> None:
+            self.linear_fn(X[r0:r1], self.W1, self.b1, self.activation, out=H[r0:r1])
+
+        return self._run(first, M, H, X, out)
 
 
 class ParallelGatedFFN(_RowParallelOutput):
@@ -225,8 +315,8 @@ class ParallelGatedFFN(_RowParallelOutput):
     row-sharded on the same hidden slice (the ``ffn_gated`` chain)."""
 
     def __init__(self, Wg_full, bg_full, Wu_full, bu_full, Wo_full, bo_full, activation="silu",
-                 group=None, gated_fn=None, linear_fn=None, chunks: int = 1, align: int = 64,
-                 mode: str | None = None):
+                 group=None, gated_fn=None, linear_fn=None, chunks: int | None = None,
+                 align: int = 64, mode: str | None = None, first_chunks: int | None = None):
         world, rank = _group_info(group)
         hidden = Wg_full.shape[1]
         if Wu_full.shape != Wg_full.shape or Wo_full.shape[0] != hidden:
@@ -238,27 +328,35 @@ class ParallelGatedFFN(_RowParallelOutput):
                           Wu_full[:, sl].contiguous(),
                           bu_full[sl].contiguous() if bu_full is not None else None,
                           Wo_full[sl, :].contiguous(), bo_full, activation, group, gated_fn,
-                          linear_fn, chunks, mode)
+                          linear_fn, chunks, mode, first_chunks)
         self.h0, self.h1 = h0, h1
 
     @classmethod
     def from_shards(cls, Wg_shard, bg_shard, Wu_shard, bu_shard, Wo_shard, bo_full,
                     activation="silu", group=None, gated_fn=None, linear_fn=None,
-                    chunks: int = 1, mode: str | None = None):
+                    chunks: int | None = None, mode: str | None = None,
+                    first_chunks: int | None = None):
         self = cls.__new__(cls)
         self._init_shards(Wg_shard, bg_shard, Wu_shard, bu_shard, Wo_shard, bo_full, activation,
-                          group, gated_fn, linear_fn, chunks, mode)
+                          group, gated_fn, linear_fn, chunks, mode, first_chunks)
         return self
 
     def _init_shards(self, Wg, bg, Wu, bu, Wo, bo_full, activation, group, gated_fn, linear_fn,
-                     chunks, mode):
+                     chunks, mode, first_chunks=None):
         self.Wg, self.bg, self.Wu, self.bu = Wg, bg, Wu, bu
         self.activation = activation
         self.gated_fn = gated_fn or _default_gated()
         self._init_output(Wo, bo_full, group, linear_fn, chunks, mode,
-                          on_gpu=Wg.is_cuda and gated_fn is None)
+                          on_gpu=Wg.is_cuda and gated_fn is None, first_chunks=first_chunks)
 
     def __call__(self, X: torch.Tensor, hidden: torch.Tensor | None = None,
                  out: torch.Tensor | None = None) -> torch.Tensor:
-        H = self.gated_fn(X, self.Wg, self.Wu, self.bg, self.bu, self.activation, out=hidden)
-        return self._row_parallel(H, None, out)
+        M = X.shape[0]
+        H = hidden if hidden is not None else torch.empty(
+            (M, self.Wg.shape[1]), dtype=X.dtype, device=X.device)
+
+        def first(r0: int, r1: int) -> None:
+            self.gated_fn(X[r0:r1], self.Wg, self.Wu, self.bg, self.bu, self.activation,
+                          out=H[r0:r1])
+
+        return self._run(first, M, H, None, out)

@@ -121,6 +121,45 @@ int dx_reduce_broadcast(void* const* P, int world, int rank, int64_t rows_per_ra
                         int64_t ldp, const void* bias, const void* R, int64_t ldr,
                         void* const* Y, int64_t ldy, int dtype, void* stream);
 
+/*
+ * Chunked, overlapped reduction of a row-parallel linear over `world` ranks
+ * (no reference counterpart: the reference is single-GPU, and fusion.py:42-43
+ * marks the two-layer FFN multi_kernel).  The second GEMM of the chain runs
+ * in row chunks; after chunk `a_chunk` (rows a_row0 .. a_row0 + a_rows) of
+ * the local partial is complete, one call on a side stream — while the next
+ * chunk's GEMMs run on the caller's main stream — does
+ *   phase A: announces the local partial chunk to every rank, waits until
+ *     every rank's is complete, then sums this rank's slab of the chunk (rows
+ *     a_row0 + rank * a_rows / world, a_rows / world of them) over all
+ *     partials P[s] in rank order in fp32, adds bias[N] and R once, rounds,
+ *     and writes the rows into Y and into its own slab buffer S[rank];
+ *   phase B: for the chunk b_row0 .. b_row0 + b_rows reduced by an earlier
+ *     call of the same step, waits until every rank has announced its slab
+ *     and copies the other ranks' slabs from S[s] into Y.
+ * a_rows = 0 or b_rows = 0 skips a phase; a step ends with a call that only
+ * gathers its last chunk.  Only this rank writes Y, so Y is any caller-owned
+ * device buffer [M][ldy].  P[s] ([M][ldp]), S[s] ([2 * M / world][N]) and
+ * F[s] (dx_row_flag_words() int32 words, zeroed once before first use) are
+ * rank s's buffers, mapped so every rank reaches them over NVLink.  `epoch`
+ * numbers the step: the same positive value on every rank, one larger per
+ * step; flags carry it, and its parity selects the half of S the step uses,
+ * so a slab is never overwritten while a peer may still read it.  The caller
+ * keeps steps apart on each rank: the main stream waits for the step's last
+ * call before reusing P, and chunk indices of one step are distinct (< 64).
+ * Chunk starts and sizes are multiples of `world`; N % 8 == 0; fp16/bf16.
+ * grid <= 0 uses one CTA per SM.  Waits are bounded (2 s): on expiry the
+ * call's kernel sets DX_DEVICE_STATUS_TIMEOUT and returns.
+ */
+int dx_row_reduce(void* const* P, void* const* S, int* const* F, int world, int rank,
+                  int64_t M, int64_t N, int64_t ldp,
+                  int64_t a_row0, int64_t a_rows, int a_chunk,
+                  int64_t b_row0, int64_t b_rows, int b_chunk,
+                  const void* bias, const void* R, int64_t ldr, void* Y, int64_t ldy,
+                  int epoch, int grid, int dtype, void* stream);
+
+/* int32 flag words dx_row_reduce needs in each rank's F buffer. */
+int dx_row_flag_words(void);
+
 /* Skinny-M (decode) fused linear that allocates nothing.  No counterpart in
  * the reference: it exists for callers that cannot allocate device memory at
  * call time — a runtime whose own heap manager owns every device buffer and

@@ -16,3 +16,4 @@ from .fused_linear import (  # noqa: F401
     mlp_residual_f32,
     mlp_residual_f64,
 )
+from . import torch_cpu  # noqa: F401,E402

@@ -1,24 +1,66 @@
 """Worker for tests/test_gpu_multi.py: one process per GPU under torchrun.
 
-Checks, on every rank, the sharded engine against the single-GPU engine on
-the same seeded inputs: the column-parallel layer (gathered), the
-column -> row MLP and the column -> row gated FFN, each with the NVLink
-reduce-broadcast and with NCCL.  Exits non-zero on a mismatch.
+Checks, on every rank, the sharded engine against the fp64 CPU oracle (the
+reference expression act(a @ b + bias), kernel.py:64-66, restated in
+oracle/) on row blocks of the same seeded inputs:
+
+* the column-parallel layer (gathered);
+* the column -> row MLP, Y = GELU(X W1 + b1) W2 + b2 + X, with the
+  overlapped NVLink reduction (1, 3 and 4 row chunks, the first GEMM grouped
+  or not) and with NCCL;
+* the column -> row gated FFN, both reductions;
+* a row count the overlapped reduction cannot take (M not a multiple of the
+  world size, as decode rows are): it must run the NCCL path and still be
+  right;
+* output ownership: a second call must not overwrite the first call's Y.
+
+Bit equality between the two reductions is not expected (NCCL sums in its own
+order); each is held to the bf16 tolerance rtol = atol = 2e-2 against the
+oracle.  Exits non-zero on any mismatch.
 """
 import os
 import sys
 from datetime import timedelta
 from pathlib import Path
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
 sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
 
-from deepx_op_gpukernelcompiler_b200 import (_native, fused_linear, gated_ffn,  # noqa: E402
-                                             mlp_residual)
+import oracle  # noqa: E402
+from deepx_op_gpukernelcompiler_b200 import _native  # noqa: E402
 from deepx_op_gpukernelcompiler_b200.shard import (ColumnParallelLinear,  # noqa: E402
                                                    ParallelGatedFFN, ParallelMLP)
+
+TOL = 2e-2
+
+
+def row_blocks(M: int, rows: int = 16) -> list[tuple[int, int]]:
+    """First, middle (straddling a slab boundary) and last row blocks."""
+    mid = max(0, M // 2 - rows // 2)
+    blocks = [(0, min(rows, M)), (mid, min(M, mid + rows)), (max(0, M - rows), M)]
+    return sorted(set(blocks))
+
+
+def cpu(t):
+    return t.detach().float().cpu().numpy()
+
+
+def compare(name, got, want_fn, M, failures, blocks=None):
+    """got: [M, N] device tensor; want_fn(r0, r1) -> fp64 oracle rows."""
+    g = cpu(got)
+    worst = 0.0
+    for r0, r1 in (blocks or row_blocks(M)):
+        want = want_fn(r0, r1)
+        err = np.abs(g[r0:r1] - want)
+        bad = err > TOL + TOL * np.abs(want)
+        worst = max(worst, float(err.max()) if err.size else 0.0)
+        if bad.any():
+            failures.append(f"{name}: rows {r0}..{r1} off by up to {float(err.max()):.4g}")
+            return worst
+    return worst
 
 
 def main() -> int:
@@ -27,7 +69,7 @@ def main() -> int:
     dev = torch.device("cuda", local)
     dist.init_process_group("nccl", timeout=timedelta(seconds=60), device_id=dev)
     rank, world = dist.get_rank(), dist.get_world_size()
-    failures = []
+    failures, report = [], {}
     try:
         g = torch.Generator(device=dev)
         g.manual_seed(7)
@@ -35,47 +77,84 @@ def main() -> int:
         X = torch.randn(M, K, generator=g, device=dev).bfloat16()
         W = (torch.randn(K, N, generator=g, device=dev) / K ** 0.5).bfloat16()
         b = (torch.rand(N, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
-        full = fused_linear(X, W, b, "silu").float()
+        Xc, Wc, bc = cpu(X), cpu(W), cpu(b)
         col = ColumnParallelLinear(W, b, "silu", gather_output=True)
-        got = col(X).float()
+        got = col(X)
         torch.cuda.synchronize()
-        # A shard may be scheduled with a different K split of its last tiles
-        # than the full problem, so compare within the bf16 tolerance.
-        err = (got - full).abs()
-        if bool((err > 2e-2 + 2e-2 * full.abs()).any()):
-            failures.append(f"column-parallel differs: max {err.max().item():.4g}")
+        report["column"] = compare(
+            "column-parallel", got,
+            lambda r0, r1: oracle.fused_linear_f64(Xc[r0:r1], Wc, bc, "silu"), M, failures)
 
         H = 4096
         W1 = (torch.randn(K, H, generator=g, device=dev) / K ** 0.5).bfloat16()
         b1 = (torch.rand(H, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
         W2 = (torch.randn(H, K, generator=g, device=dev) / H ** 0.5).bfloat16()
         b2 = (torch.rand(K, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
-        ref = mlp_residual(X, W1, b1, W2, b2, "gelu").float()
-        for mode, chunks in (("nccl", 1), ("nccl", 4), ("fused", 1)):
-            mlp = ParallelMLP(W1, b1, W2, b2, "gelu", chunks=chunks, mode=mode)
-            for rep in range(2):  # the fused mode reuses its peer buffers
-                out = mlp(X).float()
-                torch.cuda.synchronize()
-                err = (out - ref).abs()
-                tol = 2e-2 + 2e-2 * ref.abs()
-                if bool((err > tol).any()):
-                    failures.append(f"MLP ({mode}, chunks={chunks}, call {rep}) off by up to "
-                                    f"{err.max().item():.4g}")
+        W1c, b1c, W2c, b2c = cpu(W1), cpu(b1), cpu(W2), cpu(b2)
+        cache = {}
+
+        def mlp_ref(Xh):
+            def rows(r0, r1):
+                key = (id(Xh), r0, r1)
+                if key not in cache:
+                    cache[key] = oracle.mlp_residual_f64(Xh[r0:r1], W1c, b1c, W2c, b2c, "gelu")
+                return cache[key]
+            return rows
+
+        ref_rows = mlp_ref(Xc)
+        for mode, chunks, first in (("nccl", 1, None), ("nccl", 4, None), ("fused", 1, None),
+                                    ("fused", 4, None), ("fused", 4, 2), ("fused", 3, 1)):
+            mlp = ParallelMLP(W1, b1, W2, b2, "gelu", chunks=chunks, mode=mode,
+                              first_chunks=first)
+            outs = []
+            for rep in range(3):  # the fused mode reuses its buffers and flips slab halves
+                outs.append(mlp(X))
+            torch.cuda.synchronize()
+            if mlp.last_path != mode:
+                failures.append(f"MLP {mode}: ran the {mlp.last_path} path")
+            for rep, out in enumerate(outs):
+                report[f"mlp_{mode}_c{chunks}_f{first}_{rep}"] = compare(
+                    f"MLP ({mode}, chunks={chunks}, first={first}, call {rep})", out, ref_rows,
+                    M, failures)
+
+        # Output ownership: a later call with other inputs leaves Y1 intact.
+        mlp = ParallelMLP(W1, b1, W2, b2, "gelu", mode="fused")
+        X2 = torch.randn(M, K, generator=g, device=dev).bfloat16()
+        Y1 = mlp(X)
+        Y1_copy = Y1.clone()
+        Y2 = mlp(X2)
+        torch.cuda.synchronize()
+        if Y1.data_ptr() == Y2.data_ptr() or not torch.equal(Y1, Y1_copy):
+            failures.append("MLP fused: a second call overwrote the first call's output")
+        report["mlp_second_input"] = compare("MLP fused, second input", Y2, mlp_ref(cpu(X2)), M,
+                                             failures)
+
+        # Rows the overlapped reduction cannot split evenly over the ranks.
+        m_odd = world + 1 if world > 1 else 3
+        Xo = X[:m_odd].contiguous()
+        mlp = ParallelMLP(W1, b1, W2, b2, "gelu", mode="fused")
+        out = mlp(Xo)
+        torch.cuda.synchronize()
+        if world > 1 and mlp.last_path != "nccl":
+            failures.append(f"MLP with M={m_odd}: expected the NCCL fallback")
+        report["mlp_odd_rows"] = compare(f"MLP M={m_odd}", out, mlp_ref(cpu(Xo)), m_odd,
+                                         failures, blocks=[(0, m_odd)])
 
         Wg = (torch.randn(K, H, generator=g, device=dev) / K ** 0.5).bfloat16()
         Wu = (torch.randn(K, H, generator=g, device=dev) / K ** 0.5).bfloat16()
         bg = (torch.rand(H, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
         bu = (torch.rand(H, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
-        ref = gated_ffn(X, Wg, bg, Wu, bu, W2, b2, "silu").float()
+        Wgc, Wuc, bgc, buc = cpu(Wg), cpu(Wu), cpu(bg), cpu(bu)
         for mode in ("nccl", "fused"):
             ffn = ParallelGatedFFN(Wg, bg, Wu, bu, W2, b2, "silu", mode=mode)
-            for rep in range(2):
-                out = ffn(X).float()
-                torch.cuda.synchronize()
-                err = (out - ref).abs()
-                if bool((err > 2e-2 + 2e-2 * ref.abs()).any()):
-                    failures.append(f"gated FFN ({mode}, call {rep}) off by up to "
-                                    f"{err.max().item():.4g}")
+            outs = [ffn(X) for _ in range(2)]
+            torch.cuda.synchronize()
+            for rep, out in enumerate(outs):
+                report[f"gated_{mode}_{rep}"] = compare(
+                    f"gated FFN ({mode}, call {rep})", out,
+                    lambda r0, r1: oracle.gated_ffn_f64(Xc[r0:r1], Wgc, bgc, Wuc, buc, W2c, b2c,
+                                                        "silu"),
+                    M, failures)
         status = _native.device_status(torch.cuda.current_stream(dev).cuda_stream)
         if status:
             failures.append(f"device status {status}")
@@ -84,6 +163,9 @@ def main() -> int:
         dist.destroy_process_group()
     for f in failures:
         print(f"rank {rank}/{world}: {f}", flush=True)
+    if rank == 0:
+        print("max |err| vs fp64 oracle: " +
+              ", ".join(f"{k}={v:.3g}" for k, v in report.items()), flush=True)
     return 1 if failures else 0
 
 

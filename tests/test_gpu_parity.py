@@ -398,3 +398,28 @@ def test_bounded_wait_reports_timeout_and_context_survives():
     torch.cuda.synchronize()
     _assert_close(Y, oracle.fused_linear_f64(X, W, b, "silu"), torch.bfloat16, "after timeout")
     _status_clean()
+
+
+def test_timeout_makes_the_next_call_raise():
+    """A launch whose bounded wait ran out is reported by the next call on
+    the device (through the status word's host-mapped copy, no added
+    synchronisation): fused_linear raises DX_ERR_DEVICE_TIMEOUT until
+    dx_device_status has read and cleared the condition."""
+    lib = nat.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    assert nat.device_status(stream) == 0
+    X, W, b, _ = _rand(300, 256, 512, torch.bfloat16, seed=78)
+    Xd, Wd, bd = X.to(DEV), W.to(DEV), b.to(DEV)
+    fused_linear(Xd, Wd, bd, "silu")  # installs the host-mapped copy on this device
+    flag = torch.zeros(1, dtype=torch.int32, device=DEV)
+    nat.check("dx_selftest_bounded_wait", lib.dx_selftest_bounded_wait(flag.data_ptr(), stream))
+    torch.cuda.synchronize()  # the wait has given up by now
+    with pytest.raises(nat.NativeError) as info:
+        fused_linear(Xd, Wd, bd, "silu")
+    assert info.value.code == nat.DX_ERR_DEVICE_TIMEOUT
+    assert "bounded wait" in str(info.value)
+    assert nat.device_status(stream) == nat.DX_DEVICE_STATUS_TIMEOUT  # read and clear
+    Y = fused_linear(Xd, Wd, bd, "silu")
+    torch.cuda.synchronize()
+    _assert_close(Y, oracle.fused_linear_f64(X, W, b, "silu"), torch.bfloat16, "after clear")
+    _status_clean()

@@ -36,6 +36,20 @@ F32 = {"linear": oracle.fused_linear_f32, "mlp": oracle.mlp_residual_f32,
        "gated": oracle.gated_linear_f32, "ffn_gated": oracle.gated_ffn_f32}
 
 
+def _torch_linear(X, W, b, act, residual=None):
+    return oracle.torch_cpu.fused_linear(X, W, b, act, residual=residual).numpy()
+
+
+@pytest.mark.parametrize("case", [c for c in cases() if not c.get("gated")],
+                         ids=lambda c: c["name"])
+def test_oracle_torch_cpu_matches_reference(case):
+    """The torch-CPU restatement timed as the CPU baseline."""
+    fn = {"linear": _torch_linear,
+          "mlp": lambda *a: oracle.torch_cpu.mlp_residual(*a).numpy()}
+    got, ref = _run(case, fn)
+    np.testing.assert_allclose(got, ref.numpy(), rtol=ORACLE_RTOL, atol=ORACLE_ATOL)
+
+
 @pytest.mark.parametrize("case", cases(), ids=lambda c: c["name"])
 def test_oracle_f64_matches_reference(case):
     got, ref = _run(case, F64)
