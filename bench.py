@@ -665,7 +665,9 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
     import torch
 
     import oracle
-    from deepx_op_gpukernelcompiler_b200.shard import ParallelGatedFFN, ParallelMLP, shard_bounds
+    from deepx_op_gpukernelcompiler_b200.shard import (ParallelGatedFFN, ParallelMLP,
+                                                       first_groups, row_chunks, row_schedule,
+                                                       shard_bounds)
     from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS
 
     out = {}
@@ -710,7 +712,7 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
     else:
         mlp = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, mode="fused")
         sweep = {}
-        for chunks, first in ((4, None), (4, 2), (8, 2), (8, 4), (2, None)):
+        for chunks, first in ((4, None), (4, 2), (8, 4), (8, 2), (16, 4), (2, None)):
             mlp.chunks, mlp.first_chunks = chunks, first
             ms = time_run(lambda: mlp(X, hidden=H, out=Yo), 1500.0)
             sweep[f"chunks={chunks},first={first or chunks}"] = round(ms, 4)
@@ -721,13 +723,15 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
         assert mlp.last_path == "fused"
         parity["mlp_fused"] = _row_parallel_parity(X, first_ref, W2, b2, True, Yo, world, dev)
         tf = w.flops / (ms * 1e-3) / 1e12
+        n_ch = len(row_chunks(w.M, world, chunks))
+        plan = row_schedule(n_ch, first_groups(n_ch, first))
         out[w.name] = {"value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
                        "frac_of_peak": round(tf / world / tflops_peak, 4),
-                       "parallelism": f"column->row x{world}, reduction overlapped with the "
-                                      f"GEMMs ({chunks} row chunks, first GEMM in {first} "
-                                      "launches; dx_row_reduce over NVLink)",
+                       "parallelism": f"column->row x{world}, reduction carried by the GEMM "
+                                      f"launches ({chunks} row chunks, first GEMM in {first} "
+                                      "launches; NVLink peer loads, dx_row_reduce_job)",
                        "chunking_ms": sweep,
-                       "gpu_launches_per_step": chunks + first + chunks + 1}
+                       "gpu_launches_per_step": len(plan)}
         # The same chain with an NCCL all-reduce of Y in 4 asynchronous chunks.
         mlp_n = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, chunks=4, mode="nccl")
         Yn = torch.empty_like(Yo)
@@ -763,9 +767,11 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
         run = lambda: gated_ffn(X, Wg, bg, Wu, bu, Wo, bo, "silu", hidden=Hg, out=Yg)  # noqa
         launches = 2
     else:
-        ffn = ParallelGatedFFN.from_shards(Wg, bg, Wu, bu, Wo, bo, "silu", mode="fused")
+        ffn = ParallelGatedFFN.from_shards(Wg, bg, Wu, bu, Wo, bo, "silu", mode="fused",
+                                           chunks=chunks, first_chunks=first)
         run = lambda: ffn(X, hidden=Hg, out=Yg)  # noqa: E731
-        launches = 4 + 4 + 5
+        n_ch = len(row_chunks(M_g, world, chunks))
+        launches = len(row_schedule(n_ch, first_groups(n_ch, first)))
     ms = time_run(run, 1500.0)
     Wgc, Wuc = Wg.float().cpu().numpy(), Wu.float().cpu().numpy()
     bgc, buc = bg.float().cpu().numpy(), bu.float().cpu().numpy()
@@ -777,7 +783,7 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
         "value": round(tf, 2), "unit": "TFLOP/s", "ms": round(ms, 4),
         "frac_of_peak": round(tf / world / tflops_peak, 4),
         "parallelism": "one GPU" if world == 1 else
-        f"column->row x{world}, reduction overlapped with the GEMMs",
+        f"column->row x{world}, reduction carried by the GEMM launches ({chunks} row chunks)",
         "gpu_launches_per_step": launches}
     return out
 

@@ -65,12 +65,13 @@ SIGNATURES = {
                                            ctypes.c_int, _i64, _i64, _i64, _vp, _vp, _i64,
                                            ctypes.POINTER(ctypes.c_void_p), _i64, ctypes.c_int,
                                            _vp]),
-    "dx_row_reduce": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p),
-                                     ctypes.POINTER(ctypes.c_void_p),
-                                     ctypes.POINTER(ctypes.c_void_p), ctypes.c_int, ctypes.c_int,
-                                     _i64, _i64, _i64, _i64, _i64, ctypes.c_int, _i64, _i64,
-                                     ctypes.c_int, _vp, _vp, _i64, _vp, _i64, ctypes.c_int,
-                                     ctypes.c_int, ctypes.c_int, _vp]),
+    "dx_row_reduce": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, _vp]),
+    "dx_fused_linear_rowjob": (ctypes.c_int, _LINEAR_ARGS + [ctypes.c_int, _vp, ctypes.c_size_t,
+                                                             ctypes.c_void_p, _vp]),
+    "dx_fused_gated_linear_rowjob": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64,
+                                                    _i64, _i64, _i64, _i64, _i64, ctypes.c_int,
+                                                    ctypes.c_int, ctypes.c_int, _vp,
+                                                    ctypes.c_size_t, ctypes.c_void_p, _vp]),
     "dx_row_flag_words": (ctypes.c_int, []),
     "dx_fused_linear_workspace_size": (ctypes.c_size_t, [_i64, _i64, _i64, ctypes.c_int, ctypes.c_int]),
     "dx_fused_gated_linear": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64,
@@ -95,6 +96,36 @@ SIGNATURES = {
     "dx_plan_call_residual": (ctypes.c_int, [_vp, _vp, _vp, _vp, _vp, _vp, _vp]),
     "dx_plan_destroy": (ctypes.c_int, [_vp]),
 }
+
+
+
+class RowReduceJob(ctypes.Structure):
+    """ctypes mirror of ``dx_row_reduce_job`` (include/deepx_fused.h)."""
+
+    _fields_ = [
+        ("P", ctypes.c_void_p * 8),
+        ("S", ctypes.c_void_p * 8),
+        ("F", ctypes.c_void_p * 8),
+        ("world", ctypes.c_int),
+        ("rank", ctypes.c_int),
+        ("M", ctypes.c_int64),
+        ("N", ctypes.c_int64),
+        ("ldp", ctypes.c_int64),
+        ("a_row0", ctypes.c_int64),
+        ("a_rows", ctypes.c_int64),
+        ("a_chunk", ctypes.c_int),
+        ("b_row0", ctypes.c_int64),
+        ("b_rows", ctypes.c_int64),
+        ("b_chunk", ctypes.c_int),
+        ("bias", ctypes.c_void_p),
+        ("R", ctypes.c_void_p),
+        ("ldr", ctypes.c_int64),
+        ("Y", ctypes.c_void_p),
+        ("ldy", ctypes.c_int64),
+        ("epoch", ctypes.c_int),
+        ("dtype", ctypes.c_int),
+    ]
+
 
 _lock = threading.Lock()
 _lib = None

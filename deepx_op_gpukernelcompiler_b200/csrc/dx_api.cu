@@ -205,6 +205,10 @@ struct Problem {
   const void* W2 = nullptr;
   const void* bias2 = nullptr;
   int64_t ldw2 = 0;
+  // Row-parallel reduction job carried by a tensor-core launch (or run as a
+  // standalone launch after the GEMM when another variant runs), or nullptr.
+  const dx::RowReduceArgs* comm = nullptr;
+  int comm_dtype = 0;
 };
 
 // ----------------------------------------------------------- decode plan
@@ -429,6 +433,8 @@ UmmaParams umma_params(const Problem& pr, const UmmaPlan& pl) {
   p.partials = pl.splits > 1
                    ? reinterpret_cast<float*>(static_cast<char*>(pr.ws) + kTicketSlabBytes)
                    : nullptr;
+  p.comm_on = pr.comm != nullptr ? 1 : 0;
+  if (pr.comm != nullptr) p.comm = *pr.comm;
   return p;
 }
 
@@ -758,11 +764,91 @@ int dispatch_typed(const Problem& p, int variant, int dev, int sms) {
   }
 }
 
+// ------------------------------------------------ row-parallel reduction
+// Checks a dx_row_reduce_job and fills the kernels' argument block.
+int row_job_args(const dx_row_reduce_job* j, dx::RowReduceArgs* a) {
+  if (j == nullptr || j->Y == nullptr)
+    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: NULL job or output");
+  const int world = j->world, rank = j->rank;
+  const int64_t M = j->M, N = j->N;
+  if (world < 1 || world > dx::kRowMaxWorld || rank < 0 || rank >= world)
+    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: world must be 1..%d and 0 <= rank < world",
+                dx::kRowMaxWorld);
+  if (j->dtype != DX_DTYPE_F16 && j->dtype != DX_DTYPE_BF16)
+    return fail(DX_ERR_UNSUPPORTED, "row_reduce supports fp16/bf16");
+  if (M <= 0 || M % world != 0 || M > 0x7fffffffLL || N <= 0 || N % 8 != 0 || N > 0x7fffffffLL)
+    return fail(DX_ERR_INVALID_ARGUMENT,
+                "row_reduce needs M > 0 divisible by world (M=%lld, world=%d) and N %% 8 == 0",
+                (long long)M, world);
+  if (j->ldp < N || j->ldp % 8 != 0 || j->ldy < N || j->ldy % 8 != 0 ||
+      (j->R != nullptr && (j->ldr < N || j->ldr % 8 != 0)))
+    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: pitches must be >= N and multiples of 8");
+  if (j->epoch <= 0) return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: epoch must be positive");
+  auto bad_chunk = [&](int64_t row0, int64_t rows, int chunk) {
+    return rows < 0 || (rows > 0 && (row0 < 0 || row0 % world != 0 || rows % world != 0 ||
+                                     row0 + rows > M || chunk < 0 ||
+                                     chunk >= dx::kRowMaxChunks));
+  };
+  if (bad_chunk(j->a_row0, j->a_rows, j->a_chunk) || bad_chunk(j->b_row0, j->b_rows, j->b_chunk))
+    return fail(DX_ERR_INVALID_ARGUMENT,
+                "row_reduce: a chunk must lie in [0, M), start and span multiples of world, "
+                "and have an index below %d",
+                dx::kRowMaxChunks);
+  if ((j->bias != nullptr && !aligned16(j->bias)) || (j->R != nullptr && !aligned16(j->R)) ||
+      !aligned16(j->Y))
+    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce needs 16-byte-aligned bias, R and Y");
+  *a = dx::RowReduceArgs{};
+  for (int r = 0; r < world; ++r) {
+    if (j->P[r] == nullptr || !aligned16(j->P[r]) || j->S[r] == nullptr || !aligned16(j->S[r]) ||
+        j->F[r] == nullptr || (reinterpret_cast<uintptr_t>(j->F[r]) & 3u) != 0)
+      return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: buffers of rank %d NULL or misaligned", r);
+    a->P.p[r] = j->P[r];
+    a->S.p[r] = j->S[r];
+    a->F.p[r] = j->F[r];
+  }
+  a->world = world;
+  a->rank = rank;
+  a->N = static_cast<int>(N);
+  a->ldp = j->ldp;
+  a->ldr = j->ldr;
+  a->ldy = j->ldy;
+  a->slab_base = static_cast<long long>(j->epoch & 1) * (M / world);
+  a->a_row0 = j->a_row0;
+  a->a_rows = static_cast<int>(j->a_rows);
+  a->a_chunk = j->a_chunk;
+  a->b_row0 = j->b_row0;
+  a->b_rows = static_cast<int>(j->b_rows);
+  a->b_chunk = j->b_chunk;
+  a->bias = j->bias;
+  a->R = j->R;
+  a->Y = j->Y;
+  a->epoch = j->epoch;
+  return DX_OK;
+}
+
+// The standalone reduction kernel (one 512-thread CTA per SM by default).
+int launch_row_reduce(const dx::RowReduceArgs& a, int dtype, int sms, int grid,
+                      cudaStream_t s) {
+  if (a.a_rows == 0 && a.b_rows == 0) return DX_OK;
+  if (grid <= 0 || grid > sms) grid = sms;
+  set_plan("row_reduce world=%d rank=%d A=[%lld,+%d) B=[%lld,+%d) N=%d grid=%d epoch=%d",
+           a.world, a.rank, a.a_row0, a.a_rows, a.b_row0, a.b_rows, a.N, grid, a.epoch);
+  if (dtype == DX_DTYPE_F16)
+    dx::row_reduce_kernel<__half><<<grid, dx::kRowThreads, 0, s>>>(a);
+  else
+    dx::row_reduce_kernel<__nv_bfloat16><<<grid, dx::kRowThreads, 0, s>>>(a);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return cuda_fail(e, "launch row_reduce_kernel");
+  return DX_OK;
+}
+
 int run(const Problem& p, int kernel) {
   t_last_error.clear();
   int rc = validate(p, kernel);
   if (rc) return rc;
-  if (p.M == 0 || p.N == 0) return DX_OK;
+  if (p.comm != nullptr && p.comm_dtype != p.dtype)
+    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce job dtype differs from the GEMM's");
+  if ((p.M == 0 || p.N == 0) && p.comm == nullptr) return DX_OK;
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
@@ -770,6 +856,7 @@ int run(const Problem& p, int kernel) {
   if ((rc = device_sms(dev, &sms))) return rc;
   if ((rc = install_status_mirror(dev, p.stream))) return rc;
   if ((rc = check_status_mirror(dev))) return rc;
+  if (p.M == 0 || p.N == 0) return launch_row_reduce(*p.comm, p.comm_dtype, sms, 0, p.stream);
 
   int variant = kernel == DX_KERNEL_AUTO ? select_variant(p, sms, true) : kernel;
   if (variant == DX_KERNEL_UMMA || variant == DX_KERNEL_UMMA_1CTA || variant == DX_KERNEL_DECODE) {
@@ -795,12 +882,26 @@ int run(const Problem& p, int kernel) {
     case DX_DTYPE_F32:
       if (variant != DX_KERNEL_SIMT)
         return fail(DX_ERR_UNSUPPORTED, "fp32 runs only on the exact-fp32 SIMT kernel");
-      return p.gated ? launch_simt_gated<float>(p, sms) : launch_simt<float>(p, sms);
+      rc = p.gated ? launch_simt_gated<float>(p, sms) : launch_simt<float>(p, sms);
+      break;
     case DX_DTYPE_F16:
-      return dispatch_typed<__half>(p, variant, dev, sms);
+      rc = dispatch_typed<__half>(p, variant, dev, sms);
+      break;
     default:
-      return dispatch_typed<__nv_bfloat16>(p, variant, dev, sms);
+      rc = dispatch_typed<__nv_bfloat16>(p, variant, dev, sms);
   }
+  // Only the tensor-core kernels carry a job; after another variant it runs
+  // as its own launch, stream-ordered after the GEMM.
+  const bool carried = variant == DX_KERNEL_UMMA || variant == DX_KERNEL_UMMA_1CTA;
+  if (rc == DX_OK && p.comm != nullptr && !carried) {
+    const std::string gemm_plan = t_last_plan;
+    rc = launch_row_reduce(*p.comm, p.comm_dtype, sms, 0, p.stream);
+    if (rc == DX_OK) set_plan("%s +row_reduce launch", gemm_plan.c_str());
+  } else if (rc == DX_OK && p.comm != nullptr) {
+    const std::string gemm_plan = t_last_plan;
+    set_plan("%s +row_reduce job A=%d B=%d", gemm_plan.c_str(), p.comm->a_rows, p.comm->b_rows);
+  }
+  return rc;
 }
 
 // One CTA waits, through the kernels' bounded mbarrier wait, on a barrier
@@ -843,6 +944,24 @@ int dx_fused_linear(const void* X, const void* W, const void* bias, const void* 
                             DX_KERNEL_AUTO, workspace, workspace_bytes, stream);
 }
 
+int dx_fused_linear_rowjob(const void* X, const void* W, const void* bias, const void* R, void* Y,
+                           int64_t M, int64_t N, int64_t K, int64_t ldx, int64_t ldw,
+                           int64_t ldr, int64_t ldy, int dtype, int act, int kernel,
+                           void* workspace, size_t workspace_bytes, const dx_row_reduce_job* job,
+                           void* stream) {
+  t_last_error.clear();
+  Problem p{X, W, bias, R, Y, M, N, K, ldx, ldw, ldr, ldy, dtype, act, workspace, workspace_bytes,
+            static_cast<cudaStream_t>(stream)};
+  dx::RowReduceArgs a{};
+  if (job != nullptr) {
+    const int rc = row_job_args(job, &a);
+    if (rc) return rc;
+    p.comm = &a;
+    p.comm_dtype = job->dtype;
+  }
+  return run(p, kernel);
+}
+
 size_t dx_fused_linear_workspace_size(int64_t M, int64_t N, int64_t K, int dtype, int kernel) {
   t_last_error.clear();
   if (M <= 0 || N <= 0 || K <= 0 || dtype == DX_DTYPE_F32 || kernel == DX_KERNEL_SIMT) return 0;
@@ -871,6 +990,29 @@ int dx_fused_gated_linear(const void* X, const void* Wg, const void* Wu, const v
   p.W2 = Wu;
   p.bias2 = bias_u;
   p.ldw2 = ldwu;
+  return run(p, kernel);
+}
+
+int dx_fused_gated_linear_rowjob(const void* X, const void* Wg, const void* Wu,
+                                 const void* bias_g, const void* bias_u, void* Y, int64_t M,
+                                 int64_t N, int64_t K, int64_t ldx, int64_t ldwg, int64_t ldwu,
+                                 int64_t ldy, int dtype, int act, int kernel, void* workspace,
+                                 size_t workspace_bytes, const dx_row_reduce_job* job,
+                                 void* stream) {
+  t_last_error.clear();
+  Problem p{X, Wg, bias_g, nullptr, Y, M, N, K, ldx, ldwg, 0, ldy, dtype, act, workspace,
+            workspace_bytes, static_cast<cudaStream_t>(stream)};
+  p.gated = true;
+  p.W2 = Wu;
+  p.bias2 = bias_u;
+  p.ldw2 = ldwu;
+  dx::RowReduceArgs a{};
+  if (job != nullptr) {
+    const int rc = row_job_args(job, &a);
+    if (rc) return rc;
+    p.comm = &a;
+    p.comm_dtype = job->dtype;
+  }
   return run(p, kernel);
 }
 
@@ -965,89 +1107,19 @@ int dx_reduce_broadcast(void* const* P, int world, int rank, int64_t rows_per_ra
 
 int dx_row_flag_words(void) { return dx::kRowFlagWords; }
 
-int dx_row_reduce(void* const* P, void* const* S, int* const* F, int world, int rank, int64_t M,
-                  int64_t N, int64_t ldp, int64_t a_row0, int64_t a_rows, int a_chunk,
-                  int64_t b_row0, int64_t b_rows, int b_chunk, const void* bias, const void* R,
-                  int64_t ldr, void* Y, int64_t ldy, int epoch, int grid, int dtype,
-                  void* stream) {
+int dx_row_reduce(const dx_row_reduce_job* job, int grid, void* stream) {
   t_last_error.clear();
-  if (P == nullptr || S == nullptr || F == nullptr || Y == nullptr)
-    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: NULL buffer array or output");
-  if (world < 1 || world > dx::kRowMaxWorld || rank < 0 || rank >= world)
-    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: world must be 1..%d and 0 <= rank < world",
-                dx::kRowMaxWorld);
-  if (dtype != DX_DTYPE_F16 && dtype != DX_DTYPE_BF16)
-    return fail(DX_ERR_UNSUPPORTED, "row_reduce supports fp16/bf16");
-  if (M <= 0 || M % world != 0 || M > 0x7fffffffLL || N <= 0 || N % 8 != 0 || N > 0x7fffffffLL)
-    return fail(DX_ERR_INVALID_ARGUMENT,
-                "row_reduce needs M > 0 divisible by world (M=%lld, world=%d) and N %% 8 == 0",
-                (long long)M, world);
-  if (ldp < N || ldp % 8 != 0 || ldy < N || ldy % 8 != 0 || (R != nullptr && (ldr < N || ldr % 8)))
-    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: pitches must be >= N and multiples of 8");
-  if (epoch <= 0) return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: epoch must be positive");
-  auto bad_chunk = [&](int64_t row0, int64_t rows, int chunk) {
-    return rows < 0 || (rows > 0 && (row0 < 0 || row0 % world != 0 || rows % world != 0 ||
-                                     row0 + rows > M || chunk < 0 ||
-                                     chunk >= dx::kRowMaxChunks));
-  };
-  if (bad_chunk(a_row0, a_rows, a_chunk) || bad_chunk(b_row0, b_rows, b_chunk))
-    return fail(DX_ERR_INVALID_ARGUMENT,
-                "row_reduce: a chunk must lie in [0, M), start and span multiples of world, "
-                "and have an index below %d",
-                dx::kRowMaxChunks);
-  if ((bias != nullptr && !aligned16(bias)) || (R != nullptr && !aligned16(R)) || !aligned16(Y))
-    return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce needs 16-byte-aligned bias, R and Y");
   dx::RowReduceArgs a{};
-  for (int r = 0; r < world; ++r) {
-    if (P[r] == nullptr || !aligned16(P[r]) || S[r] == nullptr || !aligned16(S[r]) ||
-        F[r] == nullptr || (reinterpret_cast<uintptr_t>(F[r]) & 3u) != 0)
-      return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: buffers of rank %d NULL or misaligned", r);
-    a.P.p[r] = P[r];
-    a.S.p[r] = S[r];
-    a.F.p[r] = F[r];
-  }
-  int dev = 0, sms = 0, rc;
+  int rc = row_job_args(job, &a);
+  if (rc) return rc;
+  int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   if ((rc = device_sms(dev, &sms))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if ((rc = install_status_mirror(dev, s))) return rc;
   if ((rc = check_status_mirror(dev))) return rc;
-  if (a_rows == 0 && b_rows == 0) return DX_OK;
-  a.world = world;
-  a.rank = rank;
-  a.N = static_cast<int>(N);
-  a.ldp = ldp;
-  a.ldr = ldr;
-  a.ldy = ldy;
-  a.slab_base = static_cast<long long>(epoch & 1) * (M / world);
-  a.a_row0 = a_row0;
-  a.a_rows = static_cast<int>(a_rows);
-  a.a_chunk = a_chunk;
-  a.b_row0 = b_row0;
-  a.b_rows = static_cast<int>(b_rows);
-  a.b_chunk = b_chunk;
-  a.bias = bias;
-  a.R = R;
-  a.Y = Y;
-  a.epoch = epoch;
-  if (grid <= 0 || grid > sms) grid = sms;
-  const void* fn = dtype == DX_DTYPE_F16
-                       ? reinterpret_cast<const void*>(dx::row_reduce_kernel<__half>)
-                       : reinterpret_cast<const void*>(dx::row_reduce_kernel<__nv_bfloat16>);
-  // Same shared-memory configuration preference as the GEMM kernels, so the
-  // CTAs can be placed on SMs those kernels occupy.
-  if ((rc = ensure_smem_attr(dev, fn, 0, true))) return rc;
-  set_plan("row_reduce world=%d rank=%d A=[%lld,+%lld) B=[%lld,+%lld) N=%lld grid=%d epoch=%d",
-           world, rank, (long long)a_row0, (long long)a_rows, (long long)b_row0,
-           (long long)b_rows, (long long)N, grid, epoch);
-  if (dtype == DX_DTYPE_F16)
-    dx::row_reduce_kernel<__half><<<grid, dx::kRowThreads, 0, s>>>(a);
-  else
-    dx::row_reduce_kernel<__nv_bfloat16><<<grid, dx::kRowThreads, 0, s>>>(a);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return cuda_fail(e, "launch row_reduce_kernel");
-  return DX_OK;
+  return launch_row_reduce(a, job->dtype, sms, grid, s);
 }
 
 // ------------------------------------------------------------- plans

@@ -117,14 +117,16 @@ __global__ void __launch_bounds__(256)
 // Every wait is bounded (kRowWaitLimitNs); on expiry the kernel reports the
 // timeout in the status word and returns.
 //
-// Launch with at most one CTA per SM: 128 threads and <= 80 registers per
-// thread, no dynamic shared memory, so a CTA fits beside a resident tensor-
-// core GEMM CTA (320 threads x 168 registers, ~231 KB of shared memory) and
-// the two kernels run on the same SMs at once.
+// Where it runs: the tensor-core GEMM kernels keep two spare warps per CTA
+// for it (dx_row_reduce_job), so a chunk's reduction runs on the SMs of the
+// next GEMM launch while that launch's tensor-core warps compute — a separate
+// kernel on another stream could not share those SMs, whose register files
+// the GEMM's warps fill.  The reduction of the last chunk, with no GEMM left
+// to ride on, runs as the standalone row_reduce_kernel.
 // =====================================================================
 constexpr int kRowMaxWorld = 8;
 constexpr int kRowMaxChunks = 64;
-constexpr int kRowThreads = 128;
+constexpr int kRowThreads = 512;  // standalone kernel: threads per CTA
 // Flag words per rank: PART[chunk][src], RED[chunk][src], arrival counters.
 constexpr int kRowFlagWords = 2 * kRowMaxChunks * kRowMaxWorld + kRowMaxChunks;
 constexpr uint64_t kRowWaitLimitNs = 2000ull * 1000ull * 1000ull;  // 2 s
@@ -188,28 +190,31 @@ __device__ __forceinline__ bool row_wait_flags(const int* flags, int first, int 
   return true;
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kRowThreads, 6) row_reduce_kernel(const RowReduceArgs a) {
-  const int tid = threadIdx.x;
+// The work of one reduction call, spread over `lanes` threads of the grid:
+// `gl` is this thread's index among them and `warps` = lanes / 32.  Runs at
+// warp granularity (no block-wide barrier), so it serves both the standalone
+// kernel and the spare warps of a tensor-core GEMM launch.  UA / UB: column
+// groups each thread keeps in flight in phase A / phase B.  Returns early
+// (status word set) if a wait ran out.
+template <typename T, int UA, int UB>
+__device__ __forceinline__ void row_reduce_lanes(const RowReduceArgs& a, long long gl,
+                                                 long long lanes, int warps) {
+  const int lane = threadIdx.x & 31;
   const int groups = a.N / 8;  // 16-byte column groups per row
-  const long long nthreads = static_cast<long long>(gridDim.x) * kRowThreads;
-  const long long gtid = static_cast<long long>(blockIdx.x) * kRowThreads + tid;
   T* const Y = static_cast<T*>(a.Y);
 
   if (a.a_rows > 0) {
-    // This launch follows the GEMM that wrote chunk a_chunk of the local
-    // partial: announce it to every rank (each CTA stamps the same epoch, so
-    // the announcement never waits for one particular CTA to be scheduled).
-    if (tid < a.world) {
+    // The launch follows the GEMM that wrote chunk a_chunk of the local
+    // partial: announce it to every rank.  Every warp stamps the same epoch,
+    // so the announcement never waits for one particular warp to run.
+    if (lane < a.world) {
       __threadfence_system();
-      st_release_sys(a.F.p[tid] + row_part_flag(a.a_chunk, a.rank), a.epoch);
+      st_release_sys(a.F.p[lane] + row_part_flag(a.a_chunk, a.rank), a.epoch);
     }
-    // One thread waits; the block-wide vote passes its verdict to the rest
-    // (no shared memory, which the co-resident GEMM CTA leaves almost none of).
-    const int ok = tid == 0
-        ? (row_wait_flags(a.F.p[a.rank], row_part_flag(a.a_chunk, 0), a.world, -1, a.epoch) ? 1 : 0)
-        : 1;
-    if (!__syncthreads_and(ok)) return;
+    int ok = 1;
+    if (lane == 0)
+      ok = row_wait_flags(a.F.p[a.rank], row_part_flag(a.a_chunk, 0), a.world, -1, a.epoch);
+    if (!__shfl_sync(0xffffffffu, ok, 0)) return;
 
     const int slab = a.a_rows / a.world;
     const long long row0 = a.a_row0 + static_cast<long long>(a.rank) * slab;
@@ -218,25 +223,40 @@ __global__ void __launch_bounds__(kRowThreads, 6) row_reduce_kernel(const RowRed
     const T* const bias = static_cast<const T*>(a.bias);
     const T* const R = static_cast<const T*>(a.R);
     T* const Sown = static_cast<T*>(a.S.p[a.rank]);
-    for (long long i = gtid; i < total; i += nthreads) {
-      const int r = static_cast<int>(i / groups);
-      const int c8 = static_cast<int>(i - static_cast<long long>(r) * groups) * 8;
-      uint4 part[8];
+    for (long long i0 = gl; i0 < total; i0 += UA * lanes) {
+      uint4 part[UA][kRowMaxWorld];
 #pragma unroll
-      for (int src = 0; src < kRowMaxWorld; ++src)
-        if (src < a.world)
-          part[src] = __ldcg(reinterpret_cast<const uint4*>(static_cast<const T*>(a.P.p[src]) +
-                                                            (row0 + r) * a.ldp + c8));
-      const uint4 o = rb_finish<T>(part, a.world, bias, R, (row0 + r) * a.ldr + c8, c8);
-      *reinterpret_cast<uint4*>(Y + (row0 + r) * a.ldy + c8) = o;
-      __stcg(reinterpret_cast<uint4*>(Sown + (srow0 + r) * static_cast<long long>(a.N) + c8), o);
+      for (int u = 0; u < UA; ++u) {
+        const long long i = i0 + u * lanes;
+        if (i < total) {
+          const int r = static_cast<int>(i / groups);
+          const int c8 = static_cast<int>(i - static_cast<long long>(r) * groups) * 8;
+#pragma unroll
+          for (int src = 0; src < kRowMaxWorld; ++src)
+            if (src < a.world)
+              part[u][src] = __ldcg(reinterpret_cast<const uint4*>(
+                  static_cast<const T*>(a.P.p[src]) + (row0 + r) * a.ldp + c8));
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < UA; ++u) {
+        const long long i = i0 + u * lanes;
+        if (i < total) {
+          const int r = static_cast<int>(i / groups);
+          const int c8 = static_cast<int>(i - static_cast<long long>(r) * groups) * 8;
+          const uint4 o = rb_finish<T>(part[u], a.world, bias, R, (row0 + r) * a.ldr + c8, c8);
+          __stcs(reinterpret_cast<uint4*>(Y + (row0 + r) * a.ldy + c8), o);
+          __stcg(reinterpret_cast<uint4*>(Sown + (srow0 + r) * static_cast<long long>(a.N) + c8),
+                 o);
+        }
+      }
     }
-    // The last CTA to finish announces the slab to every rank.
-    __syncthreads();
-    if (tid == 0) {
+    // The last warp to finish announces the slab to every rank.
+    __syncwarp();
+    if (lane == 0) {
       __threadfence_system();
       int* const ctr = a.F.p[a.rank] + row_counter(a.a_chunk);
-      if (atomicAdd(ctr, 1) == static_cast<int>(gridDim.x) - 1) {
+      if (atomicAdd(ctr, 1) == warps - 1) {
         atomicExch(ctr, 0);
         __threadfence_system();
         for (int s = 0; s < a.world; ++s)
@@ -246,24 +266,23 @@ __global__ void __launch_bounds__(kRowThreads, 6) row_reduce_kernel(const RowRed
   }
 
   if (a.b_rows > 0) {
-    const int ok = tid == 0
-        ? (row_wait_flags(a.F.p[a.rank], row_red_flag(a.b_chunk, 0), a.world, a.rank, a.epoch) ? 1 : 0)
-        : 1;
-    if (!__syncthreads_and(ok)) return;
+    int ok = 1;
+    if (lane == 0)
+      ok = row_wait_flags(a.F.p[a.rank], row_red_flag(a.b_chunk, 0), a.world, a.rank, a.epoch);
+    if (!__shfl_sync(0xffffffffu, ok, 0)) return;
     const int slab = a.b_rows / a.world;
     const long long srow0 = a.slab_base + a.b_row0 / a.world;
     const long long per_src = static_cast<long long>(slab) * groups;
     const long long total = per_src * (a.world - 1);
-    constexpr int kUnroll = 4;
-    for (long long i0 = gtid; i0 < total; i0 += kUnroll * nthreads) {
-      uint4 v[kUnroll];
-      long long dst[kUnroll];
+    for (long long i0 = gl; i0 < total; i0 += UB * lanes) {
+      uint4 v[UB];
+      long long dst[UB];
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u) {
-        const long long i = i0 + u * nthreads;
+      for (int u = 0; u < UB; ++u) {
+        const long long i = i0 + u * lanes;
         dst[u] = -1;
         if (i < total) {
-          int k = static_cast<int>(i / per_src);
+          const int k = static_cast<int>(i / per_src);
           const long long j = i - k * per_src;
           const int src = k + (k >= a.rank ? 1 : 0);
           const int r = static_cast<int>(j / groups);
@@ -274,10 +293,19 @@ __global__ void __launch_bounds__(kRowThreads, 6) row_reduce_kernel(const RowRed
         }
       }
 #pragma unroll
-      for (int u = 0; u < kUnroll; ++u)
-        if (dst[u] >= 0) *reinterpret_cast<uint4*>(Y + dst[u]) = v[u];
+      for (int u = 0; u < UB; ++u)
+        if (dst[u] >= 0) __stcs(reinterpret_cast<uint4*>(Y + dst[u]), v[u]);
     }
   }
+}
+
+// Standalone form: the call that ends a step (the last chunk, with nothing
+// left to overlap), or a job whose GEMM launch could not carry it.
+template <typename T>
+__global__ void __launch_bounds__(kRowThreads, 1) row_reduce_kernel(const RowReduceArgs a) {
+  const long long lanes = static_cast<long long>(gridDim.x) * kRowThreads;
+  row_reduce_lanes<T, 2, 8>(a, static_cast<long long>(blockIdx.x) * kRowThreads + threadIdx.x,
+                            lanes, static_cast<int>(lanes / 32));
 }
 
 }  // namespace dx

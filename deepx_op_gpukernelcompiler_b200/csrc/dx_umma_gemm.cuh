@@ -15,7 +15,7 @@
 //     shared memory per MMA compared with a single-CTA 128 x BN tile.
 //   umma_fused_linear_kernel   (M < 256) — single CTA, 128 x BN tiles.
 //
-// Roles inside a CTA (320 threads):
+// Roles inside a CTA (384 threads):
 //   warp 0   TMA producer: X tiles [128 x 64] (K-major) and W tiles
 //            [64 x 64] boxes (N-major, W exactly as it lies in memory) into
 //            a STAGES-deep ring of 128-byte-swizzled buffers;
@@ -27,7 +27,11 @@
 //            bias, applies the activation, adds the residual (TMA-loaded into
 //            the staging buffer), converts, and TMA-stores.  The output tile
 //            crosses HBM exactly once; the next tile's main loop runs in the
-//            other accumulator meanwhile.
+//            other accumulator meanwhile;
+//   warps 10-11 spare: when the launch carries a row-parallel reduction job
+//            (the previous chunk of a row-parallel chain's second GEMM, see
+//            dx_collective.cuh), they run it over NVLink while the GEMM
+//            computes; otherwise they exit at once.
 // Gated form (kGated): Y = act(X Wg + bg) * (X Wu + bu), the first half of a
 // gated FFN.  A BN-wide accumulator holds BN/2 gate columns followed by the
 // matching BN/2 up columns: the producer fills the B operand's first half
@@ -41,6 +45,7 @@
 // copies in flight, frees TMEM and exits with the device status bit set.
 #pragma once
 
+#include "dx_collective.cuh"
 #include "dx_epilogue.cuh"
 #include "dx_ptx.cuh"
 
@@ -67,8 +72,13 @@ struct UmmaParams {
   int* tickets;     // [tail tile][CTA of the tile][kEpiWarps][2]; zero between calls
   // Optional timeline (dx_set_trace_buffer): per CTA kTraceSlots device-time
   // stamps: [0] after set-up, [1 + i] when the epilogue finished work item i
-  // (first kTraceSlots - 2 items), [kTraceSlots - 1] at exit.
+  // (first kTraceSlots - 3 items), [kTraceSlots - 2] when the CTA's spare
+  // warps finished a carried reduction job, [kTraceSlots - 1] at exit.
   unsigned long long* trace;
+  // A row-parallel reduction job carried by this launch (dx_row_reduce_job):
+  // the CTAs' spare warps run it while the other warps compute the GEMM.
+  int comm_on;
+  RowReduceArgs comm;
 };
 
 __device__ __forceinline__ void trace_mark(const UmmaParams& p, int slot) {
@@ -124,6 +134,24 @@ constexpr int kEpiBufBytes = 32 * 32 * 2;  // [32 rows x 32 cols] of 16-bit
 // the TMA store issued kEpiBufs chunks earlier has read it, so up to
 // kEpiBufs - 1 stores stay in flight behind the producer's loads.
 constexpr int kEpiBufs = 2;
+// Spare warps per CTA (after the epilogue warps) that run a row-parallel
+// reduction job when the launch carries one, and otherwise just exit.  With
+// them a CTA has 12 warps, three on each of the SM's four sub-partitions,
+// whose register files 12 x 168 registers per thread fill (16,128 of 16,384
+// each): no other kernel's CTA could be placed beside a GEMM CTA, so work
+// that must overlap the GEMM has to live in its launch.
+constexpr int kCommWarps = 2;
+
+// The spare warps of every CTA of a GEMM launch run the launch's reduction
+// job together (2 warps x grid CTAs).
+template <typename T>
+__device__ __forceinline__ void comm_warps_run(const UmmaParams& p, int warp, int lane) {
+  const int cw = warp - 2 - kEpiWarps;
+  const int warps = static_cast<int>(gridDim.x) * kCommWarps;
+  const long long gl = (static_cast<long long>(blockIdx.x) * kCommWarps + cw) * 32 + lane;
+  row_reduce_lanes<T, 2, 8>(p.comm, gl, static_cast<long long>(warps) * 32, warps);
+  if (cw == 0 && lane == 0) trace_mark(p, kTraceSlots - 2);
+}
 
 // What one epilogue warp needs to finish accumulators.
 template <typename T>
@@ -527,7 +555,7 @@ struct UmmaShape {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN == 256) ? 4 : 6;
   static constexpr int TMEM_COLS = 2 * BN;  // two fp32 accumulators
-  static constexpr int THREADS = 64 + 32 * kEpiWarps;
+  static constexpr int THREADS = 64 + 32 * (kEpiWarps + kCommWarps);
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
@@ -692,7 +720,7 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
       mbar_wait_drain(bar(S::BAR_DRAIN), 0);
     }
     __syncwarp();
-  } else {
+  } else if (warp < 2 + kEpiWarps) {
     // --------------------------------------------------------- epilogue
     const int e = warp - 2;  // epilogue warp index 0..kEpiWarps-1
     const int q = warp & 3;  // TMEM lane quarter this warp may address
@@ -760,10 +788,13 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
                                      part_base, it, abort_flag, release);
       }
       if (!done) break;
-      if (e == 0 && lane == 0) trace_mark(p, 1 + i);
+      if (e == 0 && lane == 0 && 1 + i < kTraceSlots - 2) trace_mark(p, 1 + i);
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
+  } else if (p.comm_on) {
+    // ------------------------ spare warps: the carried reduction job
+    comm_warps_run<T>(p, warp, lane);
   }
 
   tc_fence_before();
@@ -789,7 +820,7 @@ struct Umma2Shape {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;  // per CTA
   static constexpr int STAGES = (BN == 256) ? 6 : 8;
   static constexpr int TMEM_COLS = 2 * BN;  // per CTA: two accumulators of BN fp32 columns
-  static constexpr int THREADS = 64 + 32 * kEpiWarps;
+  static constexpr int THREADS = 64 + 32 * (kEpiWarps + kCommWarps);
   static constexpr int OFF_A = 0;
   static constexpr int OFF_B = OFF_A + STAGES * A_BYTES;
   static constexpr int OFF_EPI = OFF_B + STAGES * B_BYTES;
@@ -955,7 +986,7 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
       mbar_wait_drain(bar(S::BAR_DRAIN), 0);
     }
     __syncwarp();
-  } else {
+  } else if (warp < 2 + kEpiWarps) {
     // --------------------------------------------- epilogue (both CTAs)
     const int e = warp - 2;
     const int q = warp & 3;
@@ -1025,10 +1056,13 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
                                      part_base, it, abort_flag, release);
       }
       if (!done) break;
-      if (e == 0 && lane == 0) trace_mark(p, 1 + i);
+      if (e == 0 && lane == 0 && 1 + i < kTraceSlots - 2) trace_mark(p, 1 + i);
     }
     if (lane == 0) bulk_wait_group<0>();
     __syncwarp();
+  } else if (p.comm_on) {
+    // ------------------------ spare warps: the carried reduction job
+    comm_warps_run<T>(p, warp, lane);
   }
 
   // No CTA of the pair leaves while the other may still signal it.

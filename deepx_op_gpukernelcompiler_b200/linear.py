@@ -14,6 +14,7 @@ kernel_tilelang.py:17 compute).
 """
 from __future__ import annotations
 
+import ctypes
 import threading
 
 import torch
@@ -89,8 +90,13 @@ def _ld(t: torch.Tensor) -> int:
 
 def fused_linear(X: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None = None,
                  activation=None, residual: torch.Tensor | None = None,
-                 out: torch.Tensor | None = None, kernel: str = "auto") -> torch.Tensor:
-    """Y = act(X @ W + bias) + residual, one fused launch on X's device."""
+                 out: torch.Tensor | None = None, kernel: str = "auto",
+                 row_job=None) -> torch.Tensor:
+    """Y = act(X @ W + bias) + residual, one fused launch on X's device.
+
+    `row_job` (a ``_native.RowReduceJob``, see row_job()) is a chunk of a
+    row-parallel reduction that the launch carries: its spare warps run it
+    while the GEMM computes (dx_fused_linear_rowjob)."""
     act = activation_code(activation)
     if kernel not in nat.KERNEL_NAMES:
         raise ValueError(f"unknown kernel {kernel!r}; expected one of {list(nat.KERNEL_NAMES)}")
@@ -132,15 +138,18 @@ def fused_linear(X: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None = N
         stream = torch.cuda.current_stream(X.device).cuda_stream
         ws_bytes = lib.dx_fused_linear_workspace_size(M, N, K, dtype, kcode)
         ws = _workspace(X.device, stream, ws_bytes)
-        rc = lib.dx_fused_linear_ex(
-            X.data_ptr(), W.data_ptr(),
-            bias.data_ptr() if bias is not None else None,
-            residual.data_ptr() if residual is not None else None,
-            out.data_ptr(), M, N, K, _ld(X), _ld(W),
-            _ld(residual) if residual is not None else 0, _ld(out),
-            dtype, act, kcode,
-            ws.data_ptr() if ws is not None else None,
-            ws.numel() if ws is not None else 0, stream)
+        args = (X.data_ptr(), W.data_ptr(),
+                bias.data_ptr() if bias is not None else None,
+                residual.data_ptr() if residual is not None else None,
+                out.data_ptr(), M, N, K, _ld(X), _ld(W),
+                _ld(residual) if residual is not None else 0, _ld(out),
+                dtype, act, kcode,
+                ws.data_ptr() if ws is not None else None,
+                ws.numel() if ws is not None else 0)
+        if row_job is None:
+            rc = lib.dx_fused_linear_ex(*args, stream)
+        else:
+            rc = lib.dx_fused_linear_rowjob(*args, ctypes.byref(row_job), stream)
     nat.check("dx_fused_linear", rc)
     return out
 
@@ -148,10 +157,11 @@ def fused_linear(X: torch.Tensor, W: torch.Tensor, bias: torch.Tensor | None = N
 def fused_gated_linear(X: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor,
                        bias_g: torch.Tensor | None = None, bias_u: torch.Tensor | None = None,
                        activation="silu", out: torch.Tensor | None = None,
-                       kernel: str = "auto") -> torch.Tensor:
+                       kernel: str = "auto", row_job=None) -> torch.Tensor:
     """Y = act(X @ Wg + bias_g) * (X @ Wu + bias_u) in one launch
     (dx_fused_gated_linear): the first two GEMMs of the gated FFN chain
-    ``ffn_gated`` (fusion.py:44-46), X read once for both weights."""
+    ``ffn_gated`` (fusion.py:44-46), X read once for both weights.
+    `row_job` as for fused_linear."""
     act = activation_code(activation)
     if kernel not in nat.KERNEL_NAMES:
         raise ValueError(f"unknown kernel {kernel!r}; expected one of {list(nat.KERNEL_NAMES)}")
@@ -188,13 +198,16 @@ def fused_gated_linear(X: torch.Tensor, Wg: torch.Tensor, Wu: torch.Tensor,
         stream = torch.cuda.current_stream(X.device).cuda_stream
         ws = _workspace(X.device, stream,
                         lib.dx_fused_gated_linear_workspace_size(M, N, K, dtype, kcode))
-        rc = lib.dx_fused_gated_linear(
-            X.data_ptr(), Wg.data_ptr(), Wu.data_ptr(),
-            bias_g.data_ptr() if bias_g is not None else None,
-            bias_u.data_ptr() if bias_u is not None else None,
-            out.data_ptr(), M, N, K, _ld(X), _ld(Wg), _ld(Wu), _ld(out), dtype, act, kcode,
-            ws.data_ptr() if ws is not None else None,
-            ws.numel() if ws is not None else 0, stream)
+        args = (X.data_ptr(), Wg.data_ptr(), Wu.data_ptr(),
+                bias_g.data_ptr() if bias_g is not None else None,
+                bias_u.data_ptr() if bias_u is not None else None,
+                out.data_ptr(), M, N, K, _ld(X), _ld(Wg), _ld(Wu), _ld(out), dtype, act, kcode,
+                ws.data_ptr() if ws is not None else None,
+                ws.numel() if ws is not None else 0)
+        if row_job is None:
+            rc = lib.dx_fused_gated_linear(*args, stream)
+        else:
+            rc = lib.dx_fused_gated_linear_rowjob(*args, ctypes.byref(row_job), stream)
     nat.check("dx_fused_gated_linear", rc)
     return out
 
@@ -383,28 +396,35 @@ def reduce_broadcast(partial: torch.Tensor, p_ptrs, rank: int, rows_per_rank: in
 
 
 def row_flag_words() -> int:
-    """int32 flag words each rank's flag buffer needs for row_reduce."""
+    """int32 flag words each rank's flag buffer needs for a row-reduction job."""
     return int(nat.load().dx_row_flag_words())
 
 
-def row_reduce(p_ptrs, s_ptrs, f_ptrs, rank: int, M: int, N: int, ldp: int,
-               reduce_chunk: tuple[int, int, int] | None,
-               gather_chunk: tuple[int, int, int] | None,
-               bias: torch.Tensor | None, residual: torch.Tensor | None, out: torch.Tensor,
-               epoch: int, dtype: torch.dtype, stream: int, grid: int = 0) -> None:
-    """One call of the chunked row-parallel reduction (dx_row_reduce) on
-    `stream`: reduce-scatter of `reduce_chunk` and all-gather of
-    `gather_chunk`, each given as (first row, rows, chunk index) or None.
-    `p_ptrs` / `s_ptrs` / `f_ptrs` are the peer-mapped addresses of every
-    rank's partial, slab and flag buffers; `out` is this rank's output."""
+def row_job(p_ptrs, s_ptrs, f_ptrs, rank: int, M: int, N: int, ldp: int,
+            reduce_chunk: tuple[int, int, int] | None,
+            gather_chunk: tuple[int, int, int] | None,
+            bias: torch.Tensor | None, residual: torch.Tensor | None, out: torch.Tensor,
+            epoch: int, dtype: torch.dtype) -> "nat.RowReduceJob":
+    """One job of the chunked row-parallel reduction (dx_row_reduce_job):
+    reduce-scatter of `reduce_chunk` and all-gather of `gather_chunk`, each
+    given as (first row, rows, chunk index) or None.  `p_ptrs` / `s_ptrs` /
+    `f_ptrs` are the peer-mapped addresses of every rank's partial, slab and
+    flag buffers; `out` is this rank's output."""
+    j = nat.RowReduceJob()
     world = len(p_ptrs)
-    a0, an, ac = reduce_chunk if reduce_chunk is not None else (0, 0, 0)
-    b0, bn, bc = gather_chunk if gather_chunk is not None else (0, 0, 0)
-    rc = nat.load().dx_row_reduce(
-        _ptr_array(p_ptrs), _ptr_array(s_ptrs), _ptr_array(f_ptrs), world, rank, M, N, ldp,
-        a0, an, ac, b0, bn, bc,
-        bias.data_ptr() if bias is not None else None,
-        residual.data_ptr() if residual is not None else None,
-        _ld(residual) if residual is not None else 0, out.data_ptr(), _ld(out), epoch, grid,
-        DTYPE_CODES[dtype], stream)
-    nat.check("dx_row_reduce", rc)
+    for r in range(world):
+        j.P[r], j.S[r], j.F[r] = p_ptrs[r], s_ptrs[r], f_ptrs[r]
+    j.world, j.rank, j.M, j.N, j.ldp = world, rank, M, N, ldp
+    j.a_row0, j.a_rows, j.a_chunk = reduce_chunk if reduce_chunk is not None else (0, 0, 0)
+    j.b_row0, j.b_rows, j.b_chunk = gather_chunk if gather_chunk is not None else (0, 0, 0)
+    j.bias = bias.data_ptr() if bias is not None else None
+    j.R = residual.data_ptr() if residual is not None else None
+    j.ldr = _ld(residual) if residual is not None else 0
+    j.Y, j.ldy = out.data_ptr(), _ld(out)
+    j.epoch, j.dtype = epoch, DTYPE_CODES[dtype]
+    return j
+
+
+def row_reduce(job: "nat.RowReduceJob", stream: int, grid: int = 0) -> None:
+    """Run a row-reduction job as its own launch on `stream` (dx_row_reduce)."""
+    nat.check("dx_row_reduce", nat.load().dx_row_reduce(ctypes.byref(job), grid, stream))

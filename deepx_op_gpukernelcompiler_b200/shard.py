@@ -12,12 +12,13 @@ standard way, one process per GPU over ``torch.distributed`` (NCCL on GPUs):
   H_r = act(X W1_r + b1_r) stays local and Y = sum_r H_r W2_r needs one
   all-reduce.  Two implementations:
     - ``mode="fused"`` (GPUs, default): the rows are cut into chunks; each
-      chunk's two GEMMs run on the main stream, the second writing its
-      partial into a peer-mapped (symmetric-memory) buffer, and one engine
-      kernel (dx_row_reduce) on a side stream reduce-scatters that chunk
-      over NVLink (peer loads, rank order, b2 and X added once) and gathers
-      the previous chunk, while the next chunk's GEMMs compute — no NCCL on
-      the path; the output is a buffer the caller owns;
+      chunk's two GEMMs run in turn, the second writing its partial into a
+      peer-mapped (symmetric-memory) buffer, and the following GEMM launches
+      carry that chunk's reduce-scatter and all-gather over NVLink (peer
+      loads, rank order, b2 and X added once) in their spare warps, so the
+      reduction of one chunk runs on the same SMs while the next chunk's
+      GEMMs compute — one stream, no NCCL on the path; the output is a
+      buffer the caller owns;
     - ``mode="nccl"``: b2 and X are fused into rank 0's second launch and
       Y is summed with NCCL all-reduce (in M-chunks issued asynchronously
       when ``chunks > 1``).  This mode also runs on CPU ranks (gloo), and
@@ -137,11 +138,56 @@ def first_groups(n_chunks: int, groups: int | None) -> list[tuple[int, int]]:
     return [(a, b) for a, b in zip(edges, edges[1:]) if b > a]
 
 
+def row_schedule(n_chunks: int, groups: list[tuple[int, int]]) -> list[tuple]:
+    """Launch order of one overlapped step, in stream order:
+
+    * ``("first", c0, c1, job)`` — the first GEMM for the rows of chunks
+      [c0, c1);
+    * ``("second", c, job)`` — chunk c's second GEMM (its partial);
+    * ``("reduce", job)`` — a reduction launch of its own (only at the end).
+
+    ``job = (a, b)`` names the chunk whose reduce-scatter (phase A) and the
+    chunk whose all-gather (phase B) the launch carries, or None.  A chunk's
+    phase A rides on the first launch after its second GEMM (the partial is
+    complete by then in stream order); its phase B on a later launch than its
+    phase A (so every rank's slab was announced in an earlier launch), except
+    at the very end, where one launch may do both."""
+    starts = dict(groups)
+    plan: list[tuple] = []
+    pending_a = None  # partial complete, reduce-scatter not carried yet
+    gathers: list[int] = []  # reduce-scatter carried by an earlier launch
+
+    def take():
+        nonlocal pending_a
+        a, pending_a = pending_a, None
+        return a, (gathers.pop(0) if gathers else None)
+
+    for c in range(n_chunks):
+        if c in starts:
+            job = take()
+            plan.append(("first", c, starts[c], job))
+            if job[0] is not None:
+                gathers.append(job[0])
+        job = take()
+        plan.append(("second", c, job))
+        if job[0] is not None:
+            gathers.append(job[0])
+        pending_a = c
+    while pending_a is not None or gathers:
+        a, pending_a = pending_a, None
+        if a is not None and not gathers:
+            plan.append(("reduce", (a, a)))
+        else:
+            plan.append(("reduce", (a, gathers.pop(0))))
+            if a is not None:
+                gathers.append(a)
+    return plan
+
+
 class _RowParallelBuffers:
     """Peer-mapped (symmetric-memory) buffers of the overlapped reduction for
     one (M, N, dtype): every rank's partial [M, N], slab buffer
-    [2 * M / world, N] and flag words, plus the side stream the reduction
-    runs on."""
+    [2 * M / world, N] and flag words."""
 
     def __init__(self, M: int, N: int, dtype, device, group):
         import torch.distributed._symmetric_memory as symm_mem
@@ -161,7 +207,6 @@ class _RowParallelBuffers:
         # Every rank's flags are zero before any peer stamps them.
         dist.barrier(group=group)
         self.epoch = 0
-        self.stream = torch.cuda.Stream(device)
 
 
 class _RowParallelOutput:
@@ -169,16 +214,17 @@ class _RowParallelOutput:
     classes: Y = sum_r H_r W2_r + b2 (+ R), W2_r this rank's row shard.
 
     ``mode="fused"`` (the default on GPUs with world > 1): the engine's
-    overlapped reduction.  The rows are cut into ``chunks`` chunks; on the
-    main stream each chunk's first GEMM (grouped into ``first_chunks``
-    launches) and second GEMM run in turn, the second writing its partial
-    into a peer-mapped buffer; after each, one dx_row_reduce launch on a side
-    stream reduce-scatters that chunk over NVLink (peer loads, rank order,
-    b2 and R added once) and gathers the previous chunk's slabs, concurrently
-    with the next chunk's GEMMs.  The result lands in a buffer the caller
-    owns (``out``, or a new tensor).  Shapes it cannot take (M not a
-    multiple of the world size, N not a multiple of 8, fp32, world > 8) run
-    the NCCL path instead.
+    overlapped reduction.  The rows are cut into ``chunks`` chunks; each
+    chunk's first GEMM (grouped into ``first_chunks`` launches) and second
+    GEMM run in turn on the caller's stream, the second writing its partial
+    into a peer-mapped buffer.  The next launch carries that chunk's
+    reduce-scatter over NVLink (peer loads, rank order, b2 and R added once)
+    and a later one its all-gather: the GEMM kernels' spare warps run them
+    while the tensor-core warps compute (row_schedule gives the order; the
+    last chunk's reduction runs as a launch of its own).  The result lands in
+    a buffer the caller owns (``out``, or a new tensor).  Shapes it cannot
+    take (M not a multiple of the world size, N not a multiple of 8, fp32,
+    world > 8) run the NCCL path instead.
     ``mode="nccl"``: the whole first GEMM, then the second in ``chunks``
     row chunks, each summed by an asynchronous NCCL all-reduce (b2 and R
     fused into rank 0's launch).  Also runs on CPU ranks (gloo)."""
@@ -237,7 +283,7 @@ class _RowParallelOutput:
 
     def _run_overlapped(self, first, M: int, H: torch.Tensor, R: torch.Tensor | None,
                         out: torch.Tensor | None) -> torch.Tensor:
-        from .linear import row_reduce
+        from .linear import fused_linear, row_job, row_reduce
         N = self.W2.shape[1]
         dev = H.device
         key = (M, N, H.dtype)
@@ -247,26 +293,30 @@ class _RowParallelOutput:
         bufs = self._bufs
         Y = out if out is not None else torch.empty((M, N), dtype=H.dtype, device=dev)
         chunks = row_chunks(M, self.world, self.chunks)
-        starts = {a: b for a, b in first_groups(len(chunks), self.first_chunks)}
-        main = torch.cuda.current_stream(dev)
-        side = bufs.stream
+        plan = row_schedule(len(chunks), first_groups(len(chunks), self.first_chunks))
         bufs.epoch += 1
-        common = dict(rank=self.rank, M=M, N=N, ldp=N, bias=self.b2_all, residual=R, out=Y,
-                      epoch=bufs.epoch, dtype=H.dtype, stream=side.cuda_stream)
-        ptrs = (bufs.part_ptrs, bufs.slab_ptrs, bufs.flag_ptrs)
-        side.wait_stream(main)  # Y, R and b2 are ready; earlier users of Y are done
-        prev = None
-        for j, (r0, rn) in enumerate(chunks):
-            if j in starts:
-                g0 = chunks[j][0]
-                g_last = chunks[starts[j] - 1]
-                first(g0, g_last[0] + g_last[1])
-            self.linear_fn(H[r0:r0 + rn], self.W2, None, None, out=bufs.part[r0:r0 + rn])
-            side.wait_stream(main)  # this chunk of the local partial is complete
-            row_reduce(*ptrs, reduce_chunk=(r0, rn, j), gather_chunk=prev, **common)
-            prev = (r0, rn, j)
-        row_reduce(*ptrs, reduce_chunk=None, gather_chunk=prev, **common)
-        main.wait_stream(side)
+
+        def job(ab):
+            a, b = ab
+            if a is None and b is None:
+                return None
+            return row_job(bufs.part_ptrs, bufs.slab_ptrs, bufs.flag_ptrs, self.rank, M, N, N,
+                           (chunks[a][0], chunks[a][1], a) if a is not None else None,
+                           (chunks[b][0], chunks[b][1], b) if b is not None else None,
+                           self.b2_all, R, Y, bufs.epoch, H.dtype)
+
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        for launch in plan:
+            if launch[0] == "first":
+                _, c0, c1, ab = launch
+                first(chunks[c0][0], chunks[c1 - 1][0] + chunks[c1 - 1][1], job(ab))
+            elif launch[0] == "second":
+                _, c, ab = launch
+                r0, rn = chunks[c]
+                fused_linear(H[r0:r0 + rn], self.W2, None, None, out=bufs.part[r0:r0 + rn],
+                             row_job=job(ab))
+            else:
+                row_reduce(job(launch[1]), stream)
         return Y
 
 
@@ -304,8 +354,9 @@ class ParallelMLP(_RowParallelOutput):
         H = hidden if hidden is not None else torch.empty(
             (M, self.W1.shape[1]), dtype=X.dtype, device=X.device)
 
-        def first(r0: int, r1: int) -> None:
-            self.linear_fn(X[r0:r1], self.W1, self.b1, self.activation, out=H[r0:r1])
+        def first(r0: int, r1: int, job=None) -> None:
+            kw = {"row_job": job} if job is not None else {}
+            self.linear_fn(X[r0:r1], self.W1, self.b1, self.activation, out=H[r0:r1], **kw)
 
         return self._run(first, M, H, X, out)
 
@@ -355,8 +406,9 @@ class ParallelGatedFFN(_RowParallelOutput):
         H = hidden if hidden is not None else torch.empty(
             (M, self.Wg.shape[1]), dtype=X.dtype, device=X.device)
 
-        def first(r0: int, r1: int) -> None:
+        def first(r0: int, r1: int, job=None) -> None:
+            kw = {"row_job": job} if job is not None else {}
             self.gated_fn(X[r0:r1], self.Wg, self.Wu, self.bg, self.bu, self.activation,
-                          out=H[r0:r1])
+                          out=H[r0:r1], **kw)
 
         return self._run(first, M, H, None, out)

@@ -125,39 +125,80 @@ int dx_reduce_broadcast(void* const* P, int world, int rank, int64_t rows_per_ra
  * Chunked, overlapped reduction of a row-parallel linear over `world` ranks
  * (no reference counterpart: the reference is single-GPU, and fusion.py:42-43
  * marks the two-layer FFN multi_kernel).  The second GEMM of the chain runs
- * in row chunks; after chunk `a_chunk` (rows a_row0 .. a_row0 + a_rows) of
- * the local partial is complete, one call on a side stream — while the next
- * chunk's GEMMs run on the caller's main stream — does
- *   phase A: announces the local partial chunk to every rank, waits until
- *     every rank's is complete, then sums this rank's slab of the chunk (rows
- *     a_row0 + rank * a_rows / world, a_rows / world of them) over all
- *     partials P[s] in rank order in fp32, adds bias[N] and R once, rounds,
- *     and writes the rows into Y and into its own slab buffer S[rank];
- *   phase B: for the chunk b_row0 .. b_row0 + b_rows reduced by an earlier
- *     call of the same step, waits until every rank has announced its slab
- *     and copies the other ranks' slabs from S[s] into Y.
- * a_rows = 0 or b_rows = 0 skips a phase; a step ends with a call that only
- * gathers its last chunk.  Only this rank writes Y, so Y is any caller-owned
- * device buffer [M][ldy].  P[s] ([M][ldp]), S[s] ([2 * M / world][N]) and
- * F[s] (dx_row_flag_words() int32 words, zeroed once before first use) are
- * rank s's buffers, mapped so every rank reaches them over NVLink.  `epoch`
- * numbers the step: the same positive value on every rank, one larger per
- * step; flags carry it, and its parity selects the half of S the step uses,
- * so a slab is never overwritten while a peer may still read it.  The caller
- * keeps steps apart on each rank: the main stream waits for the step's last
- * call before reusing P, and chunk indices of one step are distinct (< 64).
- * Chunk starts and sizes are multiples of `world`; N % 8 == 0; fp16/bf16.
- * grid <= 0 uses one CTA per SM.  Waits are bounded (2 s): on expiry the
- * call's kernel sets DX_DEVICE_STATUS_TIMEOUT and returns.
+ * in row chunks, each writing its partial Y into the rank's peer-mapped
+ * buffer P.  One job per chunk, on each rank, does
+ *   phase A (chunk a: rows a_row0 .. a_row0 + a_rows): announces the local
+ *     partial of the chunk to every rank, waits until every rank's is
+ *     complete, then sums this rank's slab of the chunk (rows a_row0 + rank *
+ *     a_rows / world, a_rows / world of them) over all partials P[s] in rank
+ *     order in fp32, adds bias[N] and R once, rounds, and writes the rows into
+ *     Y and into its own slab buffer S[rank];
+ *   phase B (chunk b, reduced by an earlier job of the same step): waits until
+ *     every rank has announced its slab and copies the other ranks' slabs from
+ *     S[s] into Y.
+ * a_rows = 0 or b_rows = 0 skips a phase.  Only this rank writes Y, so Y is
+ * any caller-owned device buffer [M][ldy].  P[s] ([M][ldp]), S[s]
+ * ([2 * M / world][N]) and F[s] (dx_row_flag_words() int32 words, zeroed once
+ * before first use) are rank s's buffers, mapped so every rank reaches them
+ * over NVLink.  `epoch` numbers the step: the same positive value on every
+ * rank, one larger per step; flags carry it, and its parity selects the half
+ * of S the step uses, so a slab is never overwritten while a peer may still
+ * read it.  The caller keeps steps apart on each rank (the stream that writes
+ * P waits for the step's last job before the next step writes P again), and
+ * gives the chunks of one step distinct indices (< 64).  Chunk starts and
+ * sizes are multiples of `world`; N % 8 == 0; fp16/bf16 (`dtype`).  Waits are
+ * bounded (2 s): on expiry the kernel sets DX_DEVICE_STATUS_TIMEOUT and
+ * returns.
  */
-int dx_row_reduce(void* const* P, void* const* S, int* const* F, int world, int rank,
-                  int64_t M, int64_t N, int64_t ldp,
-                  int64_t a_row0, int64_t a_rows, int a_chunk,
-                  int64_t b_row0, int64_t b_rows, int b_chunk,
-                  const void* bias, const void* R, int64_t ldr, void* Y, int64_t ldy,
-                  int epoch, int grid, int dtype, void* stream);
+typedef struct dx_row_reduce_job {
+  void* P[8];   /* every rank's partial buffer */
+  void* S[8];   /* every rank's slab buffer */
+  int* F[8];    /* every rank's flag words */
+  int world, rank;
+  int64_t M, N, ldp;
+  int64_t a_row0, a_rows;  /* phase A chunk (a_rows = 0: none) */
+  int a_chunk;
+  int64_t b_row0, b_rows;  /* phase B chunk (b_rows = 0: none) */
+  int b_chunk;
+  const void* bias;        /* [N] or NULL */
+  const void* R;           /* residual [M][ldr] or NULL */
+  int64_t ldr;
+  void* Y;                 /* this rank's output [M][ldy] */
+  int64_t ldy;
+  int epoch, dtype;
+} dx_row_reduce_job;
 
-/* int32 flag words dx_row_reduce needs in each rank's F buffer. */
+/* Runs a job as its own launch on `stream` (grid <= 0: one 512-thread CTA
+ * per SM).  Used for the last chunk of a step, which has no GEMM left to
+ * overlap. */
+int dx_row_reduce(const dx_row_reduce_job* job, int grid, void* stream);
+
+/* dx_fused_linear_ex that also carries `job` (may be NULL): when the launch is
+ * a tensor-core GEMM (DX_KERNEL_UMMA / DX_KERNEL_UMMA_1CTA), two spare warps
+ * per CTA run the job while the other warps compute the GEMM — the reduction
+ * of one chunk overlaps the next chunk's GEMM on the same SMs.  Otherwise the
+ * job runs as its own launch on `stream` right after the GEMM.  The job's
+ * phase-A chunk of P must be complete in stream order before this call (it
+ * is announced to the peers when the launch starts), and job->dtype must be
+ * the GEMM's dtype. */
+int dx_fused_linear_rowjob(const void* X, const void* W, const void* bias,
+                           const void* R, void* Y,
+                           int64_t M, int64_t N, int64_t K,
+                           int64_t ldx, int64_t ldw, int64_t ldr, int64_t ldy,
+                           int dtype, int act, int kernel,
+                           void* workspace, size_t workspace_bytes,
+                           const dx_row_reduce_job* job, void* stream);
+
+/* dx_fused_gated_linear carrying a job, as dx_fused_linear_rowjob. */
+int dx_fused_gated_linear_rowjob(const void* X, const void* Wg, const void* Wu,
+                                 const void* bias_g, const void* bias_u, void* Y,
+                                 int64_t M, int64_t N, int64_t K,
+                                 int64_t ldx, int64_t ldwg, int64_t ldwu, int64_t ldy,
+                                 int dtype, int act, int kernel,
+                                 void* workspace, size_t workspace_bytes,
+                                 const dx_row_reduce_job* job, void* stream);
+
+/* int32 flag words a job needs in each rank's F buffer. */
 int dx_row_flag_words(void);
 
 /* Skinny-M (decode) fused linear that allocates nothing.  No counterpart in

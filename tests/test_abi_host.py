@@ -216,3 +216,27 @@ def test_missing_library_fails_loudly(monkeypatch, tmp_path):
 def test_ctypes_types_match_header(lib):
     assert lib.dx_fused_linear.restype is ctypes.c_int
     assert lib.dx_fused_linear_workspace_size.restype is ctypes.c_size_t
+
+
+def test_row_reduce_job_layout_matches_header(tmp_path):
+    """The ctypes mirror of dx_row_reduce_job has the C compiler's layout."""
+    import shutil
+    import subprocess
+    from pathlib import Path
+    cc = shutil.which("gcc") or shutil.which("cc")
+    if cc is None:
+        pytest.skip("no C compiler")
+    fields = [f for f, _ in nat.RowReduceJob._fields_]
+    src = tmp_path / "layout.c"
+    body = "".join(f'printf("{f} %zu\\n", offsetof(dx_row_reduce_job, {f}));' for f in fields)
+    src.write_text('#include <stdio.h>\n#include <stddef.h>\n#include "deepx_fused.h"\n'
+                   'int main(void) {' + body +
+                   'printf("size %zu\\n", sizeof(dx_row_reduce_job)); return 0; }\n')
+    include = Path(__file__).resolve().parent.parent / "include"
+    exe = tmp_path / "layout"
+    subprocess.run([cc, f"-I{include}", str(src), "-o", str(exe)], check=True)
+    got = dict(line.split() for line in subprocess.run(
+        [str(exe)], check=True, capture_output=True, text=True).stdout.splitlines())
+    for f in fields:
+        assert int(got[f]) == getattr(nat.RowReduceJob, f).offset, f
+    assert int(got["size"]) == ctypes.sizeof(nat.RowReduceJob)
