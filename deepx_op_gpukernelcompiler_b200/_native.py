@@ -87,6 +87,7 @@ SIGNATURES = {
     "dx_set_trace_buffer": (ctypes.c_int, [_vp, ctypes.c_size_t]),
     "dx_device_status": (ctypes.c_int, [_vp, ctypes.POINTER(ctypes.c_int)]),
     "dx_version": (ctypes.c_int, []),
+    "dx_kernel_arch": (ctypes.c_int, [ctypes.POINTER(ctypes.c_int), ctypes.POINTER(ctypes.c_int)]),
     "dx_selftest_bounded_wait": (ctypes.c_int, [_vp, _vp]),
     "dx_plan_create": (ctypes.c_int, [ctypes.POINTER(ctypes.c_void_p), _i64, _i64, _i64,
                                       ctypes.c_int, ctypes.c_int, ctypes.c_float, ctypes.c_int]),

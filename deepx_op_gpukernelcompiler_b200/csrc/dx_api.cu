@@ -85,10 +85,40 @@ bool load_encode_fn() {
   return g_encode != nullptr;
 }
 
+// Unique id of the calling thread's current CUDA context (0 if none is
+// current yet).  Device-side state of this library — the module's __device__
+// variables, function attributes — belongs to a context, and a device can
+// have several over a process's life (cudaDeviceReset, or a caller's own
+// context), so caches of that state are keyed by this id, which the driver
+// never reuses within a process.
+PFN_cuCtxGetCurrent_v4000 g_ctx_current = nullptr;
+PFN_cuCtxGetId_v12000 g_ctx_id = nullptr;
+std::once_flag g_ctx_once;
+
+unsigned long long current_context_id() {
+  std::call_once(g_ctx_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_current = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuCtxGetId", &fn, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_ctx_id = reinterpret_cast<PFN_cuCtxGetId_v12000>(fn);
+  });
+  CUcontext ctx = nullptr;
+  unsigned long long id = 0;
+  if (g_ctx_current == nullptr || g_ctx_id == nullptr || g_ctx_current(&ctx) != CUDA_SUCCESS ||
+      ctx == nullptr || g_ctx_id(ctx, &id) != CUDA_SUCCESS)
+    return 0;
+  return id;
+}
+
 // --------------------------------------------------------- device facts
 std::mutex g_mu;
 std::map<int, int> g_sm_count;
-std::map<std::pair<int, const void*>, bool> g_attr_done;
+std::map<std::pair<unsigned long long, const void*>, bool> g_attr_done;
 
 int device_sms(int dev, int* sms) {
   std::lock_guard<std::mutex> lk(g_mu);
@@ -112,12 +142,13 @@ int device_sms(int dev, int* sms) {
 // point reads its device's word before launching, without synchronising.
 constexpr int kMaxDevices = 64;
 int* g_host_status = nullptr;  // kMaxDevices words, pinned and mapped
-bool g_mirror_installed[kMaxDevices] = {};
+std::map<unsigned long long, bool> g_mirror_installed;  // by context id
 
 int install_status_mirror(int dev, cudaStream_t s) {
   if (dev < 0 || dev >= kMaxDevices) return DX_OK;
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lk(g_mu);
-  if (g_mirror_installed[dev]) return DX_OK;
+  if (ctx != 0 && g_mirror_installed.count(ctx)) return DX_OK;
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(s, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) {
     (void)cudaGetLastError();
@@ -136,7 +167,8 @@ int install_status_mirror(int dev, cudaStream_t s) {
   if (e != cudaSuccess) return cuda_fail(e, "cudaHostGetDevicePointer(status mirror)");
   e = cudaMemcpyToSymbol(dx::g_status_mirror, &dptr, sizeof(dptr));
   if (e != cudaSuccess) return cuda_fail(e, "install status mirror");
-  g_mirror_installed[dev] = true;
+  const unsigned long long now = current_context_id();  // the copy made one current
+  if (now != 0) g_mirror_installed[now] = true;
   return DX_OK;
 }
 
@@ -153,8 +185,10 @@ int check_status_mirror(int dev) {
 }
 
 int ensure_smem_attr(int dev, const void* fn, int smem_bytes, bool max_carveout) {
+  (void)dev;
+  const unsigned long long ctx = current_context_id();
   std::lock_guard<std::mutex> lk(g_mu);
-  auto key = std::make_pair(dev, fn);
+  auto key = std::make_pair(ctx, fn);
   if (g_attr_done.count(key)) return DX_OK;
   cudaError_t e =
       cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, smem_bytes);
@@ -164,7 +198,7 @@ int ensure_smem_attr(int dev, const void* fn, int smem_bytes, bool max_carveout)
                              cudaSharedmemCarveoutMaxShared);
     if (e != cudaSuccess) return cuda_fail(e, "cudaFuncSetAttribute(carveout)");
   }
-  g_attr_done[key] = true;
+  if (ctx != 0) g_attr_done[key] = true;  // no context yet: set again next time
   return DX_OK;
 }
 
@@ -1236,6 +1270,19 @@ int dx_selftest_bounded_wait(int* result, void* stream) {
   return DX_OK;
 }
 
+int dx_kernel_arch(int* binary_version, int* ptx_version) {
+  t_last_error.clear();
+  if (binary_version == nullptr || ptx_version == nullptr)
+    return fail(DX_ERR_INVALID_ARGUMENT, "dx_kernel_arch: NULL output");
+  cudaFuncAttributes fa{};
+  const cudaError_t e = cudaFuncGetAttributes(
+      &fa, reinterpret_cast<const void*>(dx::umma2_fused_linear_kernel<256, __nv_bfloat16>));
+  if (e != cudaSuccess) return cuda_fail(e, "cudaFuncGetAttributes");
+  *binary_version = fa.binaryVersion;
+  *ptx_version = fa.ptxVersion;
+  return DX_OK;
+}
+
 int dx_version(void) { return 100; }
 
 }  // extern "C"
@@ -1253,11 +1300,14 @@ int dx_version(void) { return 100; }
 // kStaticScratchBytes large; every GPU that loads the library holds it until
 // the process exits.
 //
-// Set-up: the first call on a device resolves the array's device address
-// with cudaGetSymbolAddress while that device is current, and caches it.
-// Make that first call before any stream capture.
+// Set-up: the first split-K call in a context (normally once per device)
+// resolves the array's device address with cudaGetSymbolAddress while that
+// device is current, and caches it by context.  Make that first call before
+// any stream capture.
 // All calls on a device share the array and it keeps the last call's
-// contents; the tickets are cleared on the caller's stream at every call.
+// contents; a split-K call clears the tickets on the caller's stream (the
+// partial sums are written before they are read); a call whose plan streams
+// whole tiles uses no scratch and clears nothing.
 // Calls that overlap on the GPU (different streams, or concurrent host
 // threads) race on the shared scratch — serialise them.
 // =========================================================================
@@ -1267,12 +1317,15 @@ constexpr size_t kStaticScratchBytes = size_t(8) << 20;  // 8 MiB per device
 static __device__ __align__(256) unsigned char g_static_decode_scratch[kStaticScratchBytes];
 
 std::mutex g_static_scratch_mu;
-std::map<int, void*> g_static_scratch_addr;
+std::map<unsigned long long, void*> g_static_scratch_addr;  // by context id
 
-// Device address of the static scratch on device `dev` (current device).
-int static_scratch_address(int dev, void** out) {
+// Device address of the static scratch in the current context.  Each context
+// holds its own copy of the array (the module is loaded per context), so the
+// address is cached per context id, not per device ordinal.
+int static_scratch_address(void** out) {
   std::lock_guard<std::mutex> lk(g_static_scratch_mu);
-  auto it = g_static_scratch_addr.find(dev);
+  const unsigned long long ctx = current_context_id();
+  auto it = ctx != 0 ? g_static_scratch_addr.find(ctx) : g_static_scratch_addr.end();
   if (it != g_static_scratch_addr.end()) {
     *out = it->second;
     return DX_OK;
@@ -1281,7 +1334,8 @@ int static_scratch_address(int dev, void** out) {
   cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_decode_scratch);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress(static decode scratch)");
   if (ptr == nullptr) return fail(DX_ERR_CUDA, "static decode scratch has no device address");
-  g_static_scratch_addr[dev] = ptr;
+  const unsigned long long now = current_context_id();  // current after the runtime call
+  if (now != 0) g_static_scratch_addr[now] = ptr;
   *out = ptr;
   return DX_OK;
 }
@@ -1317,14 +1371,17 @@ extern "C" int dx_fused_linear_decode_noalloc(const void* X, const void* W, cons
                 d.bytes, kStaticScratchBytes);
   if (!load_encode_fn())
     return fail(DX_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
-  void* scratch = nullptr;
-  if ((rc = static_scratch_address(dev, &scratch))) return rc;
-  // The tickets must start at zero (an aborted earlier call may have left
-  // some set); the partial sums are always written before they are read.
-  e = cudaMemsetAsync(scratch, 0, d.ticket_bytes, p.stream);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(static decode scratch tickets)");
-  p.ws = scratch;
-  p.ws_bytes = kStaticScratchBytes;
+  if (d.bytes > 0) {
+    // Split-K plan: its tickets must start at zero (an aborted earlier call
+    // may have left some set); the partial sums are always written before
+    // they are read.  A whole-tile plan touches no scratch at all.
+    void* scratch = nullptr;
+    if ((rc = static_scratch_address(&scratch))) return rc;
+    e = cudaMemsetAsync(scratch, 0, d.ticket_bytes, p.stream);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(static decode scratch tickets)");
+    p.ws = scratch;
+    p.ws_bytes = kStaticScratchBytes;
+  }
   if (dtype == DX_DTYPE_F16) {
     if (d.mn == 16) return launch_decode<16, __half>(p, dev, sms, d);
     if (d.mn == 32) return launch_decode<32, __half>(p, dev, sms, d);

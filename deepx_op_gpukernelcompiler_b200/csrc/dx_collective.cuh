@@ -190,15 +190,50 @@ __device__ __forceinline__ bool row_wait_flags(const int* flags, int first, int 
   return true;
 }
 
+// Sums W partials of one 16-byte column group (rank order, fp32), adds bias
+// and residual, rounds.  W is the world size when known at compile time, or
+// kRowMaxWorld with `world` bounding the ranks used.
+template <typename T, int W>
+__device__ __forceinline__ uint4 row_finish(const uint4 (&part)[W], int world, const T* bias,
+                                           const T* R, long long roff, int c8) {
+  using Tr = ElemTraits<T>;
+  float acc[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) acc[j] = 0.0f;
+  auto add = [&acc](const uint4& w) {
+    const uint32_t wv[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float2 f = Tr::unpack2(wv[h]);
+      acc[2 * h] += f.x;
+      acc[2 * h + 1] += f.y;
+    }
+  };
+#pragma unroll
+  for (int src = 0; src < W; ++src)
+    if (W < kRowMaxWorld || src < world) add(part[src]);  // rank order
+  if (bias != nullptr) add(__ldg(reinterpret_cast<const uint4*>(bias + c8)));
+  if (R != nullptr) add(__ldcs(reinterpret_cast<const uint4*>(R + roff)));
+  uint4 out;
+  out.x = Tr::pack2(acc[0], acc[1]);
+  out.y = Tr::pack2(acc[2], acc[3]);
+  out.z = Tr::pack2(acc[4], acc[5]);
+  out.w = Tr::pack2(acc[6], acc[7]);
+  return out;
+}
+
 // The work of one reduction call, spread over `lanes` threads of the grid:
 // `gl` is this thread's index among them and `warps` = lanes / 32.  Runs at
 // warp granularity (no block-wide barrier), so it serves both the standalone
-// kernel and the spare warps of a tensor-core GEMM launch.  UA / UB: column
-// groups each thread keeps in flight in phase A / phase B.  Returns early
-// (status word set) if a wait ran out.
-template <typename T, int UA, int UB>
-__device__ __forceinline__ void row_reduce_lanes(const RowReduceArgs& a, long long gl,
-                                                 long long lanes, int warps) {
+// kernel and the spare warps of a tensor-core GEMM launch.  The loads are
+// latency-bound (a peer's memory is microseconds away), so each thread keeps
+// many 16-byte loads in flight: UA column groups x W ranks in phase A, UB
+// groups in phase B.  W is the world size when it is 2, 4 or 8 (then the
+// loops are fully unrolled), else kRowMaxWorld with a run-time bound.
+// Returns early (status word set) if a wait ran out.
+template <typename T, int W, int UA, int UB>
+__device__ __forceinline__ void row_reduce_lanes_w(const RowReduceArgs& a, long long gl,
+                                                   long long lanes, int warps) {
   const int lane = threadIdx.x & 31;
   const int groups = a.N / 8;  // 16-byte column groups per row
   T* const Y = static_cast<T*>(a.Y);
@@ -224,7 +259,7 @@ __device__ __forceinline__ void row_reduce_lanes(const RowReduceArgs& a, long lo
     const T* const R = static_cast<const T*>(a.R);
     T* const Sown = static_cast<T*>(a.S.p[a.rank]);
     for (long long i0 = gl; i0 < total; i0 += UA * lanes) {
-      uint4 part[UA][kRowMaxWorld];
+      uint4 part[UA][W];
 #pragma unroll
       for (int u = 0; u < UA; ++u) {
         const long long i = i0 + u * lanes;
@@ -232,8 +267,8 @@ __device__ __forceinline__ void row_reduce_lanes(const RowReduceArgs& a, long lo
           const int r = static_cast<int>(i / groups);
           const int c8 = static_cast<int>(i - static_cast<long long>(r) * groups) * 8;
 #pragma unroll
-          for (int src = 0; src < kRowMaxWorld; ++src)
-            if (src < a.world)
+          for (int src = 0; src < W; ++src)
+            if (W < kRowMaxWorld || src < a.world)
               part[u][src] = __ldcg(reinterpret_cast<const uint4*>(
                   static_cast<const T*>(a.P.p[src]) + (row0 + r) * a.ldp + c8));
         }
@@ -244,7 +279,7 @@ __device__ __forceinline__ void row_reduce_lanes(const RowReduceArgs& a, long lo
         if (i < total) {
           const int r = static_cast<int>(i / groups);
           const int c8 = static_cast<int>(i - static_cast<long long>(r) * groups) * 8;
-          const uint4 o = rb_finish<T>(part[u], a.world, bias, R, (row0 + r) * a.ldr + c8, c8);
+          const uint4 o = row_finish<T, W>(part[u], a.world, bias, R, (row0 + r) * a.ldr + c8, c8);
           __stcs(reinterpret_cast<uint4*>(Y + (row0 + r) * a.ldy + c8), o);
           __stcg(reinterpret_cast<uint4*>(Sown + (srow0 + r) * static_cast<long long>(a.N) + c8),
                  o);
@@ -299,13 +334,25 @@ __device__ __forceinline__ void row_reduce_lanes(const RowReduceArgs& a, long lo
   }
 }
 
+// About 16 loads of 16 bytes in flight per thread in either phase.
+template <typename T>
+__device__ __forceinline__ void row_reduce_lanes(const RowReduceArgs& a, long long gl,
+                                                 long long lanes, int warps) {
+  switch (a.world) {
+    case 2: row_reduce_lanes_w<T, 2, 8, 16>(a, gl, lanes, warps); break;
+    case 4: row_reduce_lanes_w<T, 4, 4, 16>(a, gl, lanes, warps); break;
+    case 8: row_reduce_lanes_w<T, 8, 2, 16>(a, gl, lanes, warps); break;
+    default: row_reduce_lanes_w<T, kRowMaxWorld, 2, 16>(a, gl, lanes, warps); break;
+  }
+}
+
 // Standalone form: the call that ends a step (the last chunk, with nothing
 // left to overlap), or a job whose GEMM launch could not carry it.
 template <typename T>
 __global__ void __launch_bounds__(kRowThreads, 1) row_reduce_kernel(const RowReduceArgs a) {
   const long long lanes = static_cast<long long>(gridDim.x) * kRowThreads;
-  row_reduce_lanes<T, 2, 8>(a, static_cast<long long>(blockIdx.x) * kRowThreads + threadIdx.x,
-                            lanes, static_cast<int>(lanes / 32));
+  row_reduce_lanes<T>(a, static_cast<long long>(blockIdx.x) * kRowThreads + threadIdx.x, lanes,
+                      static_cast<int>(lanes / 32));
 }
 
 }  // namespace dx

@@ -24,7 +24,10 @@ dispatcher) sees which versions exist and how to call them.  Supported patterns:
 every ``linear*`` pattern, ``linear_residual``, and the single-GEMM
 ``needs_template`` neighbours the engine runs on the same kernels:
 ``attention_output`` (a plain GEMM) and ``attention_score`` (GEMM times a
-scale; the request's optional ``"scale"`` gives its value).
+scale; the request's optional ``"scale"`` gives its value).  The two-GEMM
+``mlp_residual`` chain (Y = GELU(X W1 + b1) W2 + b2 + X; inputs X[M,K],
+W1[K,H], b1[H], W2[H,K], b2[K]) compiles into two native plans, the second
+taking X as its residual; its record lists both calls.
 """
 from __future__ import annotations
 
@@ -54,6 +57,9 @@ PLAN_PATTERNS = {
     "attention_output": (None, False, False),
     "attention_score": (None, False, False),
 }
+# Chains of two plans: pattern -> activation of the first GEMM.  For these a
+# request's N is the hidden width H and the output is [M, K].
+CHAIN_PATTERNS = {"mlp_residual": "gelu"}
 
 
 class CompileError(ValueError):
@@ -84,8 +90,14 @@ class CompileRequest:
 
     def to_json(self) -> dict:
         """A compile request that parses back to this one."""
-        _, has_bias, has_res = PLAN_PATTERNS[self.pattern]
         dt = DTYPE_OF[self.dtype]
+        if self.pattern in CHAIN_PATTERNS:
+            M, H, K = self.M, self.N, self.K
+            inputs = [{"shape": s_, "dtype": dt} for s_ in ([M, K], [K, H], [H], [H, K], [K])]
+            return {"func": self.func, "pattern": self.pattern, "ops": list(self.ops),
+                    "inputs": inputs, "outputs": [{"shape": [M, K], "dtype": dt}],
+                    "accum_dtype": "float32", "scale": self.scale}
+        _, has_bias, has_res = PLAN_PATTERNS[self.pattern]
         inputs = [{"shape": [self.M, self.K], "dtype": dt}, {"shape": [self.K, self.N], "dtype": dt}]
         if has_bias:
             inputs.append({"shape": [self.N], "dtype": dt})
@@ -111,11 +123,13 @@ class CompileRequest:
         row = FUSION_DB.get(chain)
         if row is None or row[0] != pattern:
             raise CompileError(f"ops {list(ops)} do not form pattern {pattern!r}")
-        if pattern not in PLAN_PATTERNS:
-            raise CompileError(f"pattern {pattern!r} is not a single fused GEMM "
-                               f"(status {row[2]})")
+        if pattern not in PLAN_PATTERNS and pattern not in CHAIN_PATTERNS:
+            raise CompileError(f"pattern {pattern!r} is not a fused GEMM or chain the engine "
+                               f"plans (status {row[2]})")
         if req.get("accum_dtype", "float32") != "float32":
             raise CompileError("only float32 accumulation is supported")
+        if pattern in CHAIN_PATTERNS:
+            return cls._chain_from_json(req, pattern, ops, inputs, outputs)
         _, has_bias, has_res = PLAN_PATTERNS[pattern]
         n_in = 2 + int(has_bias) + int(has_res) + (1 if pattern == "attention_score" else 0)
         if len(inputs) != n_in or len(outputs) != 1:
@@ -134,6 +148,24 @@ class CompileRequest:
         if has_res and list(inputs[3]["shape"]) != [M, N]:
             raise CompileError(f"residual shape {inputs[3]['shape']} is not [{M}, {N}]")
         return cls(req.get("func", ""), pattern, ops, int(M), int(N), int(K),
+                   DTYPE_NAMES[next(iter(dtypes))], float(req.get("scale", 1.0)))
+
+    @classmethod
+    def _chain_from_json(cls, req, pattern, ops, inputs, outputs) -> "CompileRequest":
+        if len(inputs) != 5 or len(outputs) != 1:
+            raise CompileError(f"{pattern} takes 5 inputs (X, W1, b1, W2, b2) and 1 output, got "
+                               f"{len(inputs)} and {len(outputs)}")
+        dtypes = {t["dtype"] for t in list(inputs) + list(outputs)}
+        if len(dtypes) != 1 or next(iter(dtypes)) not in DTYPE_NAMES:
+            raise CompileError(f"inputs/outputs must share one of {list(DTYPE_NAMES)}")
+        (M, K), (K1, H) = inputs[0]["shape"], inputs[1]["shape"]
+        want = [[M, K], [K, H], [H], [H, K], [K]]
+        got = [list(t["shape"]) for t in inputs]
+        if K1 != K or got != want:
+            raise CompileError(f"{pattern} input shapes {got} are not {want}")
+        if list(outputs[0]["shape"]) != [M, K]:
+            raise CompileError(f"output shape {outputs[0]['shape']} is not [{M}, {K}]")
+        return cls(req.get("func", ""), pattern, ops, int(M), int(H), int(K),
                    DTYPE_NAMES[next(iter(dtypes))], float(req.get("scale", 1.0)))
 
 
@@ -186,6 +218,29 @@ class Plan:
         return out
 
 
+class ChainPlan:
+    """Two native plans for a two-GEMM chain (``mlp_residual``):
+    call(x, W1, b1, W2, b2, out=None, hidden=None) -> out, where
+    hidden = act(x W1 + b1) and out = hidden W2 + b2 + x."""
+
+    def __init__(self, request: CompileRequest, kernel: str = "auto"):
+        self.request = request
+        M, H, K, dt = request.M, request.N, request.K, request.dtype
+        act = CHAIN_PATTERNS[request.pattern]
+        up = CompileRequest(request.func, "linear_gelu", ("matmul", "add", "gelu"), M, H, K, dt)
+        down = CompileRequest(request.func, "linear_residual", ("matmul", "add", "add"), M, K, H,
+                              dt)
+        self.up = Plan(up, kernel)
+        self.down = Plan(down, kernel)
+        del act  # the up plan's activation (linear_gelu) is the chain's GELU
+
+    def __call__(self, x: torch.Tensor, W1: torch.Tensor, b1: torch.Tensor, W2: torch.Tensor,
+                 b2: torch.Tensor, out: torch.Tensor | None = None,
+                 hidden: torch.Tensor | None = None) -> torch.Tensor:
+        H = self.up(x, W1, b1, out=hidden)
+        return self.down(H, W2, b2, out=out, residual=x)
+
+
 def record_key(req: CompileRequest, prefix: str = "/func") -> str:
     """kvspace key of a compiled version: ``<prefix>/<func>_b200/<shape hash>``."""
     return f"{prefix.rstrip('/')}/{req.func or req.pattern}_b200/{req.shape_hash}"
@@ -194,6 +249,20 @@ def record_key(req: CompileRequest, prefix: str = "/func") -> str:
 def plan_record(req: CompileRequest) -> dict:
     """What a dispatcher needs to call a compiled version without Python."""
     lib = nat.load()
+    if req.pattern in CHAIN_PATTERNS:
+        names = {v: k for k, v in nat.KERNEL_NAMES.items()}
+        M, H, K = req.M, req.N, req.K
+        dt = DTYPE_CODES[req.dtype]
+        return {"request": req.to_json(), "shape_hash": req.shape_hash,
+                "library": nat.LIB_PATH.name, "abi_version": int(lib.dx_version()),
+                "create": "dx_plan_create",
+                "calls": [
+                    {"entry": "dx_plan_call", "M": M, "N": H, "K": K,
+                     "act": CHAIN_PATTERNS[req.pattern], "args": ["X", "W1", "b1", "hidden"],
+                     "kernel": names.get(lib.dx_select_kernel(M, H, K, dt), "?")},
+                    {"entry": "dx_plan_call_residual", "M": M, "N": K, "K": H, "act": None,
+                     "args": ["hidden", "W2", "b2", "X", "out"],
+                     "kernel": names.get(lib.dx_select_kernel(M, K, H, dt), "?")}]}
     kernel = lib.dx_select_kernel(req.M, req.N, req.K, DTYPE_CODES[req.dtype])
     names = {v: k for k, v in nat.KERNEL_NAMES.items()}
     return {"request": req.to_json(), "shape_hash": req.shape_hash,
@@ -213,7 +282,7 @@ class PlanCache:
     rebuilt from the stored request, which must match the one asked for."""
 
     def __init__(self, kv=None, prefix: str = "/func"):
-        self._plans: dict[tuple, Plan] = {}
+        self._plans: dict[tuple, Plan | ChainPlan] = {}
         self._lock = threading.Lock()
         self.kv = kv
         self.prefix = prefix
@@ -234,7 +303,7 @@ class PlanCache:
                                f"request (shape-hash collision)")
         return record
 
-    def get(self, request) -> Plan:
+    def get(self, request) -> "Plan | ChainPlan":
         req = request if isinstance(request, CompileRequest) else CompileRequest.from_json(request)
         with self._lock:
             plan = self._plans.get(req.key)
@@ -242,7 +311,7 @@ class PlanCache:
                 self.hits += 1
                 return plan
             stored = self._stored(req)
-            plan = Plan(req)
+            plan = ChainPlan(req) if req.pattern in CHAIN_PATTERNS else Plan(req)
             if stored is not None:
                 self.kv_hits += 1
             else:

@@ -209,9 +209,10 @@ int dx_row_flag_words(void);
  * with DX_KERNEL_DECODE (fp16/bf16, M <= 64, TMA-aligned X and W), but the
  * split-K scratch is a fixed 8 MiB device array inside the library; problems
  * whose scratch (the same bytes dx_fused_linear_workspace_size reports for
- * DX_KERNEL_DECODE) exceeds it return DX_ERR_WORKSPACE.  The first call on a device resolves that
- * array's address and should precede any stream capture; calls that overlap on
- * the GPU race on the shared array. */
+ * DX_KERNEL_DECODE) exceeds it return DX_ERR_WORKSPACE.  A plan that streams
+ * whole tiles uses no scratch.  The first split-K call in a context (once per
+ * device, normally) resolves the array's address and should precede any stream
+ * capture; calls that overlap on the GPU race on the shared array. */
 int dx_fused_linear_decode_noalloc(const void* X, const void* W, const void* bias,
                                    const void* R, void* Y,
                                    int64_t M, int64_t N, int64_t K,
@@ -320,6 +321,12 @@ int dx_selftest_bounded_wait(int* result, void* stream);
 /* Synchronises `stream`, then reads and clears the calling device's status
  * word (DX_DEVICE_STATUS_* bits) into *status. */
 int dx_device_status(void* stream, int* status);
+
+/* Architecture the library's kernels were compiled for, read from the loaded
+ * module on the current device (cudaFuncGetAttributes): *binary_version is
+ * 10 * major + minor of the SASS (100 for sm_100a) and *ptx_version that of
+ * any embedded PTX (0 when there is none). */
+int dx_kernel_arch(int* binary_version, int* ptx_version);
 
 /* ABI version: 100 * major + minor. */
 int dx_version(void);

@@ -1,9 +1,9 @@
 """Generate the golden fixtures under tests/golden/ from the reference itself.
 
-Run in a container that has the reference checkout (read-only) at
-/root/reference:
+Run where a checkout of the reference is readable, giving its root as the
+argument or in DEEPX_REFERENCE_DIR:
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py /path/to/deepx-op-gpukernelcompiler
 
 What it writes, and from which reference code:
 
@@ -36,6 +36,7 @@ from __future__ import annotations
 import importlib.util
 import json
 import math
+import os
 import sys
 import types
 from pathlib import Path
@@ -212,7 +213,11 @@ def make_numeric(fusion) -> tuple[dict, dict]:
 
 
 def main() -> None:
-    ref_root = Path(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("DEEPX_REFERENCE_DIR")
+    if not arg:
+        raise SystemExit("usage: make_golden.py <reference checkout root> "
+                         "(or set DEEPX_REFERENCE_DIR)")
+    ref_root = Path(arg)
     fusion, kvfunc = _import_reference(ref_root)
     (HERE / "reference_classify.json").write_text(
         json.dumps(make_classify(ref_root, fusion, kvfunc), indent=1, ensure_ascii=False) + "\n")

@@ -35,9 +35,11 @@ def test_every_declared_symbol_is_exported(lib):
     assert declared == set(nat.SIGNATURES), "ctypes signatures out of sync with the header"
 
 
-def test_library_is_sm100a_only():
-    lib_bytes = nat.LIB_PATH.read_bytes()
-    assert b"sm_100a" in lib_bytes
+def test_library_is_built_for_sm100a_only():
+    """The build compiles one target, sm_100a (the run-time check of the
+    loaded kernels' architecture is test_gpu_parity's dx_kernel_arch test)."""
+    from deepx_op_gpukernelcompiler_b200 import _build
+    assert _build.ARCH_FLAGS == ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
 def test_version(lib):

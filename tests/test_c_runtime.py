@@ -46,3 +46,4 @@ def test_runtime_demo_runs_plans(tmp_path):
     assert any(l.startswith("linear_relu M=512") and "bad=0" in l for l in lines)
     assert any(l.startswith("linear_gelu M=16") and "bad=0" in l and "workspace=0" not in l
                for l in lines)
+    assert any(l.startswith("mlp_residual M=256") and "bad=0" in l for l in lines)

@@ -423,3 +423,13 @@ def test_timeout_makes_the_next_call_raise():
     torch.cuda.synchronize()
     _assert_close(Y, oracle.fused_linear_f64(X, W, b, "silu"), torch.bfloat16, "after clear")
     _status_clean()
+
+
+def test_loaded_kernels_are_sm100a():
+    """The kernels the driver loaded from the library are SASS for sm_100
+    (binaryVersion 100), with no PTX that could be JIT-compiled instead."""
+    import ctypes
+    binv, ptxv = ctypes.c_int(0), ctypes.c_int(-1)
+    nat.check("dx_kernel_arch", nat.load().dx_kernel_arch(ctypes.byref(binv), ctypes.byref(ptxv)))
+    assert binv.value == 100
+    assert ptxv.value in (0, 100)

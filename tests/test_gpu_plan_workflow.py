@@ -98,3 +98,31 @@ def test_workflow_all(capsys):
     workflow.main(["--load", str(KV_DIR), "--all"])
     out = capsys.readouterr().out
     assert "summary" in out and "compilable: 7" in out
+
+
+def test_mlp_residual_chain_plan_and_record():
+    """cfg5's pattern through the compile-then-call runtime: two native plans
+    (dx_plan_call, then dx_plan_call_residual with X as the residual), and a
+    kvspace record that lists both calls for a non-Python dispatcher."""
+    M, K, H = 512, 256, 1024
+    dt = "bfloat16"
+    req = {"func": "mlp_block", "pattern": "mlp_residual",
+           "ops": ["matmul", "add", "gelu", "matmul", "add", "add"],
+           "inputs": [{"shape": s, "dtype": dt} for s in ([M, K], [K, H], [H], [H, K], [K])],
+           "outputs": [{"shape": [M, K], "dtype": dt}]}
+    store = KVSpace()
+    cache = PlanCache(store)
+    plan = cache.get(req)
+    g = torch.Generator().manual_seed(41)
+    X = torch.randn(M, K, generator=g).bfloat16()
+    W1 = (torch.randn(K, H, generator=g) / K ** 0.5).bfloat16()
+    b1 = (torch.rand(H, generator=g) * 0.2 - 0.1).bfloat16()
+    W2 = (torch.randn(H, K, generator=g) / H ** 0.5).bfloat16()
+    b2 = (torch.rand(K, generator=g) * 0.2 - 0.1).bfloat16()
+    Y = plan(X.to(DEV), W1.to(DEV), b1.to(DEV), W2.to(DEV), b2.to(DEV))
+    torch.cuda.synchronize()
+    ref = oracle.mlp_residual_f64(X, W1, b1, W2, b2, "gelu")
+    assert torch.allclose(Y.float().cpu(), torch.from_numpy(ref).float(), rtol=2e-2, atol=2e-2)
+    (record,) = cache.records("mlp_block").values()
+    assert [c["entry"] for c in record["calls"]] == ["dx_plan_call", "dx_plan_call_residual"]
+    assert cache.get(req) is plan and cache.hits == 1

@@ -30,7 +30,7 @@ def test_doc_example_parses():
 @pytest.mark.parametrize("mutate,msg", [
     (lambda r: r.update(ops=["matmul", "add", "gelu"]), "do not form"),
     (lambda r: r.update(pattern="ffn_two_layer", ops=["matmul", "add", "relu", "matmul", "add"]),
-     "not a single fused GEMM"),
+     "not a fused GEMM or chain the engine plans"),
     (lambda r: r["inputs"][1].update(shape=[255, 512]), "inner dimensions"),
     (lambda r: r["outputs"][0].update(shape=[512, 511]), "output shape"),
     (lambda r: r["inputs"][2].update(shape=[511]), "bias shape"),
@@ -150,3 +150,28 @@ def test_plan_cache_is_thread_safe():
     assert cache.hits == 32 * len(reqs) - len(reqs)
     for row in got:
         assert all(p is row[0] for p in row)
+
+
+def _mlp_request(M=512, K=256, H=1024, dt="bfloat16"):
+    return {"func": "mlp_block", "pattern": "mlp_residual",
+            "ops": ["matmul", "add", "gelu", "matmul", "add", "add"],
+            "inputs": [{"shape": s, "dtype": dt} for s in ([M, K], [K, H], [H], [H, K], [K])],
+            "outputs": [{"shape": [M, K], "dtype": dt}]}
+
+
+def test_mlp_residual_request_round_trips():
+    r = CompileRequest.from_json(_mlp_request())
+    assert (r.pattern, r.M, r.N, r.K) == ("mlp_residual", 512, 1024, 256)
+    assert CompileRequest.from_json(r.to_json()).key == r.key
+
+
+@pytest.mark.parametrize("mutate,msg", [
+    (lambda r: r["inputs"].pop(), "takes 5 inputs"),
+    (lambda r: r["inputs"][3].update(shape=[1024, 128]), "input shapes"),
+    (lambda r: r["outputs"][0].update(shape=[512, 1024]), "output shape"),
+])
+def test_mlp_residual_request_validation(mutate, msg):
+    req = _mlp_request()
+    mutate(req)
+    with pytest.raises(CompileError, match=msg):
+        CompileRequest.from_json(req)

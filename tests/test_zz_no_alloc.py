@@ -5,17 +5,21 @@ runtime whose own heap manager owns every device buffer hands the kernel only
 raw pointers and a stream, so it has no workspace to pass and may not call
 cudaMalloc behind its allocator's back.  ``dx_fused_linear_decode_noalloc``
 serves them: it runs the split-K decode kernel with its scratch in a fixed
-array inside the library.  Its output must match the workspace-taking entry
-point (``dx_fused_linear`` via ``fused_linear(kernel="decode")``) within the
-fp16/bf16 tolerance the parity tests use, on consecutive calls that reuse the
-shared scratch.
+array inside the library.  Its output must be bitwise equal to the
+workspace-taking entry point (``dx_fused_linear`` via
+``fused_linear(kernel="decode")``, which runs the same deterministic plan)
+and within the fp16/bf16 tolerance of the fp64 oracle, on consecutive calls
+that reuse the shared scratch — split-K plans of every row template (16, 32
+and 64 padded rows) and a whole-tile plan that needs no scratch.
 
 This file is collected last so that a failure here comes after every other
 test has run.
 """
+import numpy as np
 import pytest
 import torch
 
+import oracle
 from deepx_op_gpukernelcompiler_b200 import _native as nat
 from deepx_op_gpukernelcompiler_b200 import fused_linear
 
@@ -52,26 +56,38 @@ def _noalloc(X, W, b, R, act):
 
 def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
     # Consecutive calls with different shapes share the static scratch; the
-    # third repeats the first to show nothing stale carries over.
+    # last repeats the first to show nothing stale carries over.  Every
+    # split-K case must fit the 8 MiB array; the whole-tile case needs none.
+    lib = nat.load()
     calls = [
-        (16, 4096, 3072, torch.float16, "gelu_erf", 1, False),
-        (5, 2048, 1536, torch.bfloat16, "silu", 2, True),
-        (16, 4096, 3072, torch.float16, "gelu_erf", 1, False),
+        # M, K, N, dtype, act, seed, residual, split-K
+        (16, 4096, 3072, torch.float16, "gelu_erf", 1, False, True),
+        (5, 2048, 1536, torch.bfloat16, "silu", 2, True, True),
+        (24, 2048, 3072, torch.float16, "relu", 4, False, True),    # 32-row template
+        (48, 1024, 1536, torch.bfloat16, "gelu_erf", 5, True, True),  # 64-row template
+        (16, 1024, 28672, torch.float16, "silu", 6, False, False),  # whole tiles
+        (16, 4096, 3072, torch.float16, "gelu_erf", 1, False, True),
     ]
-    for M, K, N, dtype, act, seed, residual in calls:
+    for M, K, N, dtype, act, seed, residual, split in calls:
+        need = lib.dx_fused_linear_workspace_size(M, N, K, DTYPES[dtype], nat.DX_KERNEL_DECODE)
+        assert (0 < need <= (8 << 20)) if split else need == 0, (M, K, N, need)
         X, W, b, R = _inputs(M, K, N, dtype, seed, residual)
         got = _noalloc(X, W, b, R, act)
         want = fused_linear(X, W, b, act, residual=R, kernel="decode")
         torch.cuda.synchronize()
-        assert torch.allclose(got.float(), want.float(), rtol=RTOL, atol=ATOL), (
+        assert torch.equal(got, want), (
             f"{M}x{K}x{N} {dtype}: max |diff| {(got.float() - want.float()).abs().max().item()}")
+        ref = oracle.fused_linear_f64(X.cpu(), W.cpu(), b.cpu(), act,
+                                      residual=R.cpu() if R is not None else None)
+        np.testing.assert_allclose(got.float().cpu().numpy(), ref, rtol=RTOL, atol=ATOL,
+                                   err_msg=f"{M}x{K}x{N} {dtype} {act} against the fp64 oracle")
     assert nat.device_status(torch.cuda.current_stream(DEV).cuda_stream) == 0
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
     # 64 tiles of 256 columns (fewer than half the SMs, so K is split): up to
-    # 3 segments x 64 padded rows x 256 columns of fp32 partial sums per tile,
-    # 12.6 MiB > the 8 MiB array.
+    # 4 segments x 64 padded rows x 256 columns of fp32 partial sums per tile,
+    # 16 MiB > the 8 MiB array.
     M, K, N = 64, 8192, 16384
     lib = nat.load()
     assert lib.dx_fused_linear_workspace_size(M, N, K, nat.DX_DTYPE_F16,
