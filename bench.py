@@ -508,6 +508,7 @@ def run_gpu(args) -> None:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     if world > 1:
+        torch.cuda.synchronize()  # nothing of ours in flight before any rank leaves
         dist.barrier()
         dist.destroy_process_group()
 
@@ -721,6 +722,7 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
         mlp.chunks, mlp.first_chunks = chunks, first
         ms = time_run(lambda: mlp(X, hidden=H, out=Yo), 1500.0)
         assert mlp.last_path == "fused"
+        multicast = mlp.last_multicast
         parity["mlp_fused"] = _row_parallel_parity(X, first_ref, W2, b2, True, Yo, world, dev)
         tf = w.flops / (ms * 1e-3) / 1e12
         n_ch = len(row_chunks(w.M, world, chunks))
@@ -729,7 +731,9 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
                        "frac_of_peak": round(tf / world / tflops_peak, 4),
                        "parallelism": f"column->row x{world}, reduction carried by the GEMM "
                                       f"launches ({chunks} row chunks, first GEMM in {first} "
-                                      "launches; NVLink peer loads, dx_row_reduce_job)",
+                                      "launches; dx_row_reduce_job over NVLink "
+                                      + ("multicast: multimem.ld_reduce / multimem.st)"
+                                         if multicast else "peer loads)"),
                        "chunking_ms": sweep,
                        "gpu_launches_per_step": len(plan)}
         # The same chain with an NCCL all-reduce of Y in 4 asynchronous chunks.
@@ -742,6 +746,7 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
                                  "frac_of_peak": round(tf / world / tflops_peak, 4),
                                  "parallelism": f"column->row x{world} + NCCL all-reduce "
                                                 "(4 chunks)"}
+        mlp.release()
         del mlp, mlp_n, Yn
     del X, W1, b1, W2, b2, H, Yo
 
@@ -785,6 +790,8 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
         "parallelism": "one GPU" if world == 1 else
         f"column->row x{world}, reduction carried by the GEMM launches ({chunks} row chunks)",
         "gpu_launches_per_step": launches}
+    if world > 1:
+        ffn.release()
     return out
 
 

@@ -125,6 +125,10 @@ class RowReduceJob(ctypes.Structure):
         ("ldy", ctypes.c_int64),
         ("epoch", ctypes.c_int),
         ("dtype", ctypes.c_int),
+        ("mc_part", ctypes.c_void_p),
+        ("mc_out", ctypes.c_void_p),
+        ("out_sym", ctypes.c_void_p),
+        ("ldo", ctypes.c_int64),
     ]
 
 

@@ -831,9 +831,16 @@ int row_job_args(const dx_row_reduce_job* j, dx::RowReduceArgs* a) {
   if ((j->bias != nullptr && !aligned16(j->bias)) || (j->R != nullptr && !aligned16(j->R)) ||
       !aligned16(j->Y))
     return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce needs 16-byte-aligned bias, R and Y");
+  const bool nvls = j->mc_part != nullptr;
+  if (nvls && (j->mc_out == nullptr || j->out_sym == nullptr || !aligned16(j->mc_part) ||
+               !aligned16(j->mc_out) || !aligned16(j->out_sym) || j->ldo < N || j->ldo % 8 != 0))
+    return fail(DX_ERR_INVALID_ARGUMENT,
+                "row_reduce (multicast): mc_out and out_sym must be 16-byte aligned and ldo a "
+                "multiple of 8 no smaller than N");
   *a = dx::RowReduceArgs{};
   for (int r = 0; r < world; ++r) {
-    if (j->P[r] == nullptr || !aligned16(j->P[r]) || j->S[r] == nullptr || !aligned16(j->S[r]) ||
+    if (j->P[r] == nullptr || !aligned16(j->P[r]) ||
+        (!nvls && (j->S[r] == nullptr || !aligned16(j->S[r]))) ||
         j->F[r] == nullptr || (reinterpret_cast<uintptr_t>(j->F[r]) & 3u) != 0)
       return fail(DX_ERR_INVALID_ARGUMENT, "row_reduce: buffers of rank %d NULL or misaligned", r);
     a->P.p[r] = j->P[r];
@@ -857,6 +864,10 @@ int row_job_args(const dx_row_reduce_job* j, dx::RowReduceArgs* a) {
   a->R = j->R;
   a->Y = j->Y;
   a->epoch = j->epoch;
+  a->mc_part = j->mc_part;
+  a->mc_out = nvls ? j->mc_out : nullptr;
+  a->out_sym = nvls ? j->out_sym : nullptr;
+  a->ldo = nvls ? j->ldo : 0;
   return DX_OK;
 }
 

@@ -160,7 +160,47 @@ struct RowReduceArgs {
   const void* R;        // residual [M][ldr] or nullptr
   void* Y;              // this rank's output [M][ldy]
   int epoch;
+  // NVLink multicast (NVLS) form, when mc_part != nullptr: the multicast
+  // addresses of the partial buffers and of the peer-written output buffers
+  // (bound at the same offsets on every rank), and this rank's own view of
+  // the latter, pitch ldo.  The slab buffers S are then unused.
+  void* mc_part;
+  void* mc_out;
+  void* out_sym;
+  long long ldo;
 };
+
+// NVLS: the sum over every rank's copy of 16 bytes (8 fp16/bf16 values) at a
+// multicast address, accumulated in fp32 by the switch and rounded to T.
+template <typename T>
+__device__ __forceinline__ uint4 multimem_ld_reduce_add(const void* mc) {
+  uint4 v;
+  if constexpr (ElemTraits<T>::kIsBf16)
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.bf16x2 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(mc)
+                 : "memory");
+  else
+    asm volatile("multimem.ld_reduce.relaxed.sys.global.add.acc::f32.v4.f16x2 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(mc)
+                 : "memory");
+  return v;
+}
+
+// NVLS: 16 bytes stored at a multicast address land in every rank's copy.
+__device__ __forceinline__ void multimem_st16(void* mc, const uint4& v) {
+  asm volatile("multimem.st.relaxed.sys.global.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(mc),
+               "f"(__uint_as_float(v.x)), "f"(__uint_as_float(v.y)), "f"(__uint_as_float(v.z)),
+               "f"(__uint_as_float(v.w))
+               : "memory");
+}
+
+// Orders this thread's accesses through a multicast address with its
+// accesses to the same memory through the ordinary address.
+__device__ __forceinline__ void fence_proxy_alias() {
+  asm volatile("fence.proxy.alias;" ::: "memory");
+}
 
 __device__ __forceinline__ void st_release_sys(int* p, int v) {
   asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
@@ -250,6 +290,7 @@ __device__ __forceinline__ void row_reduce_lanes_w(const RowReduceArgs& a, long 
     if (lane == 0)
       ok = row_wait_flags(a.F.p[a.rank], row_part_flag(a.a_chunk, 0), a.world, -1, a.epoch);
     if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+    __syncwarp();  // lane 0's acquire orders the whole warp's reads after it
 
     const int slab = a.a_rows / a.world;
     const long long row0 = a.a_row0 + static_cast<long long>(a.rank) * slab;
@@ -258,6 +299,38 @@ __device__ __forceinline__ void row_reduce_lanes_w(const RowReduceArgs& a, long 
     const T* const bias = static_cast<const T*>(a.bias);
     const T* const R = static_cast<const T*>(a.R);
     T* const Sown = static_cast<T*>(a.S.p[a.rank]);
+    if (a.mc_part != nullptr) {
+      // The switch sums the ranks' partials; the finished rows go to this
+      // rank's output and, by one multicast store, to every rank's buffer.
+      constexpr int UN = 8;
+      const T* const mcp = static_cast<const T*>(a.mc_part);
+      T* const mco = static_cast<T*>(a.mc_out);
+      for (long long i0 = gl; i0 < total; i0 += UN * lanes) {
+        uint4 sum[UN];
+#pragma unroll
+        for (int u = 0; u < UN; ++u) {
+          const long long i = i0 + u * lanes;
+          if (i < total) {
+            const int r = static_cast<int>(i / groups);
+            const int c8 = static_cast<int>(i - static_cast<long long>(r) * groups) * 8;
+            sum[u] = multimem_ld_reduce_add<T>(mcp + (row0 + r) * a.ldp + c8);
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < UN; ++u) {
+          const long long i = i0 + u * lanes;
+          if (i < total) {
+            const int r = static_cast<int>(i / groups);
+            const int c8 = static_cast<int>(i - static_cast<long long>(r) * groups) * 8;
+            const uint4 parts[1] = {sum[u]};
+            const uint4 o = row_finish<T, 1>(parts, 1, bias, R, (row0 + r) * a.ldr + c8, c8);
+            __stcs(reinterpret_cast<uint4*>(Y + (row0 + r) * a.ldy + c8), o);
+            multimem_st16(mco + (row0 + r) * a.ldo + c8, o);
+          }
+        }
+      }
+      fence_proxy_alias();
+    } else
     for (long long i0 = gl; i0 < total; i0 += UA * lanes) {
       uint4 part[UA][W];
 #pragma unroll
@@ -305,10 +378,40 @@ __device__ __forceinline__ void row_reduce_lanes_w(const RowReduceArgs& a, long 
     if (lane == 0)
       ok = row_wait_flags(a.F.p[a.rank], row_red_flag(a.b_chunk, 0), a.world, a.rank, a.epoch);
     if (!__shfl_sync(0xffffffffu, ok, 0)) return;
+    __syncwarp();
     const int slab = a.b_rows / a.world;
     const long long srow0 = a.slab_base + a.b_row0 / a.world;
     const long long per_src = static_cast<long long>(slab) * groups;
     const long long total = per_src * (a.world - 1);
+    if (a.mc_part != nullptr) {
+      // The other ranks' slabs are already in this rank's multicast output
+      // buffer (their phase A stored them there): a local copy into Y.
+      fence_proxy_alias();
+      const T* const osym = static_cast<const T*>(a.out_sym);
+      for (long long i0 = gl; i0 < total; i0 += UB * lanes) {
+        uint4 v[UB];
+        long long dst[UB];
+#pragma unroll
+        for (int u = 0; u < UB; ++u) {
+          const long long i = i0 + u * lanes;
+          dst[u] = -1;
+          if (i < total) {
+            const int k = static_cast<int>(i / per_src);
+            const long long j = i - k * per_src;
+            const int src = k + (k >= a.rank ? 1 : 0);
+            const int r = static_cast<int>(j / groups);
+            const int c8 = static_cast<int>(j - static_cast<long long>(r) * groups) * 8;
+            const long long row = a.b_row0 + static_cast<long long>(src) * slab + r;
+            v[u] = __ldcg(reinterpret_cast<const uint4*>(osym + row * a.ldo + c8));
+            dst[u] = row * a.ldy + c8;
+          }
+        }
+#pragma unroll
+        for (int u = 0; u < UB; ++u)
+          if (dst[u] >= 0) __stcs(reinterpret_cast<uint4*>(Y + dst[u]), v[u]);
+      }
+      return;
+    }
     for (long long i0 = gl; i0 < total; i0 += UB * lanes) {
       uint4 v[UB];
       long long dst[UB];

@@ -404,16 +404,21 @@ def row_job(p_ptrs, s_ptrs, f_ptrs, rank: int, M: int, N: int, ldp: int,
             reduce_chunk: tuple[int, int, int] | None,
             gather_chunk: tuple[int, int, int] | None,
             bias: torch.Tensor | None, residual: torch.Tensor | None, out: torch.Tensor,
-            epoch: int, dtype: torch.dtype) -> "nat.RowReduceJob":
+            epoch: int, dtype: torch.dtype, mc_part: int = 0, mc_out: int = 0,
+            out_sym: torch.Tensor | None = None) -> "nat.RowReduceJob":
     """One job of the chunked row-parallel reduction (dx_row_reduce_job):
     reduce-scatter of `reduce_chunk` and all-gather of `gather_chunk`, each
     given as (first row, rows, chunk index) or None.  `p_ptrs` / `s_ptrs` /
     `f_ptrs` are the peer-mapped addresses of every rank's partial, slab and
-    flag buffers; `out` is this rank's output."""
+    flag buffers; `out` is this rank's output.  With `mc_part` (the NVLink
+    multicast address of the partial buffers) the job runs in the multicast
+    form: `mc_out` / `out_sym` are the multicast address and this rank's view
+    of the peer-written output buffer, and `s_ptrs` is unused."""
     j = nat.RowReduceJob()
     world = len(p_ptrs)
     for r in range(world):
-        j.P[r], j.S[r], j.F[r] = p_ptrs[r], s_ptrs[r], f_ptrs[r]
+        j.P[r], j.F[r] = p_ptrs[r], f_ptrs[r]
+        j.S[r] = s_ptrs[r] if s_ptrs is not None else None
     j.world, j.rank, j.M, j.N, j.ldp = world, rank, M, N, ldp
     j.a_row0, j.a_rows, j.a_chunk = reduce_chunk if reduce_chunk is not None else (0, 0, 0)
     j.b_row0, j.b_rows, j.b_chunk = gather_chunk if gather_chunk is not None else (0, 0, 0)
@@ -422,6 +427,9 @@ def row_job(p_ptrs, s_ptrs, f_ptrs, rank: int, M: int, N: int, ldp: int,
     j.ldr = _ld(residual) if residual is not None else 0
     j.Y, j.ldy = out.data_ptr(), _ld(out)
     j.epoch, j.dtype = epoch, DTYPE_CODES[dtype]
+    if mc_part:
+        j.mc_part, j.mc_out = mc_part, mc_out
+        j.out_sym, j.ldo = out_sym.data_ptr(), _ld(out_sym)
     return j
 
 

@@ -186,27 +186,66 @@ def row_schedule(n_chunks: int, groups: list[tuple[int, int]]) -> list[tuple]:
 
 class _RowParallelBuffers:
     """Peer-mapped (symmetric-memory) buffers of the overlapped reduction for
-    one (M, N, dtype): every rank's partial [M, N], slab buffer
-    [2 * M / world, N] and flag words."""
+    one (M, N, dtype): every rank's partial [M, N] and flag words, and either
+    (NVLink multicast form) a peer-written output [M, N] bound, like the
+    partials, to a multicast address, or (peer-load form) a slab buffer
+    [2 * M / world, N].  The multicast form is used when `nvls` allows it
+    and every rank's buffers have multicast addresses."""
 
-    def __init__(self, M: int, N: int, dtype, device, group):
+    def __init__(self, M: int, N: int, dtype, device, group, nvls: bool | None):
+        import os
+
         import torch.distributed._symmetric_memory as symm_mem
 
         from .linear import row_flag_words
         world = dist.get_world_size(group)
+        rank = dist.get_rank(group)
+        pg = group if group is not None else dist.group.WORLD
         self.key = (M, N, dtype)
         self.part = symm_mem.empty(M, N, dtype=dtype, device=device)
-        self.slab = symm_mem.empty(2 * M // world, N, dtype=dtype, device=device)
         self.flags = symm_mem.empty(row_flag_words(), dtype=torch.int32, device=device)
         self.flags.zero_()
         torch.cuda.current_stream(device).synchronize()
-        pg = group if group is not None else dist.group.WORLD
-        self.handles = [symm_mem.rendezvous(t, pg) for t in (self.part, self.slab, self.flags)]
-        self.part_ptrs, self.slab_ptrs, self.flag_ptrs = (list(h.buffer_ptrs)
-                                                          for h in self.handles)
+        self.handles = [symm_mem.rendezvous(t, pg) for t in (self.part, self.flags)]
+        self.part_ptrs = self._peer_ptrs(self.handles[0], self.part, rank)
+        self.flag_ptrs = self._peer_ptrs(self.handles[1], self.flags, rank)
+        self.mc_part = self.mc_out = 0
+        self.out_sym = None
+        self.slab_ptrs = None
+        if nvls is None:
+            nvls = os.environ.get("DX_ROW_NVLS", "1") != "0"
+        if nvls:
+            self.out_sym = symm_mem.empty(M, N, dtype=dtype, device=device)
+            h_out = symm_mem.rendezvous(self.out_sym, pg)
+            self.handles.append(h_out)
+            mc_p = self._mc_ptr(self.handles[0], self.part, rank)
+            mc_o = self._mc_ptr(h_out, self.out_sym, rank)
+            have = torch.tensor([1 if (mc_p and mc_o) else 0], device=device)
+            dist.all_reduce(have, op=dist.ReduceOp.MIN, group=group)
+            if int(have.item()):
+                self.mc_part, self.mc_out = mc_p, mc_o
+        if not self.mc_part:
+            self.slab = symm_mem.empty(2 * M // world, N, dtype=dtype, device=device)
+            h_slab = symm_mem.rendezvous(self.slab, pg)
+            self.handles.append(h_slab)
+            self.slab_ptrs = self._peer_ptrs(h_slab, self.slab, rank)
         # Every rank's flags are zero before any peer stamps them.
         dist.barrier(group=group)
         self.epoch = 0
+
+    @property
+    def multicast(self) -> bool:
+        return bool(self.mc_part)
+
+    @staticmethod
+    def _peer_ptrs(handle, t: torch.Tensor, rank: int) -> list[int]:
+        off = t.data_ptr() - int(handle.buffer_ptrs[rank])
+        return [int(p) + off for p in handle.buffer_ptrs]
+
+    @staticmethod
+    def _mc_ptr(handle, t: torch.Tensor, rank: int) -> int:
+        base = int(getattr(handle, "multicast_ptr", 0) or 0)
+        return base + (t.data_ptr() - int(handle.buffer_ptrs[rank])) if base else 0
 
 
 class _RowParallelOutput:
@@ -230,8 +269,9 @@ class _RowParallelOutput:
     fused into rank 0's launch).  Also runs on CPU ranks (gloo)."""
 
     def _init_output(self, W2_shard, b2_full, group, linear_fn, chunks, mode, on_gpu,
-                     first_chunks=None):
+                     first_chunks=None, nvls=None):
         self.group = group
+        self.nvls = nvls
         self.world, self.rank = _group_info(group)
         self.mode = mode or ("fused" if (linear_fn is None and on_gpu and self.world > 1)
                              else "nccl")
@@ -244,6 +284,7 @@ class _RowParallelOutput:
             4 if self.mode == "fused" else 1)
         self.first_chunks = first_chunks
         self.last_path = None  # "fused" or "nccl": what the last call ran
+        self.last_multicast = False  # the last fused call used NVLink multicast
 
     def _fused_ok(self, M: int, N: int, dtype) -> bool:
         return (self.mode == "fused" and 1 < self.world <= 8 and M % self.world == 0
@@ -255,11 +296,24 @@ class _RowParallelOutput:
         first GEMM), then the row-parallel second GEMM and its reduction."""
         N = self.W2.shape[1]
         if self._fused_ok(M, N, H.dtype):
+            Y = self._run_overlapped(first, M, H, R, out)
             self.last_path = "fused"
-            return self._run_overlapped(first, M, H, R, out)
+            self.last_multicast = self._bufs.multicast
+            return Y
         self.last_path = "nccl"
         first(0, M)
         return self._row_parallel_nccl(H, R, out)
+
+    def release(self) -> None:
+        """Drop the peer-mapped buffers.  Collective: every rank calls it,
+        with no step of this module in flight on any rank (it synchronises
+        the device and the group first), so no rank unmaps memory that a
+        peer's multicast or peer accesses may still reach."""
+        if self._bufs is not None:
+            torch.cuda.synchronize()
+            dist.barrier(group=self.group)
+            self._bufs = None
+            dist.barrier(group=self.group)
 
     def _row_parallel_nccl(self, H: torch.Tensor, R: torch.Tensor | None,
                            out: torch.Tensor | None) -> torch.Tensor:
@@ -289,7 +343,7 @@ class _RowParallelOutput:
         key = (M, N, H.dtype)
         if self._bufs is None or self._bufs.key != key:
             self._bufs = None
-            self._bufs = _RowParallelBuffers(M, N, H.dtype, dev, self.group)
+            self._bufs = _RowParallelBuffers(M, N, H.dtype, dev, self.group, self.nvls)
         bufs = self._bufs
         Y = out if out is not None else torch.empty((M, N), dtype=H.dtype, device=dev)
         chunks = row_chunks(M, self.world, self.chunks)
@@ -303,7 +357,8 @@ class _RowParallelOutput:
             return row_job(bufs.part_ptrs, bufs.slab_ptrs, bufs.flag_ptrs, self.rank, M, N, N,
                            (chunks[a][0], chunks[a][1], a) if a is not None else None,
                            (chunks[b][0], chunks[b][1], b) if b is not None else None,
-                           self.b2_all, R, Y, bufs.epoch, H.dtype)
+                           self.b2_all, R, Y, bufs.epoch, H.dtype, bufs.mc_part, bufs.mc_out,
+                           bufs.out_sym)
 
         stream = torch.cuda.current_stream(dev).cuda_stream
         for launch in plan:
@@ -325,7 +380,8 @@ class ParallelMLP(_RowParallelOutput):
 
     def __init__(self, W1_full, b1_full, W2_full, b2_full, activation="gelu", group=None,
                  linear_fn=None, chunks: int | None = None, align: int = 64,
-                 mode: str | None = None, first_chunks: int | None = None):
+                 mode: str | None = None, first_chunks: int | None = None,
+                 nvls: bool | None = None):
         world, rank = _group_info(group)
         hidden = W1_full.shape[1]
         if W2_full.shape[0] != hidden:
@@ -335,17 +391,18 @@ class ParallelMLP(_RowParallelOutput):
         self.b1 = b1_full[self.h0:self.h1].contiguous() if b1_full is not None else None
         self.activation = activation
         self._init_output(W2_full[self.h0:self.h1, :].contiguous(), b2_full, group, linear_fn,
-                          chunks, mode, on_gpu=W1_full.is_cuda, first_chunks=first_chunks)
+                          chunks, mode, on_gpu=W1_full.is_cuda, first_chunks=first_chunks,
+                          nvls=nvls)
 
     @classmethod
     def from_shards(cls, W1_shard, b1_shard, W2_shard, b2_full, activation="gelu", group=None,
                     linear_fn=None, chunks: int | None = None, mode: str | None = None,
-                    first_chunks: int | None = None):
+                    first_chunks: int | None = None, nvls: bool | None = None):
         self = cls.__new__(cls)
         self.W1, self.b1 = W1_shard, b1_shard
         self.activation = activation
         self._init_output(W2_shard, b2_full, group, linear_fn, chunks, mode,
-                          on_gpu=W1_shard.is_cuda, first_chunks=first_chunks)
+                          on_gpu=W1_shard.is_cuda, first_chunks=first_chunks, nvls=nvls)
         return self
 
     def __call__(self, X: torch.Tensor, hidden: torch.Tensor | None = None,
@@ -367,7 +424,8 @@ class ParallelGatedFFN(_RowParallelOutput):
 
     def __init__(self, Wg_full, bg_full, Wu_full, bu_full, Wo_full, bo_full, activation="silu",
                  group=None, gated_fn=None, linear_fn=None, chunks: int | None = None,
-                 align: int = 64, mode: str | None = None, first_chunks: int | None = None):
+                 align: int = 64, mode: str | None = None, first_chunks: int | None = None,
+                 nvls: bool | None = None):
         world, rank = _group_info(group)
         hidden = Wg_full.shape[1]
         if Wu_full.shape != Wg_full.shape or Wo_full.shape[0] != hidden:
@@ -379,26 +437,27 @@ class ParallelGatedFFN(_RowParallelOutput):
                           Wu_full[:, sl].contiguous(),
                           bu_full[sl].contiguous() if bu_full is not None else None,
                           Wo_full[sl, :].contiguous(), bo_full, activation, group, gated_fn,
-                          linear_fn, chunks, mode, first_chunks)
+                          linear_fn, chunks, mode, first_chunks, nvls)
         self.h0, self.h1 = h0, h1
 
     @classmethod
     def from_shards(cls, Wg_shard, bg_shard, Wu_shard, bu_shard, Wo_shard, bo_full,
                     activation="silu", group=None, gated_fn=None, linear_fn=None,
                     chunks: int | None = None, mode: str | None = None,
-                    first_chunks: int | None = None):
+                    first_chunks: int | None = None, nvls: bool | None = None):
         self = cls.__new__(cls)
         self._init_shards(Wg_shard, bg_shard, Wu_shard, bu_shard, Wo_shard, bo_full, activation,
-                          group, gated_fn, linear_fn, chunks, mode, first_chunks)
+                          group, gated_fn, linear_fn, chunks, mode, first_chunks, nvls)
         return self
 
     def _init_shards(self, Wg, bg, Wu, bu, Wo, bo_full, activation, group, gated_fn, linear_fn,
-                     chunks, mode, first_chunks=None):
+                     chunks, mode, first_chunks=None, nvls=None):
         self.Wg, self.bg, self.Wu, self.bu = Wg, bg, Wu, bu
         self.activation = activation
         self.gated_fn = gated_fn or _default_gated()
         self._init_output(Wo, bo_full, group, linear_fn, chunks, mode,
-                          on_gpu=Wg.is_cuda and gated_fn is None, first_chunks=first_chunks)
+                          on_gpu=Wg.is_cuda and gated_fn is None, first_chunks=first_chunks,
+                          nvls=nvls)
 
     def __call__(self, X: torch.Tensor, hidden: torch.Tensor | None = None,
                  out: torch.Tensor | None = None) -> torch.Tensor:

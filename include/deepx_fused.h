@@ -166,6 +166,19 @@ typedef struct dx_row_reduce_job {
   void* Y;                 /* this rank's output [M][ldy] */
   int64_t ldy;
   int epoch, dtype;
+  /* NVLink multicast (NVLS) form, used when mc_part is not NULL: the
+   * multicast addresses of the partial buffers and of peer-written output
+   * buffers Ysym (bound at the same offsets on every rank), and this rank's
+   * own Ysym, pitch ldo.  Phase A then reads its slab's sum over the ranks
+   * with one multimem.ld_reduce (the switch adds, fp32 accumulation, rounded
+   * to the dtype), adds bias and R, writes Y and multicast-stores the rows
+   * into every rank's Ysym; phase B copies the other ranks' slabs from the
+   * local Ysym into Y.  S is unused.  Per GPU this moves about half the
+   * NVLink bytes of the peer-load form. */
+  void* mc_part;
+  void* mc_out;
+  void* out_sym;
+  int64_t ldo;
 } dx_row_reduce_job;
 
 /* Runs a job as its own launch on `stream` (grid <= 0: one 512-thread CTA

@@ -6,8 +6,9 @@ oracle/) on row blocks of the same seeded inputs:
 
 * the column-parallel layer (gathered);
 * the column -> row MLP, Y = GELU(X W1 + b1) W2 + b2 + X, with the
-  overlapped NVLink reduction (1, 3 and 4 row chunks, the first GEMM grouped
-  or not) and with NCCL;
+  overlapped NVLink reduction carried by the GEMM launches (1, 3 and 4 row
+  chunks, the first GEMM grouped or not; its NVLink-multicast form where the
+  fabric offers it, and its peer-load form) and with NCCL;
 * the column -> row gated FFN, both reductions;
 * a row count the overlapped reduction cannot take (M not a multiple of the
   world size, as decode rows are): it must run the NCCL path and still be
@@ -78,6 +79,7 @@ def main() -> int:
         W = (torch.randn(K, N, generator=g, device=dev) / K ** 0.5).bfloat16()
         b = (torch.rand(N, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
         Xc, Wc, bc = cpu(X), cpu(W), cpu(b)
+        modules = []
         col = ColumnParallelLinear(W, b, "silu", gather_output=True)
         got = col(X)
         torch.cuda.synchronize()
@@ -102,23 +104,31 @@ def main() -> int:
             return rows
 
         ref_rows = mlp_ref(Xc)
-        for mode, chunks, first in (("nccl", 1, None), ("nccl", 4, None), ("fused", 1, None),
-                                    ("fused", 4, None), ("fused", 4, 2), ("fused", 3, 1)):
+        for mode, chunks, first, nvls in (("nccl", 1, None, None), ("nccl", 4, None, None),
+                                          ("fused", 1, None, False), ("fused", 4, None, False),
+                                          ("fused", 4, 2, False), ("fused", 3, 1, False),
+                                          ("fused", 1, None, True), ("fused", 4, None, True),
+                                          ("fused", 4, 2, True), ("fused", 3, 1, True)):
             mlp = ParallelMLP(W1, b1, W2, b2, "gelu", chunks=chunks, mode=mode,
-                              first_chunks=first)
+                              first_chunks=first, nvls=nvls)
+            modules.append(mlp)
             outs = []
             for rep in range(3):  # the fused mode reuses its buffers and flips slab halves
                 outs.append(mlp(X))
             torch.cuda.synchronize()
             if mlp.last_path != mode:
                 failures.append(f"MLP {mode}: ran the {mlp.last_path} path")
+            tag = f"{mode}{'_mc' if mlp.last_multicast else ''}"
+            if nvls and mode == "fused":
+                report["multicast_available"] = bool(mlp.last_multicast)
             for rep, out in enumerate(outs):
-                report[f"mlp_{mode}_c{chunks}_f{first}_{rep}"] = compare(
-                    f"MLP ({mode}, chunks={chunks}, first={first}, call {rep})", out, ref_rows,
+                report[f"mlp_{tag}_c{chunks}_f{first}_{rep}"] = compare(
+                    f"MLP ({tag}, chunks={chunks}, first={first}, call {rep})", out, ref_rows,
                     M, failures)
 
         # Output ownership: a later call with other inputs leaves Y1 intact.
         mlp = ParallelMLP(W1, b1, W2, b2, "gelu", mode="fused")
+        modules.append(mlp)
         X2 = torch.randn(M, K, generator=g, device=dev).bfloat16()
         Y1 = mlp(X)
         Y1_copy = Y1.clone()
@@ -145,20 +155,27 @@ def main() -> int:
         bg = (torch.rand(H, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
         bu = (torch.rand(H, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
         Wgc, Wuc, bgc, buc = cpu(Wg), cpu(Wu), cpu(bg), cpu(bu)
-        for mode in ("nccl", "fused"):
-            ffn = ParallelGatedFFN(Wg, bg, Wu, bu, W2, b2, "silu", mode=mode)
+        for mode, nvls in (("nccl", None), ("fused", False), ("fused", True)):
+            ffn = ParallelGatedFFN(Wg, bg, Wu, bu, W2, b2, "silu", mode=mode, nvls=nvls)
+            modules.append(ffn)
             outs = [ffn(X) for _ in range(2)]
             torch.cuda.synchronize()
             for rep, out in enumerate(outs):
-                report[f"gated_{mode}_{rep}"] = compare(
-                    f"gated FFN ({mode}, call {rep})", out,
+                tag = f"{mode}{'_mc' if ffn.last_multicast else ''}"
+                report[f"gated_{tag}_{rep}"] = compare(
+                    f"gated FFN ({tag}, call {rep})", out,
                     lambda r0, r1: oracle.gated_ffn_f64(Xc[r0:r1], Wgc, bgc, Wuc, buc, W2c, b2c,
                                                         "silu"),
                     M, failures)
         status = _native.device_status(torch.cuda.current_stream(dev).cuda_stream)
         if status:
             failures.append(f"device status {status}")
+        # Collective release of the peer-mapped buffers: no rank unmaps memory
+        # (multicast-bound or not) while a peer's kernels may still reach it.
+        for m in modules:
+            m.release()
     finally:
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
     for f in failures:
