@@ -875,7 +875,7 @@ int row_job_args(const dx_row_reduce_job* j, dx::RowReduceArgs* a) {
 int launch_row_reduce(const dx::RowReduceArgs& a, int dtype, int sms, int grid,
                       cudaStream_t s) {
   if (a.a_rows == 0 && a.b_rows == 0) return DX_OK;
-  if (grid <= 0 || grid > sms) grid = sms;
+  if (grid <= 0 || grid > dx::kRowCtasPerSm * sms) grid = dx::kRowCtasPerSm * sms;
   set_plan("row_reduce world=%d rank=%d A=[%lld,+%d) B=[%lld,+%d) N=%d grid=%d epoch=%d",
            a.world, a.rank, a.a_row0, a.a_rows, a.b_row0, a.b_rows, a.N, grid, a.epoch);
   if (dtype == DX_DTYPE_F16)

@@ -126,7 +126,8 @@ __global__ void __launch_bounds__(256)
 // =====================================================================
 constexpr int kRowMaxWorld = 8;
 constexpr int kRowMaxChunks = 64;
-constexpr int kRowThreads = 512;  // standalone kernel: threads per CTA
+constexpr int kRowThreads = 256;    // standalone kernel: threads per CTA
+constexpr int kRowCtasPerSm = 3;    // and resident CTAs per SM (<= 85 registers)
 // Flag words per rank: PART[chunk][src], RED[chunk][src], arrival counters.
 constexpr int kRowFlagWords = 2 * kRowMaxChunks * kRowMaxWorld + kRowMaxChunks;
 constexpr uint64_t kRowWaitLimitNs = 2000ull * 1000ull * 1000ull;  // 2 s
@@ -271,7 +272,7 @@ __device__ __forceinline__ uint4 row_finish(const uint4 (&part)[W], int world, c
 // groups in phase B.  W is the world size when it is 2, 4 or 8 (then the
 // loops are fully unrolled), else kRowMaxWorld with a run-time bound.
 // Returns early (status word set) if a wait ran out.
-template <typename T, int W, int UA, int UB>
+template <typename T, int W, int UA, int UB, int UN>
 __device__ __forceinline__ void row_reduce_lanes_w(const RowReduceArgs& a, long long gl,
                                                    long long lanes, int warps) {
   const int lane = threadIdx.x & 31;
@@ -302,7 +303,6 @@ __device__ __forceinline__ void row_reduce_lanes_w(const RowReduceArgs& a, long 
     if (a.mc_part != nullptr) {
       // The switch sums the ranks' partials; the finished rows go to this
       // rank's output and, by one multicast store, to every rank's buffer.
-      constexpr int UN = 8;
       const T* const mcp = static_cast<const T*>(a.mc_part);
       T* const mco = static_cast<T*>(a.mc_out);
       for (long long i0 = gl; i0 < total; i0 += UN * lanes) {
@@ -437,25 +437,31 @@ __device__ __forceinline__ void row_reduce_lanes_w(const RowReduceArgs& a, long 
   }
 }
 
-// About 16 loads of 16 bytes in flight per thread in either phase.
-template <typename T>
+// LOADS 16-byte loads in flight per thread in phase A (split over the W
+// ranks' partials, or LOADS / 2 multicast reductions), UB in phase B.  A
+// peer's memory is several microseconds away under load, so the bandwidth a
+// grid reaches is about (threads x bytes in flight) / latency: the GEMM's two
+// spare warps per SM keep many loads each (they have the GEMM's register
+// budget); the standalone kernel runs more threads with fewer each.
+template <typename T, int LOADS, int UB>
 __device__ __forceinline__ void row_reduce_lanes(const RowReduceArgs& a, long long gl,
                                                  long long lanes, int warps) {
+  constexpr int UN = LOADS / 2;
   switch (a.world) {
-    case 2: row_reduce_lanes_w<T, 2, 8, 16>(a, gl, lanes, warps); break;
-    case 4: row_reduce_lanes_w<T, 4, 4, 16>(a, gl, lanes, warps); break;
-    case 8: row_reduce_lanes_w<T, 8, 2, 16>(a, gl, lanes, warps); break;
-    default: row_reduce_lanes_w<T, kRowMaxWorld, 2, 16>(a, gl, lanes, warps); break;
+    case 2: row_reduce_lanes_w<T, 2, LOADS / 2, UB, UN>(a, gl, lanes, warps); break;
+    case 4: row_reduce_lanes_w<T, 4, LOADS / 4, UB, UN>(a, gl, lanes, warps); break;
+    case 8: row_reduce_lanes_w<T, 8, LOADS / 8, UB, UN>(a, gl, lanes, warps); break;
+    default: row_reduce_lanes_w<T, kRowMaxWorld, LOADS / 8, UB, UN>(a, gl, lanes, warps); break;
   }
 }
 
 // Standalone form: the call that ends a step (the last chunk, with nothing
 // left to overlap), or a job whose GEMM launch could not carry it.
 template <typename T>
-__global__ void __launch_bounds__(kRowThreads, 1) row_reduce_kernel(const RowReduceArgs a) {
+__global__ void __launch_bounds__(kRowThreads, kRowCtasPerSm) row_reduce_kernel(const RowReduceArgs a) {
   const long long lanes = static_cast<long long>(gridDim.x) * kRowThreads;
-  row_reduce_lanes<T>(a, static_cast<long long>(blockIdx.x) * kRowThreads + threadIdx.x, lanes,
-                      static_cast<int>(lanes / 32));
+  row_reduce_lanes<T, 12, 8>(a, static_cast<long long>(blockIdx.x) * kRowThreads + threadIdx.x,
+                             lanes, static_cast<int>(lanes / 32));
 }
 
 }  // namespace dx

@@ -149,7 +149,7 @@ __device__ __forceinline__ void comm_warps_run(const UmmaParams& p, int warp, in
   const int cw = warp - 2 - kEpiWarps;
   const int warps = static_cast<int>(gridDim.x) * kCommWarps;
   const long long gl = (static_cast<long long>(blockIdx.x) * kCommWarps + cw) * 32 + lane;
-  row_reduce_lanes<T>(p.comm, gl, static_cast<long long>(warps) * 32, warps);
+  row_reduce_lanes<T, 24, 12>(p.comm, gl, static_cast<long long>(warps) * 32, warps);
   if (cw == 0 && lane == 0) trace_mark(p, kTraceSlots - 2);
 }
 
