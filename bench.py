@@ -875,6 +875,75 @@ def run_skinny(args) -> None:
                 torch.cuda.empty_cache()
 
 
+def run_fabric(args) -> None:
+    """All-to-all NVLink throughput between the ranks of one box (the bound of
+    the row-parallel reduction): every rank moves one slab of 16384 x 4096
+    bf16 / world to or from every peer at once over symmetric (peer-mapped)
+    memory, by copy engine (cudaMemcpyAsync via tensor copies, one stream per
+    peer) and by SM kernels (elementwise kernels reading or writing peer
+    memory).  One JSON line per method: GB/s per GPU per direction."""
+    import torch
+    import torch.distributed as dist
+    import torch.distributed._symmetric_memory as symm_mem
+
+    rank, world, local = _dist_env()
+    if world < 2:
+        raise SystemExit("--fabric needs torchrun with at least 2 ranks")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    N, slab = 4096, 16384 // world
+    rows = slab * world
+    src = symm_mem.empty(rows, N, dtype=torch.bfloat16, device=dev)
+    dst_sym = symm_mem.empty(rows, N, dtype=torch.bfloat16, device=dev)
+    src.normal_()
+    torch.cuda.synchronize()
+    hs = symm_mem.rendezvous(src, dist.group.WORLD)
+    hd = symm_mem.rendezvous(dst_sym, dist.group.WORLD)
+    dist.barrier()
+    peer_src = [hs.get_buffer(s, (rows, N), torch.bfloat16) for s in range(world)]
+    peer_dst = [hd.get_buffer(s, (rows, N), torch.bfloat16) for s in range(world)]
+    out = torch.empty(rows, N, dtype=torch.bfloat16, device=dev)
+    peers = [s for s in range(world) if s != rank]
+    streams = [torch.cuda.Stream(dev) for _ in peers]
+    main = torch.cuda.current_stream(dev)
+    moved = len(peers) * slab * N * 2  # bytes in (and out) per rank
+
+    def on_streams(copy):
+        for st, s in zip(streams, peers):
+            st.wait_stream(main)
+            with torch.cuda.stream(st):
+                copy(s)
+        for st in streams:
+            main.wait_stream(st)
+
+    def sl(t, i):
+        return t[i * slab:(i + 1) * slab]
+
+    methods = {
+        "copy_engine_pull": lambda: on_streams(lambda s: sl(out, s).copy_(sl(peer_src[s], rank))),
+        "copy_engine_push": lambda: on_streams(lambda s: sl(peer_dst[s], rank).copy_(sl(src, s))),
+        "sm_pull": lambda: [torch.mul(sl(peer_src[s], rank), 1, out=sl(out, s)) for s in peers],
+        "sm_push": lambda: [torch.mul(sl(src, s), 1, out=sl(peer_dst[s], rank)) for s in peers],
+    }
+    for name, fn in methods.items():
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        dist.barrier()
+        ms = _max_over_ranks(_time_back_to_back(fn, max(5, args.steps), main, 200.0), world, dev)
+        if rank == 0:
+            print(json.dumps({"fabric": name, "world": world, "MiB_per_rank_each_way":
+                              moved / 2 ** 20, "us": round(ms * 1e3, 1),
+                              "GBps_per_gpu_per_direction": round(moved / (ms * 1e-3) / 1e9, 1)}),
+                  flush=True)
+    torch.cuda.synchronize()
+    dist.barrier()
+    del peer_src, peer_dst, hs, hd
+    dist.barrier()
+    dist.destroy_process_group()
+
+
 def main() -> None:
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -888,6 +957,8 @@ def main() -> None:
                     help="run only W warm-up and K timed launches of the workload (for ncu)")
     ap.add_argument("--shard-of", type=int, default=1,
                     help="with --profile: run rank 0's column shard of an N-way split on one GPU")
+    ap.add_argument("--fabric", action="store_true",
+                    help="all-to-all NVLink throughput between the ranks (torchrun, >= 2 GPUs)")
     ap.add_argument("--skinny", action="store_true",
                     help="time the decode and single-CTA tensor-core kernels on decode shapes "
                          "(the evidence for AUTO's skinny-M choice), one JSON line per shape")
@@ -900,6 +971,8 @@ def main() -> None:
               file=sys.stderr)
     if args.impl == "reference":
         run_reference(args)
+    elif args.fabric:
+        run_fabric(args)
     elif args.skinny:
         run_skinny(args)
     else:
