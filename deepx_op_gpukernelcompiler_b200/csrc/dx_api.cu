@@ -631,20 +631,24 @@ int launch_simt(const Problem& pr, int sms) {
   const T* R = static_cast<const T*>(pr.R);
   T* Y = static_cast<T*>(pr.Y);
   const int M = static_cast<int>(pr.M), N = static_cast<int>(pr.N), K = static_cast<int>(pr.K);
-  const int64_t big_tiles = ((pr.M + 63) / 64) * ((pr.N + 63) / 64);
-  set_plan("simt tile=%d grid=%lld", big_tiles >= 2LL * sms ? 64 : 32,
-           (long long)(big_tiles >= 2LL * sms ? big_tiles : ((pr.M + 31) / 32) * ((pr.N + 31) / 32)));
-  if (big_tiles >= 2LL * sms) {
-    if ((pr.M + 63) / 64 > 65535) return fail(DX_ERR_UNSUPPORTED, "M too large for the SIMT kernel");
-    dim3 grid(static_cast<unsigned>((pr.N + 63) / 64), static_cast<unsigned>((pr.M + 63) / 64));
+  // The largest tile that still gives at least two CTAs per SM (64x64, 32x32,
+  // 16x32); below that, the smallest.
+  const int64_t t64 = ((pr.M + 63) / 64) * ((pr.N + 63) / 64);
+  const int64_t t32 = ((pr.M + 31) / 32) * ((pr.N + 31) / 32);
+  const int bm = t64 >= 2LL * sms ? 64 : (t32 >= 2LL * sms ? 32 : 16);
+  const int bn = bm == 16 ? 32 : bm;
+  if ((pr.M + bm - 1) / bm > 65535) return fail(DX_ERR_UNSUPPORTED, "M too large for the SIMT kernel");
+  dim3 grid(static_cast<unsigned>((pr.N + bn - 1) / bn), static_cast<unsigned>((pr.M + bm - 1) / bm));
+  set_plan("simt tile=%dx%d grid=%u", bm, bn, grid.x * grid.y);
+  if (bm == 64)
     dx::simt_fused_linear_kernel<T, 64, 64><<<grid, 256, 0, pr.stream>>>(
         X, W, b, R, Y, M, N, K, pr.ldx, pr.ldw, pr.ldr, pr.ldy, pr.act, pr.alpha);
-  } else {
-    if ((pr.M + 31) / 32 > 65535) return fail(DX_ERR_UNSUPPORTED, "M too large for the SIMT kernel");
-    dim3 grid(static_cast<unsigned>((pr.N + 31) / 32), static_cast<unsigned>((pr.M + 31) / 32));
+  else if (bm == 32)
     dx::simt_fused_linear_kernel<T, 32, 32><<<grid, 256, 0, pr.stream>>>(
         X, W, b, R, Y, M, N, K, pr.ldx, pr.ldw, pr.ldr, pr.ldy, pr.act, pr.alpha);
-  }
+  else
+    dx::simt_fused_linear_kernel<T, 16, 32><<<grid, 256, 0, pr.stream>>>(
+        X, W, b, R, Y, M, N, K, pr.ldx, pr.ldw, pr.ldr, pr.ldy, pr.act, pr.alpha);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch simt_fused_linear_kernel");
   return DX_OK;

@@ -6,8 +6,9 @@
 //   * fp16/bf16 problems whose strides or pointers TMA cannot address
 //     (rows not a multiple of 16 bytes), and K == 0.
 // Each thread accumulates its outputs over k = 0..K-1 in order, so results
-// are deterministic.  Tiles are BM x BN with 256 threads in a 16 x 16 grid;
-// thread (ty, tx) owns rows ty + 16 i and columns tx + 16 j.  A gated form
+// are deterministic (and independent of the tile shape).  Tiles are BM x BN
+// (16x32, 32x32 or 64x64) with 256 threads in a 16 x 16 grid; thread (ty, tx)
+// owns rows ty + 16 i and columns tx + 16 j.  A gated form
 // (two weight matrices, Y = act(X Wg + bg) * (X Wu + bu)) shares the tiling.
 #pragma once
 
@@ -24,9 +25,15 @@ __global__ void __launch_bounds__(256)
                              T* __restrict__ Y, int M, int N, int K, long long ldx, long long ldw,
                              long long ldr, long long ldy, int act, float alpha) {
   using Tr = ElemTraits<T>;
-  constexpr int BK = 16;
+  // K steps of 32; the next step's operands are loaded into registers while
+  // the current step is multiplied from shared memory, so the global-memory
+  // latency of a step overlaps the previous step's FFMAs (small problems run
+  // few CTAs per SM and would otherwise wait for every step's loads).
+  constexpr int BK = 32;
   constexpr int TM = BM / 16;
   constexpr int TN = BN / 16;
+  constexpr int A_PER = BM * BK / 256;  // X elements each thread stages per step
+  constexpr int B_PER = BK * BN / 256;  // W elements each thread stages per step
   __shared__ float As[BK][BM + 1];
   __shared__ float Bs[BK][BN];
   const int tx = threadIdx.x & 15;
@@ -34,24 +41,44 @@ __global__ void __launch_bounds__(256)
   const int m0 = blockIdx.y * BM;
   const int n0 = blockIdx.x * BN;
 
+  float ra[A_PER], rb[B_PER];
+  auto load_step = [&](int k0) {
+#pragma unroll
+    for (int u = 0; u < A_PER; ++u) {
+      const int idx = threadIdx.x + 256 * u;
+      const int mm = idx / BK, kk = idx % BK;
+      const int m = m0 + mm, k = k0 + kk;
+      ra[u] = (m < M && k < K) ? Tr::to_float(X[m * ldx + k]) : 0.0f;
+    }
+#pragma unroll
+    for (int u = 0; u < B_PER; ++u) {
+      const int idx = threadIdx.x + 256 * u;
+      const int kk = idx / BN, nn = idx % BN;
+      const int k = k0 + kk, n = n0 + nn;
+      rb[u] = (k < K && n < N) ? Tr::to_float(W[k * ldw + n]) : 0.0f;
+    }
+  };
+
   float acc[TM][TN];
 #pragma unroll
   for (int i = 0; i < TM; ++i)
 #pragma unroll
     for (int j = 0; j < TN; ++j) acc[i][j] = 0.0f;
 
+  if (K > 0) load_step(0);
   for (int k0 = 0; k0 < K; k0 += BK) {
-    for (int idx = threadIdx.x; idx < BM * BK; idx += 256) {
-      const int mm = idx / BK, kk = idx % BK;
-      const int m = m0 + mm, k = k0 + kk;
-      As[kk][mm] = (m < M && k < K) ? Tr::to_float(X[m * ldx + k]) : 0.0f;
+#pragma unroll
+    for (int u = 0; u < A_PER; ++u) {
+      const int idx = threadIdx.x + 256 * u;
+      As[idx % BK][idx / BK] = ra[u];
     }
-    for (int idx = threadIdx.x; idx < BK * BN; idx += 256) {
-      const int kk = idx / BN, nn = idx % BN;
-      const int k = k0 + kk, n = n0 + nn;
-      Bs[kk][nn] = (k < K && n < N) ? Tr::to_float(W[k * ldw + n]) : 0.0f;
+#pragma unroll
+    for (int u = 0; u < B_PER; ++u) {
+      const int idx = threadIdx.x + 256 * u;
+      Bs[idx / BN][idx % BN] = rb[u];
     }
     __syncthreads();
+    if (k0 + BK < K) load_step(k0 + BK);
 #pragma unroll
     for (int kk = 0; kk < BK; ++kk) {
       float a[TM], b[TN];
