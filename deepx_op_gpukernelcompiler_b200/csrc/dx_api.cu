@@ -135,6 +135,50 @@ int device_sms(int dev, int* sms) {
   return DX_OK;
 }
 
+// SMs the launching stream may use: the whole device, or the SM partition of
+// the green context the stream belongs to.  The persistent kernels size their
+// grids to it (every CTA must be resident: the split-K pieces of a tile wait
+// for one another), so they run correctly inside an SM partition.
+PFN_cuStreamGetCtx_v12050 g_stream_ctx = nullptr;
+PFN_cuGreenCtxGetDevResource_v12040 g_green_res = nullptr;
+std::once_flag g_green_once;
+std::map<CUgreenCtx, int> g_green_sms;
+
+int stream_sms(cudaStream_t s, int dev, int* sms) {
+  int rc = device_sms(dev, sms);
+  if (rc) return rc;
+  std::call_once(g_green_once, [] {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuStreamGetCtx", &fn, 12050, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_stream_ctx = reinterpret_cast<PFN_cuStreamGetCtx_v12050>(fn);
+    fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuGreenCtxGetDevResource", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_green_res = reinterpret_cast<PFN_cuGreenCtxGetDevResource_v12040>(fn);
+  });
+  (void)cudaGetLastError();
+  if (g_stream_ctx == nullptr || g_green_res == nullptr) return DX_OK;
+  CUcontext ctx = nullptr;
+  CUgreenCtx green = nullptr;
+  if (g_stream_ctx(reinterpret_cast<CUstream>(s), &ctx, &green) != CUDA_SUCCESS || green == nullptr)
+    return DX_OK;  // a regular context: the whole device
+  std::lock_guard<std::mutex> lk(g_mu);
+  auto it = g_green_sms.find(green);
+  if (it == g_green_sms.end()) {
+    CUdevResource r{};
+    int n = *sms;
+    if (g_green_res(green, &r, CU_DEV_RESOURCE_TYPE_SM) == CUDA_SUCCESS && r.sm.smCount > 0)
+      n = static_cast<int>(r.sm.smCount);
+    it = g_green_sms.emplace(green, n).first;
+  }
+  *sms = std::min(*sms, it->second);
+  return DX_OK;
+}
+
 // ------------------------------------------------- timeout reporting
 // One pinned, device-mapped int per device: the host-visible copy of the
 // device status word (dx::g_status_mirror).  Installed on a device by the
@@ -771,7 +815,9 @@ int select_variant(const Problem& p, int sms, bool ws_known) {
 // The plan for this call: with the split tail when the caller's workspace
 // holds it, else whole tiles only.
 UmmaPlan umma_plan_for(const Problem& p, int dev, int sms, bool single_cta_only) {
-  const int slots = (p.M >= 256 && !single_cta_only) ? pair_slots<256, __nv_bfloat16>(dev, sms) : 0;
+  const int slots = (p.M >= 256 && !single_cta_only)
+                        ? std::min(pair_slots<256, __nv_bfloat16>(dev, sms), sms / 2)
+                        : 0;
   UmmaPlan pl = plan_umma(p.M, p.N, p.K, sms, slots, true, single_cta_only, p.gated);
   if (pl.bytes > 0 && (p.ws == nullptr || p.ws_bytes < pl.bytes || !aligned16(p.ws)))
     pl = plan_umma(p.M, p.N, p.K, sms, slots, false, single_cta_only, p.gated);
@@ -902,7 +948,7 @@ int run(const Problem& p, int kernel) {
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
   int sms = 0;
-  if ((rc = device_sms(dev, &sms))) return rc;
+  if ((rc = stream_sms(p.stream, dev, &sms))) return rc;
   if ((rc = install_status_mirror(dev, p.stream))) return rc;
   if ((rc = check_status_mirror(dev))) return rc;
   if (p.M == 0 || p.N == 0) return launch_row_reduce(*p.comm, p.comm_dtype, sms, 0, p.stream);
@@ -1164,8 +1210,8 @@ int dx_row_reduce(const dx_row_reduce_job* job, int grid, void* stream) {
   int dev = 0, sms = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
-  if ((rc = device_sms(dev, &sms))) return rc;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if ((rc = stream_sms(s, dev, &sms))) return rc;
   if ((rc = install_status_mirror(dev, s))) return rc;
   if ((rc = check_status_mirror(dev))) return rc;
   return launch_row_reduce(a, job->dtype, sms, grid, s);
