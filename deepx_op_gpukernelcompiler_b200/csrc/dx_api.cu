@@ -685,13 +685,13 @@ int launch_simt(const Problem& pr, int sms) {
   dim3 grid(static_cast<unsigned>((pr.N + bn - 1) / bn), static_cast<unsigned>((pr.M + bm - 1) / bm));
   set_plan("simt tile=%dx%d grid=%u", bm, bn, grid.x * grid.y);
   if (bm == 64)
-    dx::simt_fused_linear_kernel<T, 64, 64><<<grid, 256, 0, pr.stream>>>(
+    dx::simt_fused_linear_kernel<T, 64, 64, 32><<<grid, 256, 0, pr.stream>>>(
         X, W, b, R, Y, M, N, K, pr.ldx, pr.ldw, pr.ldr, pr.ldy, pr.act, pr.alpha);
   else if (bm == 32)
-    dx::simt_fused_linear_kernel<T, 32, 32><<<grid, 256, 0, pr.stream>>>(
+    dx::simt_fused_linear_kernel<T, 32, 32, 128><<<grid, 256, 0, pr.stream>>>(
         X, W, b, R, Y, M, N, K, pr.ldx, pr.ldw, pr.ldr, pr.ldy, pr.act, pr.alpha);
   else
-    dx::simt_fused_linear_kernel<T, 16, 32><<<grid, 256, 0, pr.stream>>>(
+    dx::simt_fused_linear_kernel<T, 16, 32, 128><<<grid, 256, 0, pr.stream>>>(
         X, W, b, R, Y, M, N, K, pr.ldx, pr.ldw, pr.ldr, pr.ldy, pr.act, pr.alpha);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch simt_fused_linear_kernel");

@@ -18,18 +18,17 @@
 
 namespace dx {
 
-template <typename T, int BM, int BN>
+template <typename T, int BM, int BN, int BK>
 __global__ void __launch_bounds__(256)
     simt_fused_linear_kernel(const T* __restrict__ X, const T* __restrict__ W,
                              const T* __restrict__ bias, const T* __restrict__ R,
                              T* __restrict__ Y, int M, int N, int K, long long ldx, long long ldw,
                              long long ldr, long long ldy, int act, float alpha) {
   using Tr = ElemTraits<T>;
-  // K steps of 32; the next step's operands are loaded into registers while
+  // K steps of BK; the next step's operands are loaded into registers while
   // the current step is multiplied from shared memory, so the global-memory
-  // latency of a step overlaps the previous step's FFMAs (small problems run
-  // few CTAs per SM and would otherwise wait for every step's loads).
-  constexpr int BK = 32;
+  // latency of a step overlaps the previous step's FFMAs.  Small tiles take
+  // deep steps (few steps, each long enough to cover a load's latency).
   constexpr int TM = BM / 16;
   constexpr int TN = BN / 16;
   constexpr int A_PER = BM * BK / 256;  // X elements each thread stages per step
