@@ -734,14 +734,23 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
                        "frac_of_peak": round(tf / tflops_peak, 4),
                        "parallelism": "one GPU, two fused launches", "gpu_launches_per_step": 2}
     else:
-        mlp = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, mode="fused")
-        sweep = {}
-        for chunks, first in ((4, None), (4, 2), (8, 4), (8, 2), (16, 4), (2, None)):
-            mlp.chunks, mlp.first_chunks = chunks, first
-            ms = time_run(lambda: mlp(X, hidden=H, out=Yo), 1500.0)
-            sweep[f"chunks={chunks},first={first or chunks}"] = round(ms, 4)
+        # Every schedule of the engine's reduction, in both NVLink forms: the
+        # reduction carried by the GEMM launches at several chunkings, and
+        # one chunk (the two whole GEMMs, then one reduction launch of its
+        # own).  The fastest is the value; all are listed.
+        sweep, modules = {}, {}
+        for nvls in (None, False):
+            mlp = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, mode="fused", nvls=nvls)
+            modules[nvls] = mlp
+            for chunks, first in ((4, 4), (4, 2), (8, 4), (2, 2), (1, 1)):
+                mlp.chunks, mlp.first_chunks = chunks, first
+                ms = time_run(lambda: mlp(X, hidden=H, out=Yo), 1500.0)
+                form = "multicast" if mlp.last_multicast else "peer"
+                sweep[f"{form},chunks={chunks},first={first}"] = round(ms, 4)
         best = min(sweep, key=sweep.get)
-        chunks, first = (int(v.split("=")[1]) for v in best.split(","))
+        form, chunks, first = best.split(",")
+        chunks, first = int(chunks.split("=")[1]), int(first.split("=")[1])
+        mlp = modules[None] if form == "multicast" else modules[False]
         mlp.chunks, mlp.first_chunks = chunks, first
         ms = time_run(lambda: mlp(X, hidden=H, out=Yo), 1500.0)
         assert mlp.last_path == "fused"
@@ -769,8 +778,9 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
                                  "frac_of_peak": round(tf / world / tflops_peak, 4),
                                  "parallelism": f"column->row x{world} + NCCL all-reduce "
                                                 "(4 chunks)"}
-        mlp.release()
-        del mlp, mlp_n, Yn
+        for m in modules.values():
+            m.release()
+        del mlp, mlp_n, Yn, modules
     del X, W1, b1, W2, b2, H, Yo
 
     # The gated FFN chain (ffn_gated, fusion.py:44-46): Y = (silu(X Wg + bg) *

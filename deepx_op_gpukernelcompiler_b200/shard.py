@@ -218,8 +218,11 @@ class _RowParallelBuffers:
             self.out_sym = symm_mem.empty(M, N, dtype=dtype, device=device)
             h_out = symm_mem.rendezvous(self.out_sym, pg)
             self.handles.append(h_out)
-            mc_p = self._mc_ptr(self.handles[0], self.part, rank)
-            mc_o = self._mc_ptr(h_out, self.out_sym, rank)
+            try:
+                mc_p = self._mc_ptr(self.handles[0], self.part, rank)
+                mc_o = self._mc_ptr(h_out, self.out_sym, rank)
+            except RuntimeError:  # this allocation has no multicast mapping
+                mc_p = mc_o = 0
             have = torch.tensor([1 if (mc_p and mc_o) else 0], device=device)
             dist.all_reduce(have, op=dist.ReduceOp.MIN, group=group)
             if int(have.item()):
