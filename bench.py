@@ -885,6 +885,99 @@ def run_skinny(args) -> None:
                 torch.cuda.empty_cache()
 
 
+def run_timeline(args) -> None:
+    """Per-launch CTA timeline of one overlapped MLP step (the 16384 x 4096 x
+    16384 chain, column -> row over the torchrun ranks): each launch of the
+    step records %globaltimer stamps into its own trace buffer
+    (dx_set_trace_buffer switched between launches), and rank 0 prints, per
+    launch, its start, the end of its last tile's epilogue, the end of its
+    carried reduction job and its exit, in microseconds from the first
+    launch's start, plus the step time and that of the same two GEMMs
+    unchunked.  --chunks / --first set the schedule, --nvls 0 forces peer
+    loads."""
+    import torch
+    import torch.distributed as dist
+
+    from deepx_op_gpukernelcompiler_b200 import _native, fused_linear
+    from deepx_op_gpukernelcompiler_b200.shard import ParallelMLP, shard_bounds
+    from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS
+
+    rank, world, local = _dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    w = WORKLOADS["mlp_residual_16384x4096x16384_bf16"]
+    h0, h1 = shard_bounds(w.N, world, rank, 64)
+    g = torch.Generator(device=dev)
+    g.manual_seed(w.seed)
+    X = torch.randn(w.M, w.K, generator=g, device=dev).bfloat16()
+    b2 = (torch.rand(w.K, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
+    g.manual_seed(w.seed * 1000 + rank)
+    W1 = (torch.randn(w.K, h1 - h0, generator=g, device=dev) / math.sqrt(w.K)).bfloat16()
+    b1 = (torch.rand(h1 - h0, generator=g, device=dev) * 0.2 - 0.1).bfloat16()
+    W2 = (torch.randn(h1 - h0, w.K, generator=g, device=dev) / math.sqrt(w.N)).bfloat16()
+    H = torch.empty(w.M, h1 - h0, dtype=torch.bfloat16, device=dev)
+    Y = torch.empty(w.M, w.K, dtype=torch.bfloat16, device=dev)
+    mlp = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, mode="fused" if world > 1 else "nccl",
+                                  chunks=args.chunks, first_chunks=args.first,
+                                  nvls=None if args.nvls else False)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn, n=10):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize()
+        _barrier(world)
+        return _max_over_ranks(_time_back_to_back(fn, n, stream, 2000.0), world, dev)
+
+    step_ms = timed(lambda: mlp(X, hidden=H, out=Y))
+    unchunked_ms = timed(lambda: (fused_linear(X, W1, b1, w.act, out=H),
+                                  fused_linear(H, W2, None, None, out=Y)))
+    slots = 148 * 16
+    traces, kinds = [], []
+
+    def hook(i, launch):
+        while len(traces) <= i:
+            traces.append(torch.zeros(slots, dtype=torch.int64, device=dev))
+        kinds.append((launch[0], str(launch[-1])))
+        _native.load().dx_set_trace_buffer(traces[i].data_ptr(), slots * 8)
+
+    torch.cuda.synchronize()
+    _barrier(world)
+    mlp.launch_hook = hook
+    mlp(X, hidden=H, out=Y)
+    mlp.launch_hook = None
+    _native.load().dx_set_trace_buffer(None, 0)
+    torch.cuda.synchronize()
+    t0, rows = None, []
+    for i, (kind, job) in enumerate(kinds):
+        t = traces[i].view(148, 16).cpu()
+        used = t[:, 15] > 0
+        if not bool(used.any()):
+            rows.append({"launch": i, "kind": kind, "job": job, "traced": False})
+            continue
+        t = t[used]
+        if t0 is None:
+            t0 = int(t[:, 0].min())
+        items = t[:, 1:14]
+        rel = lambda v: round((int(v) - t0) / 1e3, 1)  # noqa: E731
+        rows.append({"launch": i, "kind": kind, "job": job, "start": rel(t[:, 0].min()),
+                     "last_tile": rel(items[items > 0].max()) if bool((items > 0).any()) else None,
+                     "job_end": rel(t[:, 14][t[:, 14] > 0].max()) if bool((t[:, 14] > 0).any())
+                     else None, "exit": rel(t[:, 15].max())})
+    if rank == 0:
+        print(json.dumps({"timeline": w.name, "world": world, "chunks": args.chunks,
+                          "first": args.first, "multicast": bool(mlp.last_multicast),
+                          "step_ms": round(step_ms, 4), "unchunked_gemms_ms": round(unchunked_ms, 4),
+                          "launches": rows}), flush=True)
+    torch.cuda.synchronize()
+    mlp.release()
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_fabric(args) -> None:
     """All-to-all NVLink throughput between the ranks of one box (the bound of
     the row-parallel reduction): every rank moves one slab of 16384 x 4096
@@ -967,6 +1060,11 @@ def main() -> None:
                     help="run only W warm-up and K timed launches of the workload (for ncu)")
     ap.add_argument("--shard-of", type=int, default=1,
                     help="with --profile: run rank 0's column shard of an N-way split on one GPU")
+    ap.add_argument("--timeline", action="store_true",
+                    help="per-launch timeline of one overlapped MLP step (torchrun)")
+    ap.add_argument("--chunks", type=int, default=4, help="--timeline: row chunks")
+    ap.add_argument("--first", type=int, default=4, help="--timeline: first-GEMM launches")
+    ap.add_argument("--nvls", type=int, default=1, help="--timeline: 0 forces peer loads")
     ap.add_argument("--fabric", action="store_true",
                     help="all-to-all NVLink throughput between the ranks (torchrun, >= 2 GPUs)")
     ap.add_argument("--skinny", action="store_true",
@@ -983,6 +1081,8 @@ def main() -> None:
         run_reference(args)
     elif args.fabric:
         run_fabric(args)
+    elif args.timeline:
+        run_timeline(args)
     elif args.skinny:
         run_skinny(args)
     else:

@@ -286,6 +286,10 @@ class _RowParallelOutput:
         self.chunks = max(1, int(chunks)) if chunks is not None else (
             4 if self.mode == "fused" else 1)
         self.first_chunks = first_chunks
+        # Called with (index, launch) before each launch of an overlapped step
+        # (launch as row_schedule gives it): a profiling aid, e.g. to switch
+        # dx_set_trace_buffer between launches.
+        self.launch_hook = None
         self.last_path = None  # "fused" or "nccl": what the last call ran
         self.last_multicast = False  # the last fused call used NVLink multicast
 
@@ -364,7 +368,9 @@ class _RowParallelOutput:
                            bufs.out_sym)
 
         stream = torch.cuda.current_stream(dev).cuda_stream
-        for launch in plan:
+        for i, launch in enumerate(plan):
+            if self.launch_hook is not None:
+                self.launch_hook(i, launch)
             if launch[0] == "first":
                 _, c0, c1, ab = launch
                 first(chunks[c0][0], chunks[c1 - 1][0] + chunks[c1 - 1][1], job(ab))
