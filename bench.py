@@ -185,6 +185,38 @@ def cpu_baseline(w, W_host=None, target_s: float = 8.0) -> dict:
                       f"CPU on {threads} threads (kernel.py:64-66 restated), {elapsed:.1f} s"}
 
 
+def cpu_baseline_config(w, target_s: float = 2.0) -> dict:
+    """The reference's CPU expression on a bounded row sample of any
+    configuration (single linear or the MLP chain), torch fp32 on all host
+    cores; value in the configuration's unit (TFLOP/s, GB/s for decode)."""
+    import oracle
+    from deepx_op_gpukernelcompiler_b200.workloads import make_inputs
+    threads = oracle.torch_cpu.use_threads()
+    rows = min(w.M, 256)
+    inp = {k: v.float() for k, v in make_inputs(w, device="cpu", M=rows).items()}
+    if w.mlp:
+        fn = lambda: oracle.torch_cpu.mlp_residual(inp["X"], inp["W1"], inp["b1"],  # noqa: E731
+                                                   inp["W2"], inp["b2"], w.act)
+    else:
+        fn = lambda: oracle.torch_cpu.fused_linear(inp["X"], inp["W"], inp["bias"], w.act)  # noqa
+    fn()
+    reps, elapsed = 0, 0.0
+    while reps < 2 or elapsed < target_s:
+        t0 = time.perf_counter()
+        fn()
+        elapsed += time.perf_counter() - t0
+        reps += 1
+    per = elapsed / reps
+    flops = (4 if w.mlp else 2) * rows * w.K * w.N
+    line = {"value": round(flops / per / 1e12, 4), "unit": "TFLOP/s", "cores": threads,
+            "kind": "port", "ms_per_sample": round(per * 1e3, 3),
+            "sample": f"{reps} x the configuration on X[{rows},{w.K}] (of {w.M} rows), fp32 torch "
+                      f"CPU on {threads} threads"}
+    if w.name.startswith("decode"):
+        line.update(value=round(w.min_bytes * rows / w.M / per / 1e9, 2), unit="GB/s")
+    return line
+
+
 def run_reference(args) -> None:
     rank, world, _ = _dist_env()
     if rank != 0:
@@ -494,6 +526,10 @@ def run_gpu(args) -> None:
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         cpu = cpu_baseline(w, W_host=Wt.cpu())
+        # The other configurations of the metric, same CPU expression.
+        extra["cpu_baselines"] = {name: cpu_baseline_config(WORKLOADS[name]) for name in (
+            "linear_relu_256x512x512_f32", "linear_gelu_tanh_4096x4096x4096_bf16",
+            "decode_gelu_erf_16x8192x28672_f16", "mlp_residual_16384x4096x16384_bf16")}
 
     if rank == 0:
         line = {
