@@ -775,7 +775,7 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
         # one chunk (the two whole GEMMs, then one reduction launch of its
         # own).  The fastest is the value; all are listed.
         sweep, modules = {}, {}
-        for nvls in (None, False):
+        for nvls in (True, False):
             mlp = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, mode="fused", nvls=nvls)
             modules[nvls] = mlp
             for chunks, first in ((4, 4), (4, 2), (8, 4), (2, 2), (1, 1)):
@@ -786,7 +786,7 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
         best = min(sweep, key=sweep.get)
         form, chunks, first = best.split(",")
         chunks, first = int(chunks.split("=")[1]), int(first.split("=")[1])
-        mlp = modules[None] if form == "multicast" else modules[False]
+        mlp = modules[True] if form == "multicast" else modules[False]
         mlp.chunks, mlp.first_chunks = chunks, first
         ms = time_run(lambda: mlp(X, hidden=H, out=Yo), 1500.0)
         assert mlp.last_path == "fused"

@@ -213,7 +213,10 @@ class _RowParallelBuffers:
         self.out_sym = None
         self.slab_ptrs = None
         if nvls is None:
-            nvls = os.environ.get("DX_ROW_NVLS", "1") != "0"
+            # Multicast halves the NVLink bytes per GPU but only pays with
+            # several peers (2 ranks: 1.78 ms against 1.735 with peer loads;
+            # 8 ranks: 0.832 ms against 1.043).
+            nvls = world > 2 and os.environ.get("DX_ROW_NVLS", "1") != "0"
         if nvls:
             self.out_sym = symm_mem.empty(M, N, dtype=dtype, device=device)
             h_out = symm_mem.rendezvous(self.out_sym, pg)
@@ -283,8 +286,16 @@ class _RowParallelOutput:
         self.b2_all = b2_full.contiguous() if b2_full is not None else None
         self.b2 = self.b2_all if self.rank == 0 else None
         self.linear_fn = linear_fn or _default_linear()
-        self.chunks = max(1, int(chunks)) if chunks is not None else (
-            4 if self.mode == "fused" else 1)
+        # Defaults from measurements on one 8-GPU B200 box (16384 x 4096 x 16384
+        # MLP): the reduction carried by 4 chunks' GEMMs is fully hidden at 2
+        # ranks (1.735 ms, NCCL 1.847); at 8 ranks the reduction alone (~0.44
+        # ms at the fabric's all-to-all rate) outlasts the compute (0.41 ms)
+        # and chunked GEMMs lose efficiency, so one chunk — the whole GEMMs,
+        # then one reduction launch — is fastest (0.832 ms, NCCL 1.01).
+        if chunks is None:
+            chunks = 1 if self.mode != "fused" else (4 if self.world <= 2 else
+                                                     2 if self.world <= 4 else 1)
+        self.chunks = max(1, int(chunks))
         self.first_chunks = first_chunks
         # Called with (index, launch) before each launch of an overlapped step
         # (launch as row_schedule gives it): a profiling aid, e.g. to switch
