@@ -310,9 +310,20 @@ long long decode_cta_of_host(long long u, long long U, int G) {
 struct DecodePlan {
   int n_tiles = 0, kbt = 0, grid = 0, max_seg = 0, mn = 16;
   int nh = 2;  // 128-column UMMA halves per work unit
+  int cluster = 1;  // CTAs per tile sharing partials in a thread-block cluster
   long long units = 0;
   size_t ticket_bytes = 0, bytes = 0;
 };
+
+// Thread-block cluster size for a plain decode problem whose tiles must be
+// split along K: the largest C in {8, 4, 2} with tiles * C <= SMs and at least
+// one k-block per CTA, provided tiles * C CTAs still cover half the SMs (so
+// that enough SMs stream W); 1 when no such C exists.
+int decode_cluster_size(int64_t n_tiles, int kbt, int sms) {
+  for (int c : {8, 4, 2})
+    if (n_tiles * c <= sms && kbt >= c && 2 * n_tiles * c >= sms) return c;
+  return 1;
+}
 
 // Halves per work unit: 2; the gated form with M <= 16 uses 4 (256 columns
 // of each weight, so both weights are read in 512-byte row segments).
@@ -353,6 +364,19 @@ DecodePlan decode_plan(int64_t M, int64_t N, int64_t K, int sms, bool gated = fa
   // with 112 whole tiles).
   long long want = sms;
   if (2LL * d.n_tiles >= sms && d.n_tiles <= sms) want = d.n_tiles;
+  d.ticket_bytes = kTicketSlabBytes;
+  if (!gated && want == sms) {
+    // Fewer tiles than SMs / 2: split each tile over a cluster of C CTAs that
+    // add their partials through distributed shared memory (no workspace).
+    const int c = decode_cluster_size(d.n_tiles, d.kbt, sms);
+    if (c > 1) {
+      d.cluster = c;
+      d.grid = d.n_tiles * c;
+      d.max_seg = c;
+      d.bytes = 0;
+      return d;
+    }
+  }
   d.grid = static_cast<int>(std::max<long long>(1, std::min<long long>(d.units, want)));
   int ms = 1;
   for (int t = 0; t < d.n_tiles; ++t) {
@@ -651,6 +675,7 @@ int launch_decode(const Problem& pr, int dev, int sms, const DecodePlan& d) {
   p.alpha = pr.alpha;
   p.gated = pr.gated ? 1 : 0;
   p.bias2 = pr.bias2;
+  p.cluster = d.cluster;
   {
     unsigned long long* tr = g_trace.load();
     const size_t need = static_cast<size_t>(d.grid) * dx::kTraceSlots * 8;
@@ -658,11 +683,29 @@ int launch_decode(const Problem& pr, int dev, int sms, const DecodePlan& d) {
   }
   (void)sms;
   set_plan("decode%s mn=%d halves=%d stages=%d grid=%d n_tiles=%d kbt=%d max_seg=%d "
-           "workspace=%zu",
+           "cluster=%d workspace=%zu",
            pr.gated ? "_gated" : "", MN, NH, S::STAGES, d.grid, d.n_tiles, d.kbt, d.max_seg,
-           d.bytes);
-  kern<<<d.grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tW, tW2, tX, p);
-  cudaError_t e = cudaGetLastError();
+           d.cluster, d.bytes);
+  cudaError_t e;
+  if (d.cluster > 1) {
+    cudaLaunchAttribute attr[1];
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(static_cast<unsigned>(d.grid));
+    cfg.blockDim = dim3(S::THREADS);
+    cfg.dynamicSmemBytes = S::SMEM_BYTES;
+    cfg.stream = pr.stream;
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = static_cast<unsigned>(d.cluster);
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    e = cudaLaunchKernelEx(&cfg, kern, tW, tW2, tX, p);
+    if (e == cudaSuccess) e = cudaGetLastError();
+  } else {
+    kern<<<d.grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tW, tW2, tX, p);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess) return cuda_fail(e, "launch decode_fused_linear_kernel");
   return DX_OK;
 }

@@ -17,7 +17,13 @@
 //     at least half as many tiles as SMs (no split-K at all), else one CTA
 //     per SM, so that every SM streams the same number of bytes and a CTA's
 //     range crosses at most a few n-tiles (split-K).
-//   * partial sums of a tile that several CTAs share go to a workspace as
+//   * with fewer tiles than SMs/2 (plain form) the CTAs of one tile form a
+//     thread-block cluster of C = 2, 4 or 8 (tiles x C <= SMs): each streams
+//     1/C of the tile's K range and leaves its fp32 partial in its own shared
+//     memory (the idle stage ring); after a cluster barrier CTA c sums column
+//     slice c over the cluster's shared memories in rank order and runs the
+//     epilogue — no workspace, no counters, no global round trip;
+//   * otherwise partial sums of a tile that several CTAs share go to a workspace as
 //     fp32; the last CTA to arrive at a tile (atomic counter) sums the
 //     others' partials and its own registers in fixed segment order —
 //     deterministic, no float atomics — applies bias, activation and
@@ -55,6 +61,8 @@ struct DecodeParams {
   float alpha;          // Y = act(alpha * acc + bias) + R
   int gated;            // Y = act(acc_g + bias) * (acc_u + bias2)
   const void* bias2;    // gated: up-projection bias (N) or nullptr
+  int cluster;          // CTAs per tile sharing partials through distributed
+                        // shared memory (1: off; grid = n_tiles * cluster)
   // Optional timeline (dx_set_trace_buffer), kTraceSlots stamps per CTA:
   // [0] after set-up, [1] first and [2] last TMA issue, [3] last MMA issue;
   // for the CTA's last work item (warp quarter 0): [4] accumulator ready,
@@ -137,6 +145,47 @@ __device__ __forceinline__ bool decode_wait_written(const int* ctr, int target,
     }
   }
   return true;
+}
+
+// Cluster form, after every CTA of the cluster has left its partial in its
+// own shared memory at `part_s` ([warp quarter][half][row][32 lanes] fp32):
+// this CTA (rank c of C) finishes columns c * NT/C .. (c+1) * NT/C - 1 of
+// its tile, summing the C partials in rank order (deterministic), then bias,
+// activation, residual.  Run by the 4 epilogue warps (threads 64..191).
+template <int MN, typename T, int NH>
+__device__ __forceinline__ void decode_cluster_finish(const DecodeParams& p, uint32_t part_s) {
+  using S = DecodeShape<MN, NH>;
+  using Tr = ElemTraits<T>;
+  const int C = p.cluster;
+  const int t = static_cast<int>(blockIdx.x) / C;
+  const int ncols = S::NT / C;
+  const int c0 = static_cast<int>(cluster_ctarank()) * ncols;
+  const T* const bias = static_cast<const T*>(p.bias);
+  const T* const res = static_cast<const T*>(p.residual);
+  T* const Y = static_cast<T*>(p.Y);
+  const int total = ncols * p.M;
+  for (int idx = static_cast<int>(threadIdx.x) - 64; idx < total; idx += 128) {
+    const int m = idx / ncols;
+    const int col = c0 + (idx - m * ncols);
+    const int h = col >> 7, q = (col & 127) >> 5, ln = col & 31;
+    const uint32_t off = static_cast<uint32_t>((((q * NH + h) * MN + m) * 32 + ln) * 4);
+    float v[8];
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      v[r] = r < C ? ld_shared_cluster_f32(mapa_shared(part_s + off, static_cast<uint32_t>(r)))
+                   : 0.0f;
+    float sum = 0.0f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r)
+      if (r < C) sum += v[r];
+    const int n = t * S::NT + col;
+    if (n < p.N) {
+      float y = fmaf(p.alpha, sum, bias != nullptr ? Tr::to_float(bias[n]) : 0.0f);
+      y = act_apply<true>(y, p.act);
+      if (res != nullptr) y += Tr::to_float(res[m * p.ldr + n]);
+      Y[m * p.ldy + n] = Tr::from_float(y);
+    }
+  }
 }
 
 template <int MN, typename T, int NH = 2>
@@ -364,6 +413,19 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
       if (lane == 0) mbar_arrive(bar(S::BAR_TEMPTY + b));
       if (tr) decode_trace(p, 5);
 
+      if (!(kb0 == 0 && kb1 == p.kbt) && p.cluster > 1) {
+        // Cluster form: this CTA's one work item.  Its stage ring is idle
+        // (every MMA that read it has completed), so the partial goes there
+        // for the cluster's finish after the cluster barrier below.
+        fence_proxy_async_smem();
+        float* const part = reinterpret_cast<float*>(base_ptr + S::OFF_W);
+#pragma unroll
+        for (int h = 0; h < NH; ++h)
+#pragma unroll
+          for (int m = 0; m < MN; ++m)
+            if (m < M) part[((q * NH + h) * MN + m) * 32 + lane] = acc[h][m];
+        continue;
+      }
       if (!(kb0 == 0 && kb1 == p.kbt)) {
         // Tile shared with other CTAs.  One counter word per (tile, warp
         // quarter): arrivals in the low 16 bits, partials written in the high
@@ -617,6 +679,15 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
       }
     }
     if (q == 0 && lane == 0) decode_trace(p, 14);
+  }
+
+  if (p.cluster > 1) {
+    // Every thread of every CTA of the cluster passes both barriers exactly
+    // once, whatever path it took above: first every partial is in shared
+    // memory, then no CTA leaves while another may still read its partial.
+    cluster_sync();
+    if (warp >= 2) decode_cluster_finish<MN, T, NH>(p, sW);
+    cluster_sync();
   }
 
   tc_fence_before();

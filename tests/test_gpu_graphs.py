@@ -20,7 +20,7 @@ DEV = torch.device("cuda:0")
 def test_graph_replay_matches_eager():
     torch.manual_seed(0)
     # H = 5120: 20 tiles of 256 columns, so the first launch is the decode
-    # kernel with its K range split over the SMs (counters and partials).
+    # kernel with each tile's K range split over a cluster of 4 CTAs.
     M, K, H, N = 16, 1024, 5120, 768
     bf = torch.float16
     plans = []

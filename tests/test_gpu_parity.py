@@ -433,3 +433,26 @@ def test_loaded_kernels_are_sm100a():
     nat.check("dx_kernel_arch", nat.load().dx_kernel_arch(ctypes.byref(binv), ctypes.byref(ptxv)))
     assert binv.value == 100
     assert ptxv.value in (0, 100)
+
+
+@pytest.mark.parametrize("M,K,N,cluster", [(16, 8192, 3584, 8), (16, 4096, 7168, 4),
+                                           (16, 2048, 14336, 2), (5, 2048, 3072, 8),
+                                           (24, 2048, 3584, 8), (48, 1024, 3584, 8)])
+def test_decode_cluster_split(M, K, N, cluster):
+    """Fewer 256-column tiles than SMs / 2: each tile's K range is split over
+    a thread-block cluster whose CTAs add their partials through distributed
+    shared memory — no workspace, deterministic (rank order), every row
+    template (M = 5 / 16 / 24 / 48), residual included."""
+    lib = nat.load()
+    assert lib.dx_fused_linear_workspace_size(M, N, K, nat.DX_DTYPE_F16, nat.DX_KERNEL_DECODE) == 0
+    X, W, b, R = _rand(M, K, N, torch.float16, seed=M + K + N, residual=True)
+    Xd, Wd, bd, Rd = X.to(DEV), W.to(DEV), b.to(DEV), R.to(DEV)
+    Y0 = fused_linear(Xd, Wd, bd, "gelu_erf", residual=Rd, kernel="decode")
+    plan = nat.last_launch_plan()
+    assert f"cluster={cluster} " in plan and "workspace=0" in plan, plan
+    for _ in range(3):
+        assert torch.equal(fused_linear(Xd, Wd, bd, "gelu_erf", residual=Rd, kernel="decode"), Y0)
+    torch.cuda.synchronize()
+    _assert_close(Y0, oracle.fused_linear_f64(X, W, b, "gelu_erf", residual=R), torch.float16,
+                  f"cluster decode {M}x{K}x{N} [{plan}]")
+    _status_clean()

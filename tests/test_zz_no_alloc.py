@@ -10,7 +10,8 @@ workspace-taking entry point (``dx_fused_linear`` via
 ``fused_linear(kernel="decode")``, which runs the same deterministic plan)
 and within the fp16/bf16 tolerance of the fp64 oracle, on consecutive calls
 that reuse the shared scratch — split-K plans of every row template (16, 32
-and 64 padded rows) and a whole-tile plan that needs no scratch.
+and 64 padded rows), and plans that need no scratch (tiles split over a
+thread-block cluster, whole tiles).
 
 This file is collected last so that a failure here comes after every other
 test has run.
@@ -60,13 +61,14 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
     # split-K case must fit the 8 MiB array; the whole-tile case needs none.
     lib = nat.load()
     calls = [
-        # M, K, N, dtype, act, seed, residual, split-K
-        (16, 4096, 3072, torch.float16, "gelu_erf", 1, False, True),
+        # M, K, N, dtype, act, seed, residual, split-K through the scratch
+        (16, 4096, 1536, torch.float16, "gelu_erf", 1, False, True),
         (5, 2048, 1536, torch.bfloat16, "silu", 2, True, True),
-        (24, 2048, 3072, torch.float16, "relu", 4, False, True),    # 32-row template
+        (24, 2048, 1536, torch.float16, "relu", 4, False, True),    # 32-row template
         (48, 1024, 1536, torch.bfloat16, "gelu_erf", 5, True, True),  # 64-row template
+        (16, 4096, 3072, torch.float16, "silu", 7, False, False),   # cluster of 8 per tile
         (16, 1024, 28672, torch.float16, "silu", 6, False, False),  # whole tiles
-        (16, 4096, 3072, torch.float16, "gelu_erf", 1, False, True),
+        (16, 4096, 1536, torch.float16, "gelu_erf", 1, False, True),
     ]
     for M, K, N, dtype, act, seed, residual, split in calls:
         need = lib.dx_fused_linear_workspace_size(M, N, K, DTYPES[dtype], nat.DX_KERNEL_DECODE)
