@@ -87,10 +87,11 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
 
 
 def test_noalloc_rejects_problems_beyond_its_scratch():
-    # 64 tiles of 256 columns (fewer than half the SMs, so K is split): up to
-    # 4 segments x 64 padded rows x 256 columns of fp32 partial sums per tile,
-    # 16 MiB > the 8 MiB array.
-    M, K, N = 64, 8192, 16384
+    # 8 tiles of 256 columns (too few for a cluster to cover half the SMs, so
+    # K is split over the SMs through the scratch): up to 19 segments x 64
+    # padded rows x 256 columns of fp32 partial sums per tile, 9.6 MiB > the
+    # 8 MiB array.
+    M, K, N = 64, 8192, 2048
     lib = nat.load()
     assert lib.dx_fused_linear_workspace_size(M, N, K, nat.DX_DTYPE_F16,
                                               nat.DX_KERNEL_DECODE) > (8 << 20)
