@@ -1014,6 +1014,54 @@ def run_timeline(args) -> None:
         dist.destroy_process_group()
 
 
+def run_decode_shards(args) -> None:
+    """The decode configuration's column shards for 1/2/4/8-way splits, each
+    timed on one GPU (what every rank of a column-parallel run executes; the
+    shards need no collective): back-to-back launches over rotated weight
+    copies together >= 3x L2, one JSON line per split with GB/s, the fraction
+    of the HBM peak and the launch plan."""
+    import torch
+
+    from deepx_op_gpukernelcompiler_b200 import _native, fused_linear
+    from deepx_op_gpukernelcompiler_b200.shard import shard_bounds
+    from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peaks, peak_kind = _peaks()
+    hbm = peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    w = WORKLOADS["decode_gelu_erf_16x8192x28672_f16"]
+    g = torch.Generator(device=dev)
+    g.manual_seed(w.seed)
+    X = torch.randn(w.M, w.K, generator=g, device=dev).to(w.torch_dtype)
+    for ways in (1, 2, 4, 8):
+        n0, n1 = shard_bounds(w.N, ways, 0, 64)
+        n = n1 - n0
+        copies = max(2, math.ceil(3 * L2_BYTES / (w.K * n * 2)))
+        Ws = [(torch.randn(w.K, n, generator=g, device=dev) / math.sqrt(w.K)).to(w.torch_dtype)
+              for _ in range(copies)]
+        b = (torch.rand(n, generator=g, device=dev) * 0.2 - 0.1).to(w.torch_dtype)
+        Y = torch.empty(w.M, n, dtype=w.torch_dtype, device=dev)
+        it = [0]
+
+        def dec():
+            fused_linear(X, Ws[it[0] % copies], b, w.act, out=Y)
+            it[0] += 1
+
+        for _ in range(5):
+            dec()
+        torch.cuda.synchronize()
+        ms = _time_back_to_back(dec, max(40, args.steps), stream)
+        byts = 2 * (w.M * w.K + w.K * n + n + w.M * n)
+        print(json.dumps({"decode_shard": f"1/{ways}", "M": w.M, "K": w.K, "N": n,
+                          "us": round(ms * 1e3, 2), "GBps": round(byts / (ms * 1e-3) / 1e9, 1),
+                          "frac_of_hbm": round(byts / (ms * 1e-3) / 1e9 / hbm, 4),
+                          "peak": f"{hbm} GB/s, {peak_kind}",
+                          "plan": _native.last_launch_plan()}), flush=True)
+        del Ws, b, Y
+
+
 def run_fabric(args) -> None:
     """All-to-all NVLink throughput between the ranks of one box (the bound of
     the row-parallel reduction): every rank moves one slab of 16384 x 4096
@@ -1101,6 +1149,8 @@ def main() -> None:
     ap.add_argument("--chunks", type=int, default=4, help="--timeline: row chunks")
     ap.add_argument("--first", type=int, default=4, help="--timeline: first-GEMM launches")
     ap.add_argument("--nvls", type=int, default=1, help="--timeline: 0 forces peer loads")
+    ap.add_argument("--decode-shards", action="store_true",
+                    help="time the decode configuration's 1/2/4/8-way column shards on one GPU")
     ap.add_argument("--fabric", action="store_true",
                     help="all-to-all NVLink throughput between the ranks (torchrun, >= 2 GPUs)")
     ap.add_argument("--skinny", action="store_true",
@@ -1117,6 +1167,8 @@ def main() -> None:
         run_reference(args)
     elif args.fabric:
         run_fabric(args)
+    elif args.decode_shards:
+        run_decode_shards(args)
     elif args.timeline:
         run_timeline(args)
     elif args.skinny:
