@@ -778,7 +778,7 @@ def run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g) -> dict:
         for nvls in (True, False):
             mlp = ParallelMLP.from_shards(W1, b1, W2, b2, w.act, mode="fused", nvls=nvls)
             modules[nvls] = mlp
-            for chunks, first in ((4, 4), (4, 2), (8, 4), (2, 2), (1, 1)):
+            for chunks, first in ((4, 4), (4, 2), (4, 1), (8, 4), (2, 2), (2, 1), (1, 1)):
                 mlp.chunks, mlp.first_chunks = chunks, first
                 ms = time_run(lambda: mlp(X, hidden=H, out=Yo), 1500.0)
                 form = "multicast" if mlp.last_multicast else "peer"
