@@ -16,6 +16,7 @@
 #include <atomic>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -547,6 +548,45 @@ int umma_grid_workers(const UmmaPlan& pl) {
   return static_cast<int>(std::min<int64_t>(pl.workers, items));
 }
 
+// Programmatic dependent launch for the persistent GEMM and decode kernels
+// (they wait for the preceding grid before touching global memory, so their
+// set-up overlaps its tail).  DX_PDL=0 in the environment turns it off.
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("DX_PDL");
+    return v == nullptr || std::strcmp(v, "0") != 0;
+  }();
+  return on;
+}
+
+// Launch configuration with an optional cluster size (cluster <= 1: none)
+// and, when `pdl` and pdl_enabled(), the programmatic-serialization
+// attribute; `attr` holds >= 2 entries.
+cudaLaunchConfig_t launch_config(int grid, int threads, int smem, cudaStream_t s, int cluster,
+                                 cudaLaunchAttribute* attr, bool pdl = true) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(static_cast<unsigned>(threads));
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
+  cfg.stream = s;
+  unsigned n = 0;
+  if (cluster > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = static_cast<unsigned>(cluster);
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+  }
+  if (pdl && pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cfg;
+}
+
 template <int BN, typename T, bool G = false>
 int launch_umma(const Problem& pr, int dev, const UmmaPlan& pl) {
   using S = UmmaShape<BN>;
@@ -561,26 +601,17 @@ int launch_umma(const Problem& pr, int dev, const UmmaPlan& pl) {
            "smem=%d workspace=%zu",
            G ? "_gated" : "", G ? BN / 2 : BN, S::STAGES, grid, p.num_tiles, p.dp_tiles, p.splits,
            p.group_m, S::SMEM_BYTES, pl.bytes);
-  kern<<<grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tA, tB, tB2, tY, tR, p);
-  cudaError_t e = cudaGetLastError();
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = launch_config(grid, S::THREADS, S::SMEM_BYTES, pr.stream, 1, attr);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tB2, tY, tR, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch umma_fused_linear_kernel");
   return DX_OK;
 }
 
 cudaLaunchConfig_t pair_launch_config(int grid, int threads, int smem, cudaStream_t s,
                                       cudaLaunchAttribute* attr) {
-  cudaLaunchConfig_t cfg{};
-  cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(static_cast<unsigned>(threads));
-  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
-  cfg.stream = s;
-  attr[0].id = cudaLaunchAttributeClusterDimension;
-  attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = 1;
-  attr[0].val.clusterDim.z = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cfg;
+  return launch_config(grid, threads, smem, s, 2, attr);
 }
 
 std::map<int, int> g_pair_slots;
@@ -598,7 +629,7 @@ int pair_slots(int dev, int sms) {
   auto kern = dx::umma2_fused_linear_kernel<BN, T>;
   if (ensure_smem_attr(dev, reinterpret_cast<const void*>(kern), S::SMEM_BYTES, false) != DX_OK)
     return 0;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = pair_launch_config(2 * (sms / 2), S::THREADS, S::SMEM_BYTES, nullptr, attr);
   int n = 0;
   if (cudaOccupancyMaxActiveClusters(&n, reinterpret_cast<const void*>(kern), &cfg) != cudaSuccess)
@@ -623,13 +654,16 @@ int launch_umma2(const Problem& pr, int dev, const UmmaPlan& pl) {
            "splits=%d group_m=%d smem=%d workspace=%zu",
            G ? "_gated" : "", G ? BN / 2 : BN, S::STAGES, grid, pl.workers, p.num_tiles,
            p.dp_tiles, p.splits, p.group_m, S::SMEM_BYTES, pl.bytes);
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = pair_launch_config(grid, S::THREADS, S::SMEM_BYTES, pr.stream, attr);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tB2, tY, tR, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch umma2_fused_linear_kernel");
   return DX_OK;
 }
+
+// Largest weight stream (bytes) for which a decode launch starts early.
+constexpr int64_t kDecodePdlMaxBytes = int64_t{160} << 20;
 
 template <int MN, typename T, int NH = 2>
 int launch_decode(const Problem& pr, int dev, int sms, const DecodePlan& d) {
@@ -686,26 +720,17 @@ int launch_decode(const Problem& pr, int dev, int sms, const DecodePlan& d) {
            "cluster=%d workspace=%zu",
            pr.gated ? "_gated" : "", MN, NH, S::STAGES, d.grid, d.n_tiles, d.kbt, d.max_seg,
            d.cluster, d.bytes);
-  cudaError_t e;
-  if (d.cluster > 1) {
-    cudaLaunchAttribute attr[1];
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(static_cast<unsigned>(d.grid));
-    cfg.blockDim = dim3(S::THREADS);
-    cfg.dynamicSmemBytes = S::SMEM_BYTES;
-    cfg.stream = pr.stream;
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = static_cast<unsigned>(d.cluster);
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    e = cudaLaunchKernelEx(&cfg, kern, tW, tW2, tX, p);
-    if (e == cudaSuccess) e = cudaGetLastError();
-  } else {
-    kern<<<d.grid, S::THREADS, S::SMEM_BYTES, pr.stream>>>(tW, tW2, tX, p);
-    e = cudaGetLastError();
-  }
+  // An early start gains the set-up time (barriers, TMEM, descriptor
+  // prefetch), a few microseconds; a long weight stream loses more than that
+  // to the uneven SM placement of CTAs that start while the previous grid
+  // still holds SMs (measured: 16x8192x3584 f16 18.2 -> 15.8 us, but
+  // 16x8192x28672 1.7% slower), so only short launches take it.
+  const int64_t w_bytes = pr.K * pr.N * (pr.gated ? 2 : 1) * static_cast<int64_t>(sizeof(T));
+  cudaLaunchAttribute attr[2];
+  cudaLaunchConfig_t cfg = launch_config(d.grid, S::THREADS, S::SMEM_BYTES, pr.stream, d.cluster,
+                                         attr, w_bytes <= kDecodePdlMaxBytes);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tW, tW2, tX, p);
+  if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch decode_fused_linear_kernel");
   return DX_OK;
 }

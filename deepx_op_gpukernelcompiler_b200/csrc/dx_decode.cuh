@@ -242,6 +242,10 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_word;
+  // Global memory only after the preceding launch has completed (see
+  // grid_dependency_wait); the set-up above overlaps its tail.
+  grid_dependency_wait();
+  grid_launch_dependents();
   if (threadIdx.x == 0) {
     decode_trace(p, 0);
     if (p.trace != nullptr) {

@@ -238,6 +238,23 @@ __device__ __forceinline__ uint32_t mapa_shared(uint32_t saddr, uint32_t rank) {
   return r;
 }
 
+// ------------------------------------------- programmatic dependent launch
+// With the programmatic-serialization launch attribute, a kernel may start
+// while the preceding kernel in its stream is still running.  Everything a
+// kernel does before grid_dependency_wait() must touch only its own shared
+// memory, TMEM and parameters; the wait returns once the preceding grid has
+// completed and its memory is visible (immediately without the attribute).
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+
+// Lets the next launch in the stream (if launched with the attribute) begin
+// scheduling its CTAs; it starts once every CTA of this grid has called this
+// or exited, and its own grid_dependency_wait still waits for this grid.
+__device__ __forceinline__ void grid_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // 32-bit load from another CTA's shared memory (a shared::cluster address).
 __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t cluster_addr) {
   float v;

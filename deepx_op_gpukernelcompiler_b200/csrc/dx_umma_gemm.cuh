@@ -628,6 +628,11 @@ __global__ void __launch_bounds__(UmmaShape<BN>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_word;
+  // Set-up above touched only this CTA's shared memory, TMEM and parameters;
+  // global memory may hold the preceding launch's output (inputs, Y, split-K
+  // tickets, a carried job's flags), so wait for it before any access.
+  grid_dependency_wait();
+  grid_launch_dependents();
   if (threadIdx.x == 0) trace_mark(p, 0);
 
   if (warp == 0) {
@@ -896,6 +901,11 @@ __global__ void __launch_bounds__(Umma2Shape<BN>::THREADS, 1)
   cluster_sync();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_word;
+  // Set-up above touched only this CTA's shared memory, TMEM and parameters;
+  // global memory may hold the preceding launch's output (inputs, Y, split-K
+  // tickets, a carried job's flags), so wait for it before any access.
+  grid_dependency_wait();
+  grid_launch_dependents();
   if (threadIdx.x == 0) trace_mark(p, 0);
 
   if (warp == 0) {

@@ -456,3 +456,41 @@ def test_decode_cluster_split(M, K, N, cluster):
     _assert_close(Y0, oracle.fused_linear_f64(X, W, b, "gelu_erf", residual=R), torch.float16,
                   f"cluster decode {M}x{K}x{N} [{plan}]")
     _status_clean()
+
+
+@pytest.mark.parametrize("kern,M,K", [("decode", 16, 2048), ("decode", 5, 4096), ("umma", 256, 1024),
+                                      ("umma_1cta", 256, 1024), ("auto", 16, 2048)])
+def test_dependent_launches_back_to_back(kern, M, K):
+    """Each launch reads the previous launch's output and overwrites the buffer
+    the launch before it read (two buffers, ping-pong), with no host sync in
+    between: the GEMM and decode kernels start early (programmatic dependent
+    launch) but touch global memory only once the previous grid is complete,
+    so the chain must equal, bit for bit, the same chain run with a sync after
+    every step; each synced step is checked against the fp64 oracle fed that
+    step's device input."""
+    g = torch.Generator().manual_seed(M * 7 + K)
+    Ws = [(torch.randn(K, K, generator=g) / K ** 0.5).half() for _ in range(2)]
+    bs = [(torch.rand(K, generator=g) * 0.2 - 0.1).half() for _ in range(2)]
+    X = torch.randn(M, K, generator=g).half()
+    Wd, bd = [w.to(DEV) for w in Ws], [b.to(DEV) for b in bs]
+    steps = 8
+
+    def chain(sync: bool):
+        bufs = [X.to(DEV), torch.empty(M, K, dtype=torch.float16, device=DEV)]
+        seen = [X]
+        for i in range(steps):
+            src, dst = bufs[i % 2], bufs[(i + 1) % 2]
+            fused_linear(src, Wd[i % 2], bd[i % 2], "gelu_erf", residual=src, out=dst, kernel=kern)
+            if sync:
+                torch.cuda.synchronize()
+                seen.append(dst.cpu())
+        torch.cuda.synchronize()
+        return bufs[steps % 2].clone(), seen
+
+    fast, _ = chain(False)
+    slow, seen = chain(True)
+    assert torch.equal(fast, slow), f"{kern}: back-to-back chain differs from the synced chain"
+    for i in range(steps):
+        want = oracle.fused_linear_f64(seen[i], Ws[i % 2], bs[i % 2], "gelu_erf", residual=seen[i])
+        _assert_close(seen[i + 1], want, torch.float16, f"{kern} chain step {i}")
+    _status_clean()
