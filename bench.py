@@ -18,10 +18,13 @@ flushed (256 MiB write) before every timed launch, outside the events.
 `e2e` is the same metric through the public host-buffer API
 (`fused_linear_host`) with the step's inputs copied from pinned host memory
 and Y copied back inside the timed region (copies overlapped with the
-compute block by block).  `--impl reference` times the CPU reference arm: the oracle's
-fp32 restatement of the reference expression act(a @ b + bias)
-(kernel.py:64-66) with numpy/BLAS on the host cores, on a bounded row
-sample of the same workload.
+compute block by block).  `--impl reference` times the CPU reference arm: the
+reference expression act(a @ b + bias) (kernel.py:64-66, ACTIVATION_PT of
+fusion.py:87-92) in fp32 torch on all the host cores, on a bounded row sample
+of the same workload.  At N=1 the line's `extra.reference_gpu_engines` also
+times the reference's own GPU engines (its Triton and TileLang kernels, from
+the reference package installed under baseline/_ref) beside this engine on
+the same inputs.
 """
 from __future__ import annotations
 
@@ -513,6 +516,8 @@ def run_gpu(args) -> None:
     extra = {"sustained": sustained, "pytorch_gpu": pytorch_gpu}
     if not args.no_extra:
         extra.update(run_extras(args, world, rank, dev, peaks, flush, parity))
+        if world == 1 and not args.no_ref_engines:
+            extra["reference_gpu_engines"] = run_reference_engines(args, dev, peaks, flush)
     # Parity of every rank's outputs: the line says ok only if all ranks agree.
     ok_all = all(v["ok"] for v in parity.values())
     if world > 1:
@@ -713,6 +718,102 @@ def run_extras(args, world, rank, dev, peaks, flush, parity) -> dict:
     del X, Wg, Wu, bg, bu, Y
 
     out.update(run_mlp_extras(args, world, rank, dev, peaks, flush, parity, g))
+    return out
+
+
+REF_PKG = ROOT / "baseline" / "_ref" / "deepx_op_gpukernelcompiler"
+
+
+def _reference_module(name: str):
+    """One module of the reference package installed under baseline/_ref,
+    imported by file path and unmodified (the package's __init__ imports the
+    kvspace client, which its engine modules do not need)."""
+    import importlib.util
+    path = REF_PKG / f"{name}.py"
+    if not path.exists():
+        raise FileNotFoundError(f"{path} (install the reference into baseline/_ref)")
+    spec = importlib.util.spec_from_file_location(f"_deepx_reference_{name}", path)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def run_reference_engines(args, dev, peaks, flush) -> dict:
+    """The reference's own GPU engines on this B200, beside this engine, on the
+    same fp16 inputs: its Triton kernel (kernel_triton.py:24-89, autotuned
+    over its own config list on first call) and its TileLang kernel
+    (kernel_tilelang.py:23-55, with the harness's default block
+    BM=BN=128, BK=32, kernel.py:10).  Both compute the GELU of the
+    `"gelu"` key with erf, so this engine runs "gelu_erf" there.  Same
+    timing as the other GEMM lines: one event pair per launch, L2 flushed
+    before each.  Speed only (the reference engines store fp16); each line
+    carries the max |diff| of its output from this engine's.  An engine that
+    fails to build or run is recorded with its error, not retried."""
+    import torch
+    from deepx_op_gpukernelcompiler_b200 import fused_linear
+
+    stream = torch.cuda.current_stream(dev)
+    steps = max(5, min(args.steps, 10))
+    tflops_peak = peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"])
+    mods, out = {}, {"source": "unmodified reference package, baseline/_ref",
+                     "timing": "one event pair per launch, L2 flushed before each"}
+    for name in ("kernel_triton", "kernel_tilelang"):
+        try:
+            mods[name] = _reference_module(name)
+        except Exception as e:  # noqa: BLE001 - recorded in the line
+            out[name] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+    g = torch.Generator(device=dev)
+    g.manual_seed(4242)
+    for M, K, N, act in ((4096, 4096, 4096, "gelu"), (8192, 4096, 14336, "silu")):
+        flops = 2.0 * M * N * K
+        X = torch.randn(M, K, generator=g, device=dev).half()
+        W = (torch.randn(K, N, generator=g, device=dev) / math.sqrt(K)).half()
+        b = (torch.rand(N, generator=g, device=dev) * 0.2 - 0.1).half()
+        Y = torch.empty(M, N, dtype=torch.float16, device=dev)
+        ours_act = "gelu_erf" if act == "gelu" else act
+        fns = {"b200": lambda: fused_linear(X, W, b, ours_act, out=Y)}
+        if "kernel_triton" in mods:
+            fns["triton"] = (lambda f: (lambda: f(X, W, b)))(
+                mods["kernel_triton"].make_linear_kernel(act))
+        row = {}
+        t0 = time.time()
+        if "kernel_tilelang" in mods:
+            try:
+                tl = mods["kernel_tilelang"].make_linear_kernel(act)(
+                    M, N, K, 128, 128, 32, "float16", "float32")
+                fns["tilelang"] = (lambda f: (lambda: f(X, W, b)))(tl)
+            except Exception as e:  # noqa: BLE001
+                row["tilelang"] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+        ref_y = None
+        for eng, fn in fns.items():
+            try:
+                t1 = time.time()
+                r = fn()
+                torch.cuda.synchronize()
+                first_s = time.time() - t1
+                got = Y if eng == "b200" else r
+                if eng == "b200":
+                    ref_y = Y.float()
+                diff = None if ref_y is None else float((got.float() - ref_y).abs().max())
+                for _ in range(3):
+                    fn()
+                torch.cuda.synchronize()
+                t = _time_launches(fn, steps, flush, stream)
+                ms = sum(t) / len(t)
+                tf = flops / (ms * 1e-3) / 1e12
+                row[eng] = {"ms": round(ms, 4), "tflops": round(tf, 2),
+                            "frac_of_peak": round(tf / tflops_peak, 4),
+                            "max_abs_diff_vs_b200": None if eng == "b200" else round(diff, 4),
+                            "first_call_s": round(first_s, 2)}
+            except Exception as e:  # noqa: BLE001
+                row[eng] = {"error": f"{type(e).__name__}: {str(e)[:200]}"}
+        if "tflops" in row.get("b200", {}):
+            for eng in ("triton", "tilelang"):
+                if "tflops" in row.get(eng, {}):
+                    row[eng]["b200_speedup"] = round(row["b200"]["tflops"] / row[eng]["tflops"], 2)
+        row["setup_s"] = round(time.time() - t0, 1)
+        out[f"linear_{act}_{M}x{K}x{N}_f16"] = row
+        del X, W, b, Y, fns
     return out
 
 
@@ -1140,6 +1241,8 @@ def main() -> None:
     ap.add_argument("--workload", default=DEFAULT_WORKLOAD)
     ap.add_argument("--no-extra", action="store_true", help="skip the decode/square/MLP lines")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline")
+    ap.add_argument("--no-ref-engines", action="store_true",
+                    help="skip timing the reference's Triton/TileLang engines (N=1)")
     ap.add_argument("--profile", action="store_true",
                     help="run only W warm-up and K timed launches of the workload (for ncu)")
     ap.add_argument("--shard-of", type=int, default=1,
