@@ -601,8 +601,10 @@ int launch_umma(const Problem& pr, int dev, const UmmaPlan& pl) {
            "smem=%d workspace=%zu",
            G ? "_gated" : "", G ? BN / 2 : BN, S::STAGES, grid, p.num_tiles, p.dp_tiles, p.splits,
            p.group_m, S::SMEM_BYTES, pl.bytes);
+  // Tracing writes timestamps before the grid dependency wait: no early start.
   cudaLaunchAttribute attr[2];
-  cudaLaunchConfig_t cfg = launch_config(grid, S::THREADS, S::SMEM_BYTES, pr.stream, 1, attr);
+  cudaLaunchConfig_t cfg =
+      launch_config(grid, S::THREADS, S::SMEM_BYTES, pr.stream, 1, attr, p.trace == nullptr);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tB2, tY, tR, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch umma_fused_linear_kernel");
@@ -655,7 +657,8 @@ int launch_umma2(const Problem& pr, int dev, const UmmaPlan& pl) {
            G ? "_gated" : "", G ? BN / 2 : BN, S::STAGES, grid, pl.workers, p.num_tiles,
            p.dp_tiles, p.splits, p.group_m, S::SMEM_BYTES, pl.bytes);
   cudaLaunchAttribute attr[2];
-  cudaLaunchConfig_t cfg = pair_launch_config(grid, S::THREADS, S::SMEM_BYTES, pr.stream, attr);
+  cudaLaunchConfig_t cfg =
+      launch_config(grid, S::THREADS, S::SMEM_BYTES, pr.stream, 2, attr, p.trace == nullptr);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tA, tB, tB2, tY, tR, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch umma2_fused_linear_kernel");
@@ -724,11 +727,12 @@ int launch_decode(const Problem& pr, int dev, int sms, const DecodePlan& d) {
   // prefetch), a few microseconds; a long weight stream loses more than that
   // to the uneven SM placement of CTAs that start while the previous grid
   // still holds SMs (measured: 16x8192x3584 f16 18.2 -> 15.8 us, but
-  // 16x8192x28672 1.7% slower), so only short launches take it.
+  // 16x8192x28672 1.7% slower), so only short launches take it.  Tracing
+  // writes timestamps before the wait: no early start.
   const int64_t w_bytes = pr.K * pr.N * (pr.gated ? 2 : 1) * static_cast<int64_t>(sizeof(T));
   cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = launch_config(d.grid, S::THREADS, S::SMEM_BYTES, pr.stream, d.cluster,
-                                         attr, w_bytes <= kDecodePdlMaxBytes);
+                                         attr, p.trace == nullptr && w_bytes <= kDecodePdlMaxBytes);
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, tW, tW2, tX, p);
   if (e == cudaSuccess) e = cudaGetLastError();
   if (e != cudaSuccess) return cuda_fail(e, "launch decode_fused_linear_kernel");

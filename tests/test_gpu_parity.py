@@ -494,3 +494,39 @@ def test_dependent_launches_back_to_back(kern, M, K):
         want = oracle.fused_linear_f64(seen[i], Ws[i % 2], bs[i % 2], "gelu_erf", residual=seen[i])
         _assert_close(seen[i + 1], want, torch.float16, f"{kern} chain step {i}")
     _status_clean()
+
+
+@pytest.mark.parametrize("M,K,N", [(16, 4096, 3584), (16, 2048, 28672)])
+def test_weights_written_by_the_previous_launch(M, K, N):
+    """A tensor-core launch writes the W that the next (decode) launch reads,
+    and the launch after it overwrites that W again, with no host sync: the
+    decode kernel must read W only after the producer has completed (its
+    early start covers set-up only), and the producer must not overwrite it
+    before the decode has read it; bit for bit equal to the synced run."""
+    g = torch.Generator().manual_seed(K + N)
+    K2 = 512
+    A = (torch.randn(K, K2, generator=g) / K2 ** 0.5).half().to(DEV)
+    Bs = [(torch.randn(K2, N, generator=g)).half().to(DEV) for _ in range(3)]
+    X = torch.randn(M, K, generator=g).half().to(DEV)
+    b = (torch.rand(N, generator=g) * 0.2 - 0.1).half().to(DEV)
+
+    def run(sync: bool):
+        Wbuf = torch.empty(K, N, dtype=torch.float16, device=DEV)
+        outs = []
+        for i in range(6):
+            fused_linear(A, Bs[i % 3], None, None, out=Wbuf, kernel="umma")  # W of the next step
+            if sync:
+                torch.cuda.synchronize()
+            outs.append(fused_linear(X, Wbuf, b, "gelu_erf", kernel="decode"))
+            if sync:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        return outs, Wbuf.cpu()
+
+    fast, _ = run(False)
+    slow, W_last = run(True)
+    for i, (a, c) in enumerate(zip(fast, slow)):
+        assert torch.equal(a, c), f"step {i}: decode read a W its producer had not finished"
+    ref = oracle.fused_linear_f64(X.cpu(), W_last, b.cpu(), "gelu_erf")
+    _assert_close(slow[5], ref, torch.float16, "decode on a produced W")
+    _status_clean()
