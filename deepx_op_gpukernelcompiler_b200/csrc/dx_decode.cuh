@@ -69,7 +69,9 @@ struct DecodeParams {
   // [5] accumulator read, [6] arrival counted, [7] own partial published or
   // the others' found written, [8] fix-up sums done, [9] item finished;
   // [10 + i] work item i finished (i < 2), [12] kernel entry, [13] the SM's
-  // id, [14] epilogue warps done, [15] exit.
+  // id, [14] epilogue warps done, [15] exit; cluster form: [6] first cluster
+  // barrier passed, [7] slices sent, [8] last cluster barrier passed, [9]
+  // columns finished.
   unsigned long long* trace;
 };
 
@@ -95,7 +97,12 @@ struct DecodeShape {
   static constexpr int THREADS = 192;
   static constexpr int OFF_W = 0;
   static constexpr int OFF_X = OFF_W + STAGES * W_BYTES;
-  static constexpr int OFF_BAR = OFF_X + STAGES * X_BYTES;
+  // Cluster form, 16-row template: a receive area of its own (MN x NT fp32),
+  // so a CTA can send its partial's slices as soon as its accumulator is
+  // read, whatever its cluster peers' stage rings are still doing.
+  static constexpr bool OWN_RECV = MN == 16 && NH == 2;
+  static constexpr int OFF_RECV = OFF_X + STAGES * X_BYTES;
+  static constexpr int OFF_BAR = OFF_RECV + (OWN_RECV ? MN * NT * 4 : 0);
   static constexpr int BAR_FULL = 0;
   static constexpr int BAR_EMPTY = STAGES;
   static constexpr int BAR_TFULL = 2 * STAGES;
@@ -110,6 +117,11 @@ struct DecodeShape {
   // is idle, and each epilogue warp takes a quarter of it for the other
   // segments' blocks (FIX_CAP blocks per batch of bulk copies).
   static constexpr int FIX_CAP = STAGES * W_BYTES / (4 * QBLK * 4);
+  // Cluster form without a receive area of its own: the partial (MN x NT
+  // fp32) at the start of the idle ring, the slices received from the
+  // cluster (at most MN x NT fp32) after it.
+  static constexpr int RECV_OFF = MN * NT * 4;
+  static_assert(2 * MN * NT * 4 <= STAGES * W_BYTES, "cluster partial and receive area");
   static constexpr int OFF_MISC = OFF_BAR + NUM_BARS * 8;  // tmem base, abort flag
   static constexpr int SMEM_BYTES = 1024 + OFF_MISC + 16;
   static_assert(MN == 16 || MN == 32 || MN == 64, "decode batch tile");
@@ -147,42 +159,112 @@ __device__ __forceinline__ bool decode_wait_written(const int* ctr, int target,
   return true;
 }
 
-// Cluster form, after every CTA of the cluster has left its partial in its
-// own shared memory at `part_s` ([warp quarter][half][row][32 lanes] fp32):
-// this CTA (rank c of C) finishes columns c * NT/C .. (c+1) * NT/C - 1 of
-// its tile, summing the C partials in rank order (deterministic), then bias,
-// activation, residual.  Run by the 4 epilogue warps (threads 64..191).
+// Cluster form (plain decode: NH = 2, NT = 256 columns per tile, C = 2, 4
+// or 8 CTAs per cluster): rank c of the cluster finishes columns
+// c * NT/C .. (c+1) * NT/C - 1 of the tile; log2 of that slice width.
+__device__ __forceinline__ int decode_cluster_slice_log2(int C) { return 8 - (31 - __clz(C)); }
+
+// Cluster form: the bias of the column this epilogue thread finishes (each
+// thread keeps one column: NT/C divides the 128 epilogue threads).
 template <int MN, typename T, int NH>
-__device__ __forceinline__ void decode_cluster_finish(const DecodeParams& p, uint32_t part_s) {
+__device__ __forceinline__ float decode_cluster_bias(const DecodeParams& p) {
   using S = DecodeShape<MN, NH>;
   using Tr = ElemTraits<T>;
-  const int C = p.cluster;
-  const int t = static_cast<int>(blockIdx.x) / C;
-  const int ncols = S::NT / C;
-  const int c0 = static_cast<int>(cluster_ctarank()) * ncols;
+  const int lg = decode_cluster_slice_log2(p.cluster);
+  const int col = (static_cast<int>(cluster_ctarank()) << lg) +
+                  ((static_cast<int>(threadIdx.x) - 64) & ((1 << lg) - 1));
+  const int n = static_cast<int>(blockIdx.x) / p.cluster * S::NT + col;
   const T* const bias = static_cast<const T*>(p.bias);
+  return (bias != nullptr && n < p.N) ? Tr::to_float(bias[n]) : 0.0f;
+}
+
+// Cluster form, sending: each epilogue thread (64..191) takes column
+// quarter*32 + lane of both halves and sends its rows to the CTA that
+// finishes that column, into that CTA's receive area [source rank][row]
+// [column of the slice] (a warp's 32 columns are one 128-byte run there).
+// Remote stores need no round trip; the next cluster barrier makes them
+// visible.  The 16-row template sends from registers as soon as its
+// accumulator is read (decode_cluster_send); the others leave the partial
+// in their idle stage ring at `part_s` ([warp quarter][half][row][32 lanes]
+// fp32) and send it after a cluster barrier that says every ring is idle
+// (decode_cluster_push), into the ring behind the partial.
+// Send rows 0..M-1 of column h * 128 + ql (v[m]) to the CTA finishing it,
+// into its receive area at `recv_s` (the same offset in every CTA).
+template <int MN>
+__device__ __forceinline__ void decode_cluster_send(const DecodeParams& p, uint32_t recv_s,
+                                                    int h, int ql, const float (&v)[MN]) {
+  const int lg = decode_cluster_slice_log2(p.cluster);
+  const int ncols = 1 << lg;
+  const int col = h * 128 + ql;
+  const uint32_t dst = mapa_shared(
+      recv_s + static_cast<uint32_t>(
+                   (static_cast<int>(cluster_ctarank()) * p.M * ncols + (col & (ncols - 1))) * 4),
+      static_cast<uint32_t>(col >> lg));
+#pragma unroll
+  for (int m = 0; m < MN; ++m)
+    if (m < p.M) st_shared_cluster_f32(dst + static_cast<uint32_t>(m * ncols * 4), v[m]);
+}
+
+template <int MN, int NH>
+__device__ __forceinline__ void decode_cluster_push(const DecodeParams& p, uint32_t part_s,
+                                                    uint32_t recv_s) {
+  const int ql = static_cast<int>(threadIdx.x) - 64;  // quarter * 32 + lane
+  const float* const part = reinterpret_cast<const float*>(__cvta_shared_to_generic(part_s));
+#pragma unroll
+  for (int h = 0; h < NH; ++h) {
+    const float* const src = part + (((ql >> 5) * NH + h) * MN) * 32 + (ql & 31);
+    float v[MN];
+#pragma unroll
+    for (int m = 0; m < MN; ++m) v[m] = m < p.M ? src[m * 32] : 0.0f;
+    decode_cluster_send<MN>(p, recv_s, h, ql, v);
+  }
+}
+
+// Cluster form, step 2 (after the next cluster barrier): this CTA's column
+// slice, summed over the C source ranks in rank order from its own receive
+// area (deterministic), then bias, activation and residual.  Thread ql takes
+// column ql % (NT/C) and every (128 / (NT/C))-th row from ql / (NT/C).
+template <int MN, typename T, int NH>
+__device__ __forceinline__ void decode_cluster_finish(const DecodeParams& p, uint32_t recv_s,
+                                                      float bias) {
+  using S = DecodeShape<MN, NH>;
+  using Tr = ElemTraits<T>;
+  constexpr int kRows = 4;  // rows whose loads are issued together
+  const int C = p.cluster;
+  const int lg = decode_cluster_slice_log2(C);
+  const int ncols = 1 << lg;
+  const int tpc = 128 >> lg;  // threads per column
+  const int M = p.M;
+  const int ql = static_cast<int>(threadIdx.x) - 64;
+  const int c = ql & (ncols - 1);
+  const int n = static_cast<int>(blockIdx.x) / C * S::NT +
+                (static_cast<int>(cluster_ctarank()) << lg) + c;
+  if (n >= p.N) return;
+  const float* const recv = reinterpret_cast<const float*>(__cvta_shared_to_generic(recv_s));
   const T* const res = static_cast<const T*>(p.residual);
   T* const Y = static_cast<T*>(p.Y);
-  const int total = ncols * p.M;
-  for (int idx = static_cast<int>(threadIdx.x) - 64; idx < total; idx += 128) {
-    const int m = idx / ncols;
-    const int col = c0 + (idx - m * ncols);
-    const int h = col >> 7, q = (col & 127) >> 5, ln = col & 31;
-    const uint32_t off = static_cast<uint32_t>((((q * NH + h) * MN + m) * 32 + ln) * 4);
-    float v[8];
+  for (int m0 = ql >> lg; m0 < M; m0 += kRows * tpc) {
+    float sum[kRows], rv[kRows];
 #pragma unroll
-    for (int r = 0; r < 8; ++r)
-      v[r] = r < C ? ld_shared_cluster_f32(mapa_shared(part_s + off, static_cast<uint32_t>(r)))
-                   : 0.0f;
-    float sum = 0.0f;
+    for (int i = 0; i < kRows; ++i) {
+      const int m = m0 + i * tpc;
+      float s = 0.0f;
+      rv[i] = 0.0f;
+      if (m < M) {
 #pragma unroll
-    for (int r = 0; r < 8; ++r)
-      if (r < C) sum += v[r];
-    const int n = t * S::NT + col;
-    if (n < p.N) {
-      float y = fmaf(p.alpha, sum, bias != nullptr ? Tr::to_float(bias[n]) : 0.0f);
+        for (int r = 0; r < 8; ++r)
+          if (r < C) s += recv[(r * M + m) * ncols + c];
+        if (res != nullptr) rv[i] = Tr::to_float(res[m * p.ldr + n]);
+      }
+      sum[i] = s;
+    }
+#pragma unroll
+    for (int i = 0; i < kRows; ++i) {
+      const int m = m0 + i * tpc;
+      if (m >= M) break;
+      float y = fmaf(p.alpha, sum[i], bias);
       y = act_apply<true>(y, p.act);
-      if (res != nullptr) y += Tr::to_float(res[m * p.ldr + n]);
+      if (res != nullptr) y += rv[i];
       Y[m * p.ldy + n] = Tr::from_float(y);
     }
   }
@@ -242,6 +324,11 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_word;
+  // Cluster form: the first phase of the cluster barrier, waited for before
+  // any CTA writes into another's shared memory (every CTA has started).
+  if (p.cluster > 1) cluster_arrive_relaxed();
+  bool cluster_waited = false;  // this thread has waited for that phase
+  float cluster_bias = 0.0f;    // the bias of the column it finishes
   // Global memory only after the preceding launch has completed (see
   // grid_dependency_wait); the set-up above overlaps its tail.
   grid_dependency_wait();
@@ -353,6 +440,11 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
     __syncwarp();
   } else {
     // --------------------------------------------------------- epilogue
+    // Cluster form: the bias this thread needs for its finishing column,
+    // loaded now -- at the end, behind the cluster's last weight loads in the
+    // HBM queues, a single load takes microseconds.
+    if constexpr (NH == 2)
+      if (p.cluster > 1) cluster_bias = decode_cluster_bias<MN, T, NH>(p);
     const int q = warp & 3;
     const int n_local = q * 32 + lane;
     const T* const bias = static_cast<const T*>(p.bias);
@@ -418,16 +510,26 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
       if (tr) decode_trace(p, 5);
 
       if (!(kb0 == 0 && kb1 == p.kbt) && p.cluster > 1) {
-        // Cluster form: this CTA's one work item.  Its stage ring is idle
-        // (every MMA that read it has completed), so the partial goes there
-        // for the cluster's finish after the cluster barrier below.
-        fence_proxy_async_smem();
-        float* const part = reinterpret_cast<float*>(base_ptr + S::OFF_W);
+        // Cluster form: this CTA's one work item.
+        if constexpr (S::OWN_RECV) {
+          // Straight from registers to the finishing CTAs' receive areas,
+          // once every CTA of the cluster has started.
+          cluster_wait();
+          cluster_waited = true;
 #pragma unroll
-        for (int h = 0; h < NH; ++h)
+          for (int h = 0; h < NH; ++h) decode_cluster_send<MN>(p, base + S::OFF_RECV, h, n_local, acc[h]);
+          if (tr) decode_trace(p, 7);
+        } else {
+          // The stage ring is idle (every MMA that read it has completed):
+          // the partial goes there, sent after the cluster barrier below.
+          fence_proxy_async_smem();
+          float* const part = reinterpret_cast<float*>(base_ptr + S::OFF_W);
 #pragma unroll
-          for (int m = 0; m < MN; ++m)
-            if (m < M) part[((q * NH + h) * MN + m) * 32 + lane] = acc[h][m];
+          for (int h = 0; h < NH; ++h)
+#pragma unroll
+            for (int m = 0; m < MN; ++m)
+              if (m < M) part[((q * NH + h) * MN + m) * 32 + lane] = acc[h][m];
+        }
         continue;
       }
       if (!(kb0 == 0 && kb1 == p.kbt)) {
@@ -686,12 +788,29 @@ __global__ void __launch_bounds__(DecodeShape<MN, NH>::THREADS, 1)
   }
 
   if (p.cluster > 1) {
-    // Every thread of every CTA of the cluster passes both barriers exactly
-    // once, whatever path it took above: first every partial is in shared
-    // memory, then no CTA leaves while another may still read its partial.
-    cluster_sync();
-    if (warp >= 2) decode_cluster_finish<MN, T, NH>(p, sW);
-    cluster_sync();
+    // Every thread of every CTA of the cluster takes every phase of the
+    // cluster barrier exactly once, whatever path it took above: the set-up
+    // phase (arrived at set-up; waited for before the first send, or here),
+    // for the templates without a receive area of their own a phase after
+    // which every partial is in its CTA's idle ring, and a last phase after
+    // which every slice is in its finishing CTA's receive area (no CTA
+    // touches another's shared memory after it).
+    if constexpr (NH == 2) {  // the cluster form is never gated
+      if (!cluster_waited) cluster_wait();  // the set-up phase
+      uint32_t recv_s = base + S::OFF_RECV;
+      if constexpr (!S::OWN_RECV) {
+        cluster_sync();  // every partial in its CTA's idle ring
+        if (threadIdx.x == 64) decode_trace(p, 6);
+        recv_s = sW + S::RECV_OFF;
+        if (warp >= 2) decode_cluster_push<MN, NH>(p, sW, recv_s);
+        if (threadIdx.x == 64) decode_trace(p, 7);
+      }
+      cluster_sync();  // every slice in its finishing CTA's receive area
+      if (threadIdx.x == 64) decode_trace(p, 8);
+      // No CTA touches another's shared memory after this barrier.
+      if (warp >= 2) decode_cluster_finish<MN, T, NH>(p, recv_s, cluster_bias);
+      if (threadIdx.x == 64) decode_trace(p, 9);
+    }
   }
 
   tc_fence_before();

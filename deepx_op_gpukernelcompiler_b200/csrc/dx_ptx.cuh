@@ -262,6 +262,24 @@ __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t cluster_addr) {
   return v;
 }
 
+// 32-bit store into another CTA's shared memory (a shared::cluster address);
+// visible to it after a cluster barrier (release / acquire).  No memory
+// clobber, so independent loads can be scheduled around a run of these
+// stores; the cluster barrier's asm (volatile, memory clobber) orders them.
+__device__ __forceinline__ void st_shared_cluster_f32(uint32_t cluster_addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(cluster_addr), "f"(v));
+}
+
+// Split form of the cluster barrier (all threads of all CTAs of the
+// cluster, each arrive followed by one wait): arrive without ordering, and
+// the matching wait (acquire).
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
 // All threads of all CTAs of the cluster.
 __device__ __forceinline__ void cluster_sync() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::
