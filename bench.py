@@ -1163,6 +1163,76 @@ def run_decode_shards(args) -> None:
         del Ws, b, Y
 
 
+DECODE_TRACE_SLOTS = {12: "entry", 0: "setup", 1: "first_load", 2: "last_load",
+                      3: "last_mma", 4: "acc_ready", 5: "acc_read", 7: "slices_sent",
+                      8: "last_cluster_barrier", 9: "finished", 15: "exit"}
+
+
+def run_decode_timeline(args) -> None:
+    """Per-CTA timeline of one decode launch on the 1/`--ways` column shard of
+    the decode configuration (dx_set_trace_buffer: global-timer stamps per CTA
+    at fixed points of the kernel), after back-to-back launches over rotated
+    weights; one JSON line with, per point, the min / median / max over CTAs
+    in us from the first CTA's entry.  A traced launch has no early start, so
+    the shard is also timed untraced."""
+    import numpy as np
+    import torch
+
+    from deepx_op_gpukernelcompiler_b200 import _native, fused_linear
+    from deepx_op_gpukernelcompiler_b200.shard import shard_bounds
+    from deepx_op_gpukernelcompiler_b200.workloads import WORKLOADS
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    lib = _native.load()
+    w = WORKLOADS["decode_gelu_erf_16x8192x28672_f16"]
+    n0, n1 = shard_bounds(w.N, args.ways, 0, 64)
+    n = n1 - n0
+    g = torch.Generator(device=dev)
+    g.manual_seed(w.seed)
+    X = torch.randn(w.M, w.K, generator=g, device=dev).to(w.torch_dtype)
+    copies = max(2, math.ceil(3 * L2_BYTES / (w.K * n * 2)))
+    Ws = [(torch.randn(w.K, n, generator=g, device=dev) / math.sqrt(w.K)).to(w.torch_dtype)
+          for _ in range(copies)]
+    b = (torch.rand(n, generator=g, device=dev) * 0.2 - 0.1).to(w.torch_dtype)
+    Y = torch.empty(w.M, n, dtype=w.torch_dtype, device=dev)
+    slots = 16
+    tr = torch.zeros(4096 * slots, dtype=torch.int64, device=dev)
+    it = [0]
+
+    def dec():
+        fused_linear(X, Ws[it[0] % copies], b, w.act, out=Y)
+        it[0] += 1
+
+    line = {"decode_shard": f"1/{args.ways}", "M": w.M, "K": w.K, "N": n, "act": w.act}
+    for traced in (False, True):
+        if traced:
+            _native.check("dx_set_trace_buffer", lib.dx_set_trace_buffer(tr.data_ptr(),
+                                                                         tr.numel() * 8))
+        for _ in range(5):
+            dec()
+        torch.cuda.synchronize()
+        ms = _time_back_to_back(dec, max(40, args.steps), stream)
+        line["us_traced" if traced else "us"] = round(ms * 1e3, 2)
+        if traced:
+            plan = _native.last_launch_plan()
+            grid = int(plan.split("grid=")[1].split()[0])
+            t = tr.view(-1, slots)[:grid].cpu().numpy().astype(np.int64)
+            base = t[:, 12].min()
+            points = {}
+            for slot, name in DECODE_TRACE_SLOTS.items():
+                col = t[:, slot]
+                col = col[col > 0]
+                if col.size:
+                    rel = (col - base) / 1e3
+                    points[name] = [round(float(np.percentile(rel, q)), 2) for q in (0, 50, 100)]
+            line["plan"] = plan
+            line["timeline_us_min_median_max"] = points
+            _native.check("dx_set_trace_buffer", lib.dx_set_trace_buffer(None, 0))
+    print(json.dumps(line), flush=True)
+
+
 def run_fabric(args) -> None:
     """All-to-all NVLink throughput between the ranks of one box (the bound of
     the row-parallel reduction): every rank moves one slab of 16384 x 4096
@@ -1254,6 +1324,9 @@ def main() -> None:
     ap.add_argument("--nvls", type=int, default=1, help="--timeline: 0 forces peer loads")
     ap.add_argument("--decode-shards", action="store_true",
                     help="time the decode configuration's 1/2/4/8-way column shards on one GPU")
+    ap.add_argument("--decode-timeline", action="store_true",
+                    help="per-CTA timeline of a decode launch on the 1/--ways column shard")
+    ap.add_argument("--ways", type=int, default=8, help="column shard for --decode-timeline")
     ap.add_argument("--fabric", action="store_true",
                     help="all-to-all NVLink throughput between the ranks (torchrun, >= 2 GPUs)")
     ap.add_argument("--skinny", action="store_true",
@@ -1272,6 +1345,8 @@ def main() -> None:
         run_fabric(args)
     elif args.decode_shards:
         run_decode_shards(args)
+    elif args.decode_timeline:
+        run_decode_timeline(args)
     elif args.timeline:
         run_timeline(args)
     elif args.skinny:
