@@ -25,6 +25,11 @@
  *     docs' runtime contract (doc/kvlang-to-tilelang-interface.md:86-89).  The
  *     library never allocates, frees or synchronises on the caller's behalf;
  *     every launch goes to `stream` (a cudaStream_t; NULL = legacy default).
+ *   - Stream order holds as for any kernel.  The tensor-core and (for weight
+ *     streams up to 160 MiB) decode kernels are launched with programmatic
+ *     dependent launch: their set-up may overlap the tail of the preceding
+ *     kernel on the stream, but they read and write no global memory before
+ *     it has completed.  DX_PDL=0 in the environment turns this off.
  *   - Return value: DX_OK (0) or a negative DX_ERR_* code.  The message of the
  *     last failure on the calling thread is available from
  *     dx_last_error_string().
